@@ -1,0 +1,185 @@
+// comm.cu -- NCCL communicator and the device-buffer output all-gather for the
+// column-sharded W8A8 GEMM.
+//
+// Replaces nccl/NCCLCommunicator.scala (init :44-56, allGatherNative :151-163,
+// NCCLOps.ncclAllGather :302-320), which passes host arrays to NCCL and calls
+// ncclGetUniqueId on every rank.  Here one rank makes the unique id, the caller
+// carries it to the others, and the gather runs on device buffers on the
+// caller's stream.  NCCL is opened with dlopen("libnccl.so.2") on first use, so
+// the library loads on machines without NCCL and shares the process's NCCL when
+// one is already loaded.  Initialisation is non-blocking with a host-side
+// deadline: a rank that never joins produces QGEMM_ERR_TIMEOUT, not a hang.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <thread>
+
+#include "internal.h"
+
+struct qgemm_comm_s {
+  ncclComm_t comm = nullptr;
+  qgemm_device_s* dev = nullptr;
+  int rank = 0, world = 1;
+};
+
+namespace qg {
+namespace {
+
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+#define QG_SYM(field, name) api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name))
+    QG_SYM(GetUniqueId, "ncclGetUniqueId");
+    QG_SYM(CommInitRankConfig, "ncclCommInitRankConfig");
+    QG_SYM(CommInitRank, "ncclCommInitRank");
+    QG_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+    QG_SYM(CommAbort, "ncclCommAbort");
+    QG_SYM(CommDestroy, "ncclCommDestroy");
+    QG_SYM(AllGather, "ncclAllGather");
+    QG_SYM(GetErrorString, "ncclGetErrorString");
+#undef QG_SYM
+    api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather;
+  });
+  return api;
+}
+
+qgemm_status nccl_fail(ncclResult_t r, const char* what) {
+  NcclApi& n = nccl();
+  return fail(QGEMM_ERR_NCCL, "%s: %s (%d)", what,
+              n.GetErrorString ? n.GetErrorString(r) : "nccl error", (int)r);
+}
+
+// Seconds a rank waits for its peers in qgemm_comm_init (QGEMM_COMM_TIMEOUT_S).
+double init_timeout_s() {
+  const char* e = getenv("QGEMM_COMM_TIMEOUT_S");
+  if (e) {
+    double v = atof(e);
+    if (v > 0) return v;
+  }
+  return 120.0;
+}
+
+}  // namespace
+}  // namespace qg
+
+using namespace qg;
+
+extern "C" {
+
+qgemm_status qgemm_comm_unique_id(void* out) {
+  if (!out) return fail(QGEMM_ERR_INVALID_ARG, "out is null");
+  NcclApi& n = nccl();
+  if (!n.ok) return fail(QGEMM_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  ncclResult_t r = n.GetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  memcpy(out, &id, sizeof(id));
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_comm_init(qgemm_device_t dev, const void* uid, int rank, int world,
+                             qgemm_comm_t* out) {
+  if (!out || !uid) return fail(QGEMM_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (!dev || !dev->open) return fail(QGEMM_ERR_BAD_HANDLE, "null or closed device");
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad rank %d / world %d", rank, world);
+  NcclApi& n = nccl();
+  if (!n.ok) return fail(QGEMM_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  cudaError_t ce = cudaSetDevice(dev->ordinal);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaSetDevice");
+  ncclUniqueId id;
+  memcpy(&id, uid, sizeof(id));
+  ncclComm_t comm = nullptr;
+  if (n.CommInitRankConfig && n.CommGetAsyncError && n.CommAbort) {
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = n.CommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclCommInitRankConfig");
+    const auto deadline = std::chrono::steady_clock::now() +
+                          std::chrono::duration<double>(init_timeout_s());
+    ncclResult_t st = ncclInProgress;
+    while (true) {
+      r = n.CommGetAsyncError(comm, &st);
+      if (r != ncclSuccess) { n.CommAbort(comm); return nccl_fail(r, "ncclCommGetAsyncError"); }
+      if (st != ncclInProgress) break;
+      if (std::chrono::steady_clock::now() > deadline) {
+        n.CommAbort(comm);
+        return fail(QGEMM_ERR_TIMEOUT, "ncclCommInitRank: peers did not join within %.0f s",
+                    init_timeout_s());
+      }
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    if (st != ncclSuccess) { n.CommAbort(comm); return nccl_fail(st, "ncclCommInitRank (async)"); }
+  } else {
+    ncclResult_t r = n.CommInitRank(&comm, world, id, rank);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
+  }
+  qgemm_comm_s* c = new (std::nothrow) qgemm_comm_s();
+  if (!c) { n.CommDestroy(comm); return fail(QGEMM_ERR_OOM, "host allocation failed"); }
+  c->comm = comm;
+  c->dev = dev;
+  c->rank = rank;
+  c->world = world;
+  *out = c;
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_comm_destroy(qgemm_comm_t c) {
+  if (!c) return fail(QGEMM_ERR_BAD_HANDLE, "null communicator");
+  NcclApi& n = nccl();
+  ncclResult_t r = ncclSuccess;
+  if (c->comm && n.CommDestroy) r = n.CommDestroy(c->comm);
+  delete c;
+  if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_comm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, uint64_t send,
+                                       uint64_t recv, size_t count) {
+  if (!c || !c->comm) return fail(QGEMM_ERR_BAD_HANDLE, "null communicator");
+  qgemm_status st = enter(s);
+  if (st != QGEMM_OK) return st;
+  if (s->dev != c->dev) return fail(QGEMM_ERR_INVALID_ARG, "stream and communicator devices differ");
+  if (count == 0) return QGEMM_OK;
+  if (!send || !recv) return fail(QGEMM_ERR_INVALID_ARG, "null buffer");
+  NcclApi& n = nccl();
+  ncclResult_t r = n.AllGather(reinterpret_cast<const void*>(send), reinterpret_cast<void*>(recv),
+                               count, ncclBfloat16, c->comm, s->stream);
+  if (r == ncclInProgress && n.CommGetAsyncError) {
+    // Non-blocking communicator: wait (bounded) until the call is enqueued.
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(60);
+    ncclResult_t as = ncclInProgress;
+    while (as == ncclInProgress) {
+      if (n.CommGetAsyncError(c->comm, &as) != ncclSuccess) break;
+      if (std::chrono::steady_clock::now() > deadline)
+        return fail(QGEMM_ERR_TIMEOUT, "ncclAllGather was not enqueued within 60 s");
+    }
+    r = as;
+  }
+  if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+  return QGEMM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+// internal.h -- handle structs, status helpers and launcher declarations shared
+// by the libqgemm translation units.  Not part of the public ABI (include/qgemm.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+#include <mutex>
+
+#include "qgemm.h"
+
+struct qgemm_device_s {
+  int ordinal = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t l2_bytes = 0;
+  size_t smem_optin = 0;
+  bool tcgen05 = false;       // sm_100 family: tcgen05 / TMEM / TMA kernels run
+  int* d_err = nullptr;       // device error word written by bounded waits
+  std::mutex mu;
+  bool open = false;
+};
+
+struct qgemm_stream_s {
+  qgemm_device_s* dev = nullptr;
+  cudaStream_t stream = nullptr;
+  bool owned = false;
+};
+
+namespace qg {
+
+// Records a thread-local message and returns the status.
+qgemm_status fail(qgemm_status s, const char* fmt, ...);
+// Maps a CUDA error (after a launch or API call) to a status + message.
+qgemm_status cuda_fail(cudaError_t e, const char* what);
+// Checks the stream handle and makes its device current.
+qgemm_status enter(qgemm_stream_t s);
+
+inline bool aligned(uint64_t p, uint64_t a) { return (p % a) == 0; }
+
+// Error codes a kernel writes into qgemm_device_s::d_err.
+enum : int {
+  DEVERR_NONE = 0,
+  DEVERR_TIMEOUT_PRODUCER = 1,
+  DEVERR_TIMEOUT_MMA = 2,
+  DEVERR_TIMEOUT_EPILOGUE = 3,
+  DEVERR_TIMEOUT_DRAIN = 4,
+};
+
+// ---- launchers (each returns a status and never throws) ----
+qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
+                                 const float* sA, const float* sB, void* out, int out_dtype,
+                                 int ldc, int M, int N, int K, int32_t* acc);
+bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int b_kn,
+                            uint64_t out, int out_dtype, int ldc, int M, int N, int K,
+                            const char** why);
+qgemm_status launch_w8a8_simt(qgemm_stream_s* s, const int8_t* A, const int8_t* B, int b_kn,
+                              const float* sA, const float* sB, void* out, int out_dtype,
+                              int ldc, int M, int N, int K, int32_t* acc);
+qgemm_status launch_w4a16_ref(qgemm_stream_s* s, const uint8_t* w, const float* sw,
+                              const float* x, float* y, int M, int N, int K);
+qgemm_status launch_w8a16_ref(qgemm_stream_s* s, const int8_t* w, const float* sw,
+                              const float* x, const float* bias, float* y, int M, int N,
+                              int K, int hasBias, int rowwise);
+qgemm_status launch_quantize(qgemm_stream_s* s, const float* w, float* scales, int8_t* q,
+                             int8_t* zeros, int K, int N, int qBits);
+qgemm_status launch_dequantize(qgemm_stream_s* s, const int8_t* q, const float* scales,
+                               float* w, int K, int N);
+qgemm_status launch_prepack_w8_nk(qgemm_stream_s* s, const int8_t* src, int8_t* dst, int K,
+                                  int N);
+qgemm_status launch_unshard_bf16(qgemm_stream_s* s, const uint16_t* g, uint16_t* out,
+                                 int world, int M, int ncols);
+qgemm_status launch_w4a16_grouped(qgemm_stream_s* s, const void* x, const uint32_t* wq,
+                                  const void* scales, int zp, int group, void* y, int M,
+                                  int N, int K);
+
+}  // namespace qg

@@ -1,0 +1,94 @@
+"""QuantizedGemmOps -- the reference operator object, backed by libqgemm.
+
+Mirrors ``object QuantizedGemmOps`` of
+src/main/scala/cuda/dsl/operators/linalg/QuantizedGemmOps.scala:17-247: the same
+method names, the same parameter order and meaning (``Ptr[T]`` arguments are
+device addresses -- ints, objects with ``.address`` such as qgemm.Buffer, or
+torch CUDA tensors -- followed by the Int sizes).  Each call is one
+asynchronous launch on the object's stream.
+
+Error behaviour: the reference swallows native errors and prints them
+(runtime/CUDARuntime.scala:216,256,294); here every failure raises
+``QGemmError`` carrying the library status and message.
+"""
+from __future__ import annotations
+
+import ctypes
+
+from . import _lib as L
+
+
+class QuantizedGemmOps:
+    def __init__(self, stream):
+        self.stream = stream
+        self._h = stream.handle
+
+    # -- QuantizedGemmOps.scala:24-55
+    def w8a16Gemm(self, wInt8, scalesW, x, bias, y, M: int, N: int, K: int, hasBias: bool):
+        L.call("qgemm_w8a16_gemm", self._h, L.addr(wInt8), L.addr(scalesW), L.addr(x),
+               L.addr(bias), L.addr(y), M, N, K, 1 if hasBias else 0)
+
+    # -- QuantizedGemmOps.scala:61-84
+    def w8a16GemmRowWise(self, wInt8, scalesW, x, y, M: int, N: int, K: int):
+        L.call("qgemm_w8a16_gemm_rowwise", self._h, L.addr(wInt8), L.addr(scalesW), L.addr(x),
+               L.addr(y), M, N, K)
+
+    # -- QuantizedGemmOps.scala:90-115
+    def w8a32Gemm(self, wInt8, scalesW, x, scalesX, y, M: int, N: int, K: int):
+        L.call("qgemm_w8a32_gemm", self._h, L.addr(wInt8), L.addr(scalesW), L.addr(x),
+               L.addr(scalesX), L.addr(y), M, N, K)
+
+    # -- QuantizedGemmOps.scala:121-157
+    def dynamicQuantize(self, weight, scales, qWeight, K: int, N: int, qBits: int = 8):
+        L.call("qgemm_dynamic_quantize", self._h, L.addr(weight), L.addr(scales),
+               L.addr(qWeight), K, N, qBits)
+
+    # -- QuantizedGemmOps.scala:163-192
+    def weightOnlyQuantizePerChannel(self, weight, scales, qWeight, zeros, K: int, N: int):
+        L.call("qgemm_weight_only_quantize_per_channel", self._h, L.addr(weight),
+               L.addr(scales), L.addr(qWeight), L.addr(zeros), K, N)
+
+    # -- QuantizedGemmOps.scala:198-212
+    def dequantize(self, qWeight, scales, weight, K: int, N: int):
+        L.call("qgemm_dequantize", self._h, L.addr(qWeight), L.addr(scales), L.addr(weight), K, N)
+
+    # -- QuantizedGemmOps.scala:218-247
+    def w4a16Gemm(self, wInt4, scalesW, x, y, M: int, N: int, K: int):
+        L.call("qgemm_w4a16_gemm", self._h, L.addr(wInt4), L.addr(scalesW), L.addr(x),
+               L.addr(y), M, N, K)
+
+    # -- B200 entry points behind the same object ------------------------------
+
+    def w8a8Gemm(self, A, B, sA, sB, out, M: int, N: int, K: int, *, b_layout: int = L.B_KN,
+                 out_dtype: int = L.BF16, ldc: int | None = None, acc_i32=None,
+                 algo: int = L.ALGO_AUTO):
+        """W8A8 with per-token sA [M] x per-channel sB [N] dequant (the w8a32Gemm
+        arithmetic), bf16 (RNE) or fp32 output, optional int32 accumulators."""
+        L.call("qgemm_w8a8_gemm", self._h, L.addr(A), L.addr(B), b_layout, L.addr(sA),
+               L.addr(sB), L.addr(out), out_dtype, N if ldc is None else ldc, M, N, K,
+               L.addr(acc_i32), algo)
+
+    def w4a16GemmGrouped(self, x, wq, scales, y, M: int, N: int, K: int, *,
+                         zero_point: int = 8, group_size: int = 128):
+        """Group-wise W4A16: x bf16 [M,K], wq uint32 [K,N/8] (reference nibble order),
+        scales bf16 [K/group_size, N], y bf16 [M,N]."""
+        L.call("qgemm_w4a16_grouped_gemm", self._h, L.addr(x), L.addr(wq), L.addr(scales),
+               zero_point, group_size, L.addr(y), M, N, K)
+
+    def prepackW8NK(self, src_kn, dst_nk, K: int, N: int):
+        L.call("qgemm_prepack_w8_nk", self._h, L.addr(src_kn), L.addr(dst_nk), K, N)
+
+    # -- by-name launch (dsl/TritonKernelRunner.scala:68-73) --------------------
+
+    def launchKernel(self, name: str, buffers, ints):
+        bufs = (ctypes.c_uint64 * max(1, len(buffers)))(*[L.addr(b) for b in buffers])
+        iv = (ctypes.c_int * max(1, len(ints)))(*[int(i) for i in ints])
+        L.call("qgemm_launch_by_name", self._h, name.encode(), bufs, len(buffers), iv, len(ints))
+
+
+def shard_columns(N: int, world: int, rank: int, align: int = 256) -> tuple[int, int]:
+    """Column range [n0, n1) of rank ``rank`` for an N-column weight split into
+    ``world`` contiguous slices whose boundaries are multiples of ``align``."""
+    a, b = ctypes.c_int(), ctypes.c_int()
+    L.call("qgemm_shard_columns", N, world, rank, align, ctypes.byref(a), ctypes.byref(b))
+    return a.value, b.value

@@ -1,0 +1,217 @@
+/*
+ * qgemm.h -- C ABI of libqgemm, the B200 (sm_100a) quantized-matmul library.
+ *
+ * This is the drop-in boundary for the quantized-matmul operators of
+ * bytedeco/cuda-triton-scala.  The reference exposes them as Scala methods
+ * taking device pointers (core/Ptr.scala:9-52, `address: Long`) and Ints
+ * (src/main/scala/cuda/dsl/operators/linalg/QuantizedGemmOps.scala:17-247),
+ * by kernel name (dsl/TritonKernelRunner.scala:68-73) and through a Java
+ * bridge of raw Long addresses (driver/CUDARuntimeJavaBridge.scala:121-165).
+ * Each entry point below names the reference interface it replaces.
+ *
+ * Conventions
+ *  - Device buffers are passed as uint64_t device addresses (a Ptr.address);
+ *    the caller owns every buffer.  Nothing here allocates per call.
+ *  - Every compute call is asynchronous on the given stream and returns a
+ *    status; errors never abort, exit or trap.  qgemm_last_error() gives a
+ *    thread-local message for the last failing call on this thread.
+ *  - Kernels that wait on barriers bound every wait; a wait that runs out sets
+ *    a per-device error word that qgemm_stream_sync() reports as
+ *    QGEMM_ERR_TIMEOUT.
+ *  - Handles are thread-safe per distinct stream; a device handle may be
+ *    shared across threads.
+ */
+#ifndef QGEMM_H
+#define QGEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Every entry point is exported from libqgemm.so; everything else is hidden. */
+#if defined(__GNUC__)
+#define QGEMM_API __attribute__((visibility("default")))
+#else
+#define QGEMM_API
+#endif
+
+typedef int32_t qgemm_status;
+
+enum {
+  QGEMM_OK = 0,
+  QGEMM_ERR_INVALID_ARG = -1,  /* bad size, null pointer, bad enum           */
+  QGEMM_ERR_BAD_ALIGN = -2,    /* pointer or leading dimension misaligned    */
+  QGEMM_ERR_CUDA = -3,         /* a CUDA runtime/driver call failed          */
+  QGEMM_ERR_NCCL = -4,         /* an NCCL call failed or NCCL is unavailable */
+  QGEMM_ERR_TIMEOUT = -5,      /* a bounded device-side wait ran out         */
+  QGEMM_ERR_UNSUPPORTED = -6,  /* no kernel for this device / shape          */
+  QGEMM_ERR_NO_DEVICE = -7,    /* no CUDA device, or ordinal out of range    */
+  QGEMM_ERR_OOM = -8,          /* device allocation failed                   */
+  QGEMM_ERR_BAD_HANDLE = -9    /* null or closed handle                      */
+};
+
+/* Output element types. */
+enum { QGEMM_F32 = 0, QGEMM_BF16 = 1 };
+
+/* Layouts of the int8 weight operand B of the W8A8 GEMM.
+ * QGEMM_B_KN: [K, N] row-major, the reference layout (`wInt8(k*N+col)`,
+ *             QuantizedGemmOps.scala:106).  Used as-is (MN-major operand).
+ * QGEMM_B_NK: [N, K] row-major (K-major), e.g. from qgemm_prepack_w8_nk. */
+enum { QGEMM_B_KN = 0, QGEMM_B_NK = 1 };
+
+/* Kernel selection for the W8A8 GEMM. */
+enum {
+  QGEMM_ALGO_AUTO = 0,     /* tcgen05 when the shape allows it, else SIMT       */
+  QGEMM_ALGO_TCGEN05 = 1,  /* tensor-core path only (UNSUPPORTED if it can't)   */
+  QGEMM_ALGO_SIMT = 2      /* CUDA-core path (any shape), the independent check  */
+};
+
+typedef struct qgemm_device_s* qgemm_device_t;
+typedef struct qgemm_stream_s* qgemm_stream_t;
+typedef struct qgemm_comm_s* qgemm_comm_t;
+
+/* ---- errors ----------------------------------------------------------------
+ * Replaces the reference's swallowed exceptions (runtime/CUDARuntime.scala:216,
+ * 256, 294) with statuses and a message. */
+QGEMM_API const char* qgemm_last_error(void);
+QGEMM_API const char* qgemm_status_string(qgemm_status s);
+QGEMM_API int qgemm_version(void); /* major*10000 + minor*100 + patch */
+
+/* ---- devices ---------------------------------------------------------------
+ * Replaces runtime/DeviceRuntime.scala:13-45 (`init`) and CUDARuntime.init
+ * (runtime/CUDARuntime.scala:120-183), which hard-codes device 0. */
+QGEMM_API qgemm_status qgemm_device_count(int* count);
+QGEMM_API qgemm_status qgemm_device_open(int ordinal, qgemm_device_t* out);
+QGEMM_API qgemm_status qgemm_device_close(qgemm_device_t dev);
+/* sm_count, compute capability, L2 bytes, and whether tcgen05 kernels run. */
+QGEMM_API qgemm_status qgemm_device_info(qgemm_device_t dev, int* sm_count, int* cc_major,
+                               int* cc_minor, size_t* l2_bytes, int* has_tcgen05);
+
+/* ---- streams ---------------------------------------------------------------
+ * Replaces driver/TritonDriverAPINative.scala:78-122 (NativeCUDAStream). */
+QGEMM_API qgemm_status qgemm_stream_create(qgemm_device_t dev, qgemm_stream_t* out);
+/* Adopt a caller-owned cudaStream_t (not destroyed by qgemm_stream_destroy). */
+QGEMM_API qgemm_status qgemm_stream_wrap(qgemm_device_t dev, void* cuda_stream, qgemm_stream_t* out);
+QGEMM_API qgemm_status qgemm_stream_destroy(qgemm_stream_t s);
+/* Synchronise, then report (and clear) a device-side timeout on this device. */
+QGEMM_API qgemm_status qgemm_stream_sync(qgemm_stream_t s);
+
+/* ---- buffers ---------------------------------------------------------------
+ * Replace DeviceRuntime.malloc/free/memcpyHtoD/memcpyDtoH
+ * (runtime/DeviceRuntime.scala:13-45; runtime/CUDARuntime.scala:204-311). */
+QGEMM_API qgemm_status qgemm_buffer_alloc(qgemm_device_t dev, size_t bytes, uint64_t* dev_addr);
+QGEMM_API qgemm_status qgemm_buffer_free(qgemm_device_t dev, uint64_t dev_addr);
+QGEMM_API qgemm_status qgemm_memcpy_h2d(qgemm_stream_t s, uint64_t dst, const void* src, size_t bytes);
+QGEMM_API qgemm_status qgemm_memcpy_d2h(qgemm_stream_t s, void* dst, uint64_t src, size_t bytes);
+QGEMM_API qgemm_status qgemm_memset(qgemm_stream_t s, uint64_t dst, int value, size_t bytes);
+/* Page-locked host memory for fast copies (cudaMallocHost). */
+QGEMM_API qgemm_status qgemm_host_alloc(size_t bytes, void** out);
+QGEMM_API qgemm_status qgemm_host_free(void* p);
+
+/* ---- reference operators (same names, argument order and meaning) -------- */
+
+/* QuantizedGemmOps.w8a32Gemm (QuantizedGemmOps.scala:90-115):
+ *   y[m,n] = float(sum_k x[m,k]*wInt8[k,n]) * scalesW[n] * scalesX[m]
+ * wInt8 int8 [K,N], scalesW f32 [N], x int8 [M,K], scalesX f32 [M], y f32 [M,N].
+ * Bit-exact with the reference arithmetic. */
+QGEMM_API qgemm_status qgemm_w8a32_gemm(qgemm_stream_t s, uint64_t wInt8, uint64_t scalesW,
+                              uint64_t x, uint64_t scalesX, uint64_t y,
+                              int M, int N, int K);
+
+/* QuantizedGemmOps.w4a16Gemm (QuantizedGemmOps.scala:218-247): wInt4 holds
+ * K*N nibbles (element k*N+n in byte (k*N+n)/2, low nibble first), zero point
+ * 8, per-column f32 scalesW [N], x f32 [M,K], y f32 [M,N].  Bit-exact (same
+ * per-element fp32 summation order). */
+QGEMM_API qgemm_status qgemm_w4a16_gemm(qgemm_stream_t s, uint64_t wInt4, uint64_t scalesW,
+                              uint64_t x, uint64_t y, int M, int N, int K);
+
+/* QuantizedGemmOps.w8a16Gemm (QuantizedGemmOps.scala:24-55). Bit-exact. */
+QGEMM_API qgemm_status qgemm_w8a16_gemm(qgemm_stream_t s, uint64_t wInt8, uint64_t scalesW,
+                              uint64_t x, uint64_t bias, uint64_t y,
+                              int M, int N, int K, int hasBias);
+
+/* QuantizedGemmOps.w8a16GemmRowWise (QuantizedGemmOps.scala:61-84). Bit-exact. */
+QGEMM_API qgemm_status qgemm_w8a16_gemm_rowwise(qgemm_stream_t s, uint64_t wInt8, uint64_t scalesW,
+                                      uint64_t x, uint64_t y, int M, int N, int K);
+
+/* QuantizedGemmOps.dynamicQuantize (QuantizedGemmOps.scala:121-157). */
+QGEMM_API qgemm_status qgemm_dynamic_quantize(qgemm_stream_t s, uint64_t weight, uint64_t scales,
+                                    uint64_t qWeight, int K, int N, int qBits);
+
+/* QuantizedGemmOps.weightOnlyQuantizePerChannel (QuantizedGemmOps.scala:163-192). */
+QGEMM_API qgemm_status qgemm_weight_only_quantize_per_channel(qgemm_stream_t s, uint64_t weight,
+                                                    uint64_t scales, uint64_t qWeight,
+                                                    uint64_t zeros, int K, int N);
+
+/* QuantizedGemmOps.dequantize (QuantizedGemmOps.scala:198-212). */
+QGEMM_API qgemm_status qgemm_dequantize(qgemm_stream_t s, uint64_t qWeight, uint64_t scales,
+                              uint64_t weight, int K, int N);
+
+/* ---- B200 entry points behind the same facade ----------------------------- */
+
+/* W8A8 GEMM with per-token x per-channel dequant: the w8a32Gemm arithmetic
+ * (QuantizedGemmOps.scala:102-113) with a choice of B layout and output type.
+ *   A    int8 [M,K] row-major (activations, the reference `x`)
+ *   B    int8, b_layout QGEMM_B_KN ([K,N], the reference `wInt8`) or QGEMM_B_NK
+ *   sA   f32 [M] (per token, `scalesX`);  sB f32 [N] (per channel, `scalesW`)
+ *   out  [M, ldc] of out_dtype (QGEMM_F32 or QGEMM_BF16, RNE); ldc >= N
+ *   acc_i32  optional int32 [M, N] (ld N) raw accumulators, 0 for none
+ * Also the target of TensorCoreOps.tensorCoreGemmInt8
+ * (operators/intrinsic/TensorCoreOps.scala:294-340) and CutlassGemm.int8GemmKernel
+ * (cutlass/CutlassGemm.scala:987-1041) names; their broken arithmetic (the -128
+ * offset, strided k, shared accumulator) is deliberately not reproduced. */
+QGEMM_API qgemm_status qgemm_w8a8_gemm(qgemm_stream_t s, uint64_t A, uint64_t B, int b_layout,
+                             uint64_t sA, uint64_t sB, uint64_t out, int out_dtype,
+                             int ldc, int M, int N, int K, uint64_t acc_i32, int algo);
+
+/* Group-wise W4A16 GEMV/GEMM for decode (the w4a16Gemm arithmetic,
+ * QuantizedGemmOps.scala:229-245, with a zero point and per-group scales):
+ *   x   bf16 [M,K];  wq uint32 [K, N/8]: nibble j of word (k, c) is q[k][8c+j]
+ *       (the reference nibble order read as little-endian words)
+ *   scales bf16 [K/group_size, N];  y bf16 [M,N] (RNE)
+ *   y[m,n] = sum_k (q[k,n] - zero_point) * scales[k/G, n] * x[m,k]
+ * Requires N % 8 == 0 and K % group_size == 0; 16-byte aligned wq, x, y. */
+QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm(qgemm_stream_t s, uint64_t x, uint64_t wq,
+                                      uint64_t scales, int zero_point, int group_size,
+                                      uint64_t y, int M, int N, int K);
+
+/* One-time weight repack: int8 [K,N] (reference layout) -> [N,K] (K-major). */
+QGEMM_API qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src_kn, uint64_t dst_nk,
+                                 int K, int N);
+
+/* Launch by reference kernel name, the by-name path of
+ * TritonKernelRunner.launchKernel (dsl/TritonKernelRunner.scala:68-73) and
+ * CUDARuntimeJavaBridge.launchKernel (driver/CUDARuntimeJavaBridge.scala:121-165).
+ * bufs are device addresses in the reference method's parameter order, ints
+ * the Int parameters in order (Bool as 0/1).  Names: "w8a32Gemm", "w4a16Gemm",
+ * "w8a16Gemm", "w8a16GemmRowWise", "dynamicQuantize",
+ * "weightOnlyQuantizePerChannel", "dequantize".  Unknown name -> INVALID_ARG. */
+QGEMM_API qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name,
+                                  const uint64_t* bufs, int nbufs,
+                                  const int* ints, int nints);
+
+/* ---- column sharding and the output all-gather ----------------------------
+ * The reference has only a host-array NCCL wrapper (nccl/NCCLCommunicator.scala:
+ * 35-92, 151-163, 302-320) with no unique-id exchange.  Here rank r holds the
+ * weight columns [n0, n1) of qgemm_shard_columns and the output all-gather is
+ * a device-buffer ncclAllGather on the caller's stream. */
+QGEMM_API qgemm_status qgemm_shard_columns(int N, int world, int rank, int align, int* n0, int* n1);
+/* 128-byte ncclUniqueId, made on one rank and sent to the others by the caller. */
+QGEMM_API qgemm_status qgemm_comm_unique_id(void* out_128_bytes);
+QGEMM_API qgemm_status qgemm_comm_init(qgemm_device_t dev, const void* unique_id_128, int rank,
+                             int world, qgemm_comm_t* out);
+QGEMM_API qgemm_status qgemm_comm_destroy(qgemm_comm_t comm);
+/* recv[r*count .. (r+1)*count) <- send of rank r; count in bf16 elements. */
+QGEMM_API qgemm_status qgemm_comm_allgather_bf16(qgemm_comm_t comm, qgemm_stream_t s, uint64_t send,
+                                       uint64_t recv, size_t count);
+/* [world][M][ncols] bf16 gather buffer -> [M][world*ncols] row-major. */
+QGEMM_API qgemm_status qgemm_unshard_columns_bf16(qgemm_stream_t s, uint64_t gathered, uint64_t out,
+                                        int world, int M, int ncols);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QGEMM_H */

@@ -1,0 +1,95 @@
+"""The C-ABI library loads here (no GPU) and exports exactly what
+include/qgemm.h declares; host-only entry points behave; no compute calls."""
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+
+def header_functions():
+    import qgemm._lib as L
+    src = open(L.HEADER_PATH).read()
+    return sorted(set(re.findall(r"QGEMM_API\s+[\w\s\*]+?\b(qgemm_\w+)\s*\(", src)))
+
+
+def test_library_loads():
+    import qgemm
+    assert qgemm.lib() is not None
+    assert qgemm.lib().qgemm_version() >= 10000
+
+
+def test_exports_every_header_symbol():
+    import qgemm._lib as L
+    declared = header_functions()
+    assert len(declared) >= 30
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(qgemm_\w+)", out))
+    missing = [f for f in declared if f not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    extra = sorted(exported - set(declared))
+    assert not extra, f"exported but not declared: {extra}"
+    # and the Python binding knows every one of them
+    assert set(L.SIGNATURES) == set(declared)
+
+
+def test_status_strings():
+    import qgemm
+    import qgemm._lib as L
+    assert qgemm.status_name(L.OK) == "QGEMM_OK"
+    assert qgemm.status_name(L.ERR_TIMEOUT) == "QGEMM_ERR_TIMEOUT"
+    assert qgemm.status_name(12345) == "QGEMM_ERR_UNKNOWN"
+
+
+def test_null_handles_return_status():
+    import qgemm._lib as L
+    lib = L.lib()
+    assert lib.qgemm_stream_sync(None) == L.ERR_BAD_HANDLE
+    assert "stream" in L.last_error()
+    assert lib.qgemm_w8a32_gemm(None, 1, 1, 1, 1, 1, 4, 4, 4) == L.ERR_BAD_HANDLE
+    assert lib.qgemm_device_close(None) == L.ERR_BAD_HANDLE
+    assert lib.qgemm_comm_destroy(None) == L.ERR_BAD_HANDLE
+    assert lib.qgemm_device_open(0, None) == L.ERR_INVALID_ARG
+
+
+def test_device_count_without_gpu():
+    import torch
+    import qgemm
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    assert qgemm.device_count() == 0
+    import qgemm._lib as L
+    h = ctypes.c_void_p()
+    assert L.lib().qgemm_device_open(0, ctypes.byref(h)) == L.ERR_NO_DEVICE
+
+
+@pytest.mark.parametrize("N,world,align", [(28672, 8, 256), (28672, 2, 256), (4096, 4, 128),
+                                           (1000, 3, 16), (7, 4, 1), (256, 8, 256)])
+def test_shard_columns_partition(N, world, align):
+    import qgemm
+    bounds = [qgemm.shard_columns(N, world, r, align) for r in range(world)]
+    assert bounds[0][0] == 0 and bounds[-1][1] == N
+    for (a0, a1), (b0, b1) in zip(bounds, bounds[1:]):
+        assert a1 == b0 and a0 <= a1
+    for a0, _ in bounds:
+        assert a0 % align == 0 or a0 == N
+    if N % (world * align) == 0:
+        assert len({b - a for a, b in bounds}) == 1
+
+
+def test_shard_columns_rejects_bad_input():
+    import qgemm._lib as L
+    a, b = ctypes.c_int(), ctypes.c_int()
+    assert L.lib().qgemm_shard_columns(100, 2, 2, 16, ctypes.byref(a), ctypes.byref(b)) == \
+        L.ERR_INVALID_ARG
+    assert L.lib().qgemm_shard_columns(100, 0, 0, 16, ctypes.byref(a), ctypes.byref(b)) == \
+        L.ERR_INVALID_ARG
+
+
+def test_by_name_rejects_unknown_without_a_stream():
+    import qgemm._lib as L
+    bufs = (ctypes.c_uint64 * 1)(0)
+    ints = (ctypes.c_int * 1)(0)
+    assert L.lib().qgemm_launch_by_name(None, b"noSuchKernel", bufs, 1, ints, 1) == \
+        L.ERR_INVALID_ARG

@@ -1,0 +1,126 @@
+"""The remaining reference operators on the GPU, bit-exact against the oracle
+(QuantizedGemmOps.scala:24-84 w8a16Gemm / RowWise, :121-192 quantizers,
+:198-212 dequantize), the by-name launch path, the weight prepack and the
+column unshard used after the multi-GPU all-gather."""
+import os
+
+import numpy as np
+import pytest
+
+import qgemm
+import qgemm.synthetic as syn
+from helpers import Out, dev_array
+
+pytestmark = pytest.mark.gpu
+
+GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
+
+
+def f32_bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("has_bias", [True, False])
+def test_w8a16(gpu, oracle, has_bias):
+    dev, st, ops = gpu
+    rng = np.random.default_rng(51)
+    M, N, K = 37, 300, 129
+    w = rng.integers(-127, 128, (K, N), dtype=np.int8)
+    sw = rng.uniform(0.001, 0.01, N).astype(np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    y = Out(dev, st, M * N * 4)
+    ops.w8a16Gemm(dev_array(gpu, w), dev_array(gpu, sw), dev_array(gpu, x), dev_array(gpu, b), y,
+                  M, N, K, has_bias)
+    st.sync()
+    ref = oracle.w8a16_gemm(w, sw, x, b if has_bias else None)
+    np.testing.assert_array_equal(y.read(np.uint32, (M, N)), f32_bits(ref))
+
+
+def test_w8a16_rowwise_golden(gpu):
+    dev, st, ops = gpu
+    w, x = GOLD["w8a16_w"], GOLD["w8a16_x"]
+    K, N = w.shape
+    M = x.shape[0]
+    y = Out(dev, st, M * N * 4)
+    ops.w8a16GemmRowWise(dev_array(gpu, w), dev_array(gpu, GOLD["w8a16_swr"]), dev_array(gpu, x),
+                         y, M, N, K)
+    st.sync()
+    np.testing.assert_array_equal(y.read(np.uint32, (M, N)), f32_bits(GOLD["w8a16_y_rowwise"]))
+
+
+@pytest.mark.parametrize("qbits", [8, 4])
+def test_dynamic_quantize_golden(gpu, qbits):
+    dev, st, ops = gpu
+    wt = GOLD["quant_w"]
+    K, N = wt.shape
+    s = Out(dev, st, N * 4)
+    q = Out(dev, st, K * N)
+    ops.dynamicQuantize(dev_array(gpu, wt), s, q, K, N, qbits)
+    st.sync()
+    np.testing.assert_array_equal(q.read(np.int8, (K, N)), GOLD[f"quant{qbits}_q"])
+    np.testing.assert_array_equal(s.read(np.uint32, (N,)), f32_bits(GOLD[f"quant{qbits}_scales"]))
+
+
+def test_quantizers_random(gpu, oracle):
+    dev, st, ops = gpu
+    rng = np.random.default_rng(52)
+    K, N = 513, 333
+    wt = (rng.standard_normal((K, N)) * rng.uniform(0.01, 3, N)).astype(np.float32)
+    s, q, z = Out(dev, st, N * 4), Out(dev, st, K * N), Out(dev, st, N)
+    ops.weightOnlyQuantizePerChannel(dev_array(gpu, wt), s, q, z, K, N)
+    st.sync()
+    so, qo, zo = oracle.weight_only_quantize_per_channel(wt)
+    np.testing.assert_array_equal(q.read(np.int8, (K, N)), qo)
+    np.testing.assert_array_equal(s.read(np.uint32, (N,)), f32_bits(so))
+    np.testing.assert_array_equal(z.read(np.int8, (N,)), zo)
+    # dequantize the result back (QuantizedGemmOps.scala:198-212)
+    w2 = Out(dev, st, K * N * 4)
+    ops.dequantize(dev_array(gpu, qo), dev_array(gpu, so), w2, K, N)
+    st.sync()
+    np.testing.assert_array_equal(w2.read(np.uint32, (K, N)), f32_bits(oracle.dequantize(qo, so)))
+
+
+def test_by_name_matches_direct(gpu, oracle):
+    dev, st, ops = gpu
+    A, B, sA, sB = syn.w8a8_inputs(64, 512, 512, seed=53)
+    d = {k: dev_array(gpu, v) for k, v in dict(A=A, B=B, sA=sA, sB=sB).items()}
+    y = Out(dev, st, 64 * 512 * 4)
+    ops.launchKernel("w8a32Gemm", [d["B"], d["sB"], d["A"], d["sA"], y], [64, 512, 512])
+    st.sync()
+    yo, _ = oracle.w8a32_gemm(B, sB, A, sA)
+    np.testing.assert_array_equal(y.read(np.uint32, (64, 512)), f32_bits(yo))
+    with pytest.raises(qgemm.QGemmError):
+        ops.launchKernel("w8a32Gemm", [d["B"]], [64, 512, 512])
+    with pytest.raises(qgemm.QGemmError):
+        ops.launchKernel("tritonNoSuchKernel", [], [])
+
+
+def test_prepack_roundtrip_and_gemm(gpu, oracle):
+    dev, st, ops = gpu
+    M, N, K = 96, 768, 640
+    A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=54)
+    nk = Out(dev, st, N * K)
+    ops.prepackW8NK(dev_array(gpu, B), nk, K, N)
+    st.sync()
+    np.testing.assert_array_equal(nk.read(np.int8, (N, K)), B.T)
+    y = Out(dev, st, M * N * 2)
+    ops.w8a8Gemm(dev_array(gpu, A), nk, dev_array(gpu, sA), dev_array(gpu, sB), y, M, N, K,
+                 b_layout=qgemm.B_NK)
+    st.sync()
+    yo, _ = oracle.w8a32_gemm(B, sB, A, sA)
+    np.testing.assert_array_equal(y.read(np.uint16, (M, N)), oracle.bf16_rne(yo))
+
+
+@pytest.mark.parametrize("world,M,ncols", [(4, 33, 24), (2, 16, 13), (8, 5, 256)])
+def test_unshard_columns(gpu, world, M, ncols):
+    import qgemm._lib as L
+    dev, st, _ = gpu
+    rng = np.random.default_rng(55)
+    g = rng.integers(0, 65535, (world, M, ncols), dtype=np.uint16)
+    out = Out(dev, st, M * world * ncols * 2)
+    L.call("qgemm_unshard_columns_bf16", st.handle, dev_array(gpu, g).address, out.address, world,
+           M, ncols)
+    st.sync()
+    np.testing.assert_array_equal(out.read(np.uint16, (M, world * ncols)),
+                                  np.concatenate(list(g), axis=1))

@@ -1,0 +1,109 @@
+"""W4A16 on the GPU against the CPU oracle.
+
+* reference entry point (QuantizedGemmOps.w4a16Gemm, QuantizedGemmOps.scala:218-247):
+  bit-exact, same per-element fp32 order;
+* group-wise decode path (bf16 x, per-group bf16 scales, zero point):
+  - tensor-core fast path: max elementwise relative error <= 1e-2 on bf16
+    outputs (helpers.rel_err: |y-r| / max(|r|, 1e-2*rms(r)));
+  - any-shape CUDA-core path: bit-exact (same order as the oracle).
+"""
+import numpy as np
+import pytest
+
+import qgemm.synthetic as syn
+from helpers import Out, dev_array, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 1e-2
+
+
+def grouped(gpu, x, wq, sc, M, N, K, G, zp=8):
+    dev, st, ops = gpu
+    y = Out(dev, st, M * N * 2)
+    ops.w4a16GemmGrouped(dev_array(gpu, x), dev_array(gpu, wq), dev_array(gpu, sc), y, M, N, K,
+                         zero_point=zp, group_size=G)
+    st.sync()
+    return y.read(np.uint16, (M, N))
+
+
+def test_reference_entry_point(gpu, oracle):
+    dev, st, ops = gpu
+    M, N, K = 64, 512, 512
+    rng = np.random.default_rng(21)
+    wb = rng.integers(0, 256, size=K * N // 2, dtype=np.uint8)
+    sw = rng.uniform(0.005, 0.02, N).astype(np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    y = Out(dev, st, M * N * 4)
+    ops.w4a16Gemm(dev_array(gpu, wb), dev_array(gpu, sw), dev_array(gpu, x), y, M, N, K)
+    st.sync()
+    ref = oracle.w4a16_gemm(wb, sw, x, N)
+    np.testing.assert_array_equal(y.read(np.uint32, (M, N)), ref.view(np.uint32))
+
+
+def test_reference_entry_point_odd_n(gpu, oracle):
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
+    dev, st, ops = gpu
+    x = g["w4a16_x"]
+    M, K = x.shape
+    N = int(g["w4a16_N"])
+    y = Out(dev, st, M * N * 4)
+    ops.w4a16Gemm(dev_array(gpu, g["w4a16_w"]), dev_array(gpu, g["w4a16_sw"]), dev_array(gpu, x),
+                  y, M, N, K)
+    st.sync()
+    np.testing.assert_array_equal(y.read(np.uint32, (M, N)), g["w4a16_y"].view(np.uint32))
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_grouped_config3(gpu, oracle, M):
+    N, K, G = 14336, 4096, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=30 + M)
+    y = grouped(gpu, x, wq, sc, M, N, K, G)
+    ref, _ = oracle.w4a16_grouped(wq, sc, 8, G, x)
+    err = rel_err(syn.bf16_to_float(y), ref)
+    assert err <= TOL_BF16, err
+
+
+@pytest.mark.parametrize("M,N,K,G,zp", [(3, 400, 512, 64, 8), (20, 256, 1024, 128, 3),
+                                        (8, 128, 256, 128, 8), (2, 2048, 4096, 32, 0),
+                                        (9, 1040, 2048, 128, 15)])
+def test_grouped_fast_path_shapes(gpu, oracle, M, N, K, G, zp):
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M + N + K)
+    y = grouped(gpu, x, wq, sc, M, N, K, G, zp)
+    ref, _ = oracle.w4a16_grouped(wq, sc, zp, G, x)
+    err = rel_err(syn.bf16_to_float(y), ref)
+    assert err <= TOL_BF16, err
+
+
+@pytest.mark.parametrize("M,N,K,G", [(2, 24, 40, 8), (3, 8, 16, 16), (1, 40, 30, 10)])
+def test_grouped_simt_path_exact(gpu, oracle, M, N, K, G):
+    x, wq, _ = syn.w4a16_inputs(M, N, K, group=K, seed=7)
+    rng = np.random.default_rng(8)
+    sc = syn.bf16_bits(rng.uniform(0.005, 0.02, (K // G, N)).astype(np.float32))
+    y = grouped(gpu, x, wq, sc, M, N, K, G)
+    _, refb = oracle.w4a16_grouped(wq, sc, 8, G, x)
+    np.testing.assert_array_equal(y, refb)
+
+
+def test_grouped_deterministic(gpu):
+    M, N, K, G = 4, 14336, 4096, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=40)
+    a = grouped(gpu, x, wq, sc, M, N, K, G)
+    b = grouped(gpu, x, wq, sc, M, N, K, G)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_grouped_rejects_bad_args(gpu):
+    import qgemm
+    dev, st, ops = gpu
+    with pytest.raises(qgemm.QGemmError) as e:
+        ops.w4a16GemmGrouped(8, 8, 8, 8, 1, 12, 64, group_size=64)  # N % 8 != 0
+    assert e.value.status == qgemm._lib.ERR_INVALID_ARG
+    with pytest.raises(qgemm.QGemmError) as e:
+        ops.w4a16GemmGrouped(8, 8, 8, 8, 1, 16, 100, group_size=64)  # K % G != 0
+    assert e.value.status == qgemm._lib.ERR_INVALID_ARG
+    with pytest.raises(qgemm.QGemmError) as e:
+        ops.w4a16GemmGrouped(8, 8, 8, 8, 1, 16, 64, group_size=64, zero_point=16)
+    assert e.value.status == qgemm._lib.ERR_INVALID_ARG
+    st.sync()
