@@ -51,6 +51,8 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-large", action="store_true", help="skip the sharded large GEMM")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large"], default="all",
+                   help="run one workload alone (for profiling); prints its own JSON line")
     return p.parse_args()
 
 
@@ -87,13 +89,12 @@ class ClockSampler:
             import pynvml as nv
             nv.nvmlInit()
             self.nv = nv
-            h = None
-            try:
-                import torch
-                bus = torch.cuda.get_device_properties(torch_dev).pci_bus_id
-                h = nv.nvmlDeviceGetHandleByPciBusId(bus)
-            except Exception:
-                h = nv.nvmlDeviceGetHandleByIndex(torch_dev)
+            import torch
+            p = torch.cuda.get_device_properties(torch_dev)
+            # torch reports the PCI location as integers; NVML wants "DDDDDDDD:BB:DD.F".
+            bus = "%08X:%02X:%02X.0" % (int(p.pci_domain_id), int(p.pci_bus_id),
+                                        int(p.pci_device_id))
+            h = nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
             self.h = h
             self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
             self.ok = True
@@ -459,7 +460,13 @@ def reference_arm(args):
     return 0
 
 
+def log(msg: str):
+    print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
 def main():
+    import faulthandler
+    faulthandler.enable()
     args = parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -473,7 +480,28 @@ def main():
     clocks = ClockSampler(local)
     K, W = max(1, args.steps), max(3, args.warmup)
 
+    if args.only == "w4a16":
+        log("w4a16 decode (only)")
+        r = w4a16_decode(ops, peaks)
+        if rank == 0:
+            print(json.dumps({"only": "w4a16", "w4a16_decode": r}), flush=True)
+        return 0
+    if args.only == "large":
+        log("w8a8 large (only)")
+        r = w8a8_large(ops, st, rank, world, K, W)
+        if rank == 0:
+            print(json.dumps({"only": "large", "w8a8_large": r}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return 0
+    log("w8a8 headline")
     hb = w8a8_headline(ops, st, rank, world, K, W, clocks)
+    if args.only == "w8a8":
+        if rank == 0:
+            print(json.dumps({"only": "w8a8", "TOPS": hb["value"],
+                              "us_per_launch": hb["per_launch_s"] * 1e6}), flush=True)
+        return 0
     int8_peak = 2.0 * peaks["bf16_tflops"]
     achieved = hb["ops_per_launch"] / hb["per_launch_s"] / 1e12
     roofline = {"bound": "tensor", "kernel": "w8a8_tcgen05", "achieved": achieved,
@@ -482,9 +510,11 @@ def main():
                 "algorithmic_ops_per_launch": hb["ops_per_launch"],
                 "peak_basis": f"2 x bf16_tflops ({peak_src}, burst cuBLAS bf16): dense int8 "
                               f"runs at twice the bf16 rate on B200"}
+    log("e2e")
     e2e = w8a8_e2e(ops, st, hb, rank, world, max(10, min(K, 50)))
     extra = {}
     if world == 1 and rank == 0:
+        log("w4a16 decode")
         extra["w4a16_decode"] = w4a16_decode(ops, peaks)
         extra["w4a16_decode"]["peak_GB_s"] = peaks["hbm_gbs"]
         extra["w4a16_decode"]["peak_basis"] = f"hbm_gbs ({peak_src})"
@@ -493,9 +523,11 @@ def main():
         hb.pop(k)
     torch.cuda.empty_cache()
     if not args.no_large:
+        log("w8a8 large")
         extra["w8a8_large"] = w8a8_large(ops, st, rank, world, 10, 3)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
+        log("cpu baseline")
         cpu = cpu_w8a8_sample()
     if rank == 0:
         clk = clocks.summary()
