@@ -70,6 +70,13 @@ qgemm_status launch_prepack_w8_nk(qgemm_stream_s* s, const int8_t* src, int8_t* 
                                   int N);
 qgemm_status launch_unshard_bf16(qgemm_stream_s* s, const uint16_t* g, uint16_t* out,
                                  int world, int M, int ncols);
+bool w4a16_tile_supported(const qgemm_device_s* d, uint64_t x, uint64_t wt, uint64_t sc, int M,
+                          int N, int K, int G, const char** why);
+qgemm_status launch_w4a16_tile(qgemm_stream_s* s, const void* x, const uint8_t* wt,
+                               const void* sc, int zp, int G, void* y, int M, int N, int K);
+size_t w4_tiled_bytes(int K, int N);
+qgemm_status launch_prepack_w4_tiled(qgemm_stream_s* s, const uint32_t* src, uint8_t* dst, int K,
+                                     int N);
 qgemm_status launch_w4a16_grouped(qgemm_stream_s* s, const void* x, const uint32_t* wq,
                                   const void* scales, int zp, int group, void* y, int M,
                                   int N, int K);

@@ -54,6 +54,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As above, but a thread whose phase is not complete may be suspended for up to
+// `hint_ns` instead of returning at once, so waiting warps do not take issue slots
+// from the warps that are computing.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that sleeps between polls (for warps that have nothing else to do).
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity,
+                                                const volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 10000u)) return true;
+    if (abort && *abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // Waits for the phase with the given parity to complete.  Returns false when
 // the wait runs past kWaitLimitNs or when *abort (shared memory) becomes
 // non-zero, so that no wait can spin forever.
@@ -81,8 +109,28 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Programmatic dependent launch: wait for the previous kernel in the stream to
+// complete (and its writes to be visible); let the next kernel start launching.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---- tcgen05 ----------------------------------------------------------------

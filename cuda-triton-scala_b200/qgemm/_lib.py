@@ -69,6 +69,9 @@ SIGNATURES = {
     "qgemm_dequantize": (_S, [_P, _U64, _U64, _U64, _I, _I]),
     "qgemm_w8a8_gemm": (_S, [_P, _U64, _U64, _I, _U64, _U64, _U64, _I, _I, _I, _I, _I, _U64, _I]),
     "qgemm_w4a16_grouped_gemm": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I]),
+    "qgemm_w4a16_grouped_gemm_tiled": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I]),
+    "qgemm_w4_tiled_bytes": (_S, [_I, _I, ctypes.POINTER(_SZ)]),
+    "qgemm_prepack_w4_tiled": (_S, [_P, _U64, _U64, _I, _I]),
     "qgemm_prepack_w8_nk": (_S, [_P, _U64, _U64, _I, _I]),
     "qgemm_launch_by_name": (_S, [_P, ctypes.c_char_p, ctypes.POINTER(_U64), _I,
                                   ctypes.POINTER(_I), _I]),

@@ -75,6 +75,22 @@ class QuantizedGemmOps:
         L.call("qgemm_w4a16_grouped_gemm", self._h, L.addr(x), L.addr(wq), L.addr(scales),
                zero_point, group_size, L.addr(y), M, N, K)
 
+    def w4a16GemmGroupedTiled(self, x, wt, scales, y, M: int, N: int, K: int, *,
+                              zero_point: int = 8, group_size: int = 128):
+        """Group-wise W4A16 on weights prepacked by prepackW4Tiled (the fast decode path)."""
+        L.call("qgemm_w4a16_grouped_gemm_tiled", self._h, L.addr(x), L.addr(wt), L.addr(scales),
+               zero_point, group_size, L.addr(y), M, N, K)
+
+    @staticmethod
+    def w4TiledBytes(K: int, N: int) -> int:
+        n = ctypes.c_size_t(0)
+        L.call("qgemm_w4_tiled_bytes", K, N, ctypes.byref(n))
+        return n.value
+
+    def prepackW4Tiled(self, wq, dst, K: int, N: int):
+        """uint32 [K, N/8] reference-order int4 weights -> 256-column tiles (one time)."""
+        L.call("qgemm_prepack_w4_tiled", self._h, L.addr(wq), L.addr(dst), K, N)
+
     def prepackW8NK(self, src_kn, dst_nk, K: int, N: int):
         L.call("qgemm_prepack_w8_nk", self._h, L.addr(src_kn), L.addr(dst_nk), K, N)
 

@@ -178,6 +178,23 @@ QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm(qgemm_stream_t s, uint64_t x, ui
                                       uint64_t scales, int zero_point, int group_size,
                                       uint64_t y, int M, int N, int K);
 
+/* The same group-wise W4A16 on weights repacked once by qgemm_prepack_w4_tiled
+ * (64-column tiles, each tile's rows contiguous, so every CTA streams one block of
+ * memory: the fast decode path).  Requires sm_100, K % 512 == 0, group_size a
+ * multiple of 16 that divides 128 or is a multiple of 128, N % 8 == 0 and 16-byte
+ * aligned x, wt and scales; otherwise QGEMM_ERR_UNSUPPORTED.  Deterministic. */
+QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_tiled(qgemm_stream_t s, uint64_t x, uint64_t wt,
+                                                      uint64_t scales, int zero_point,
+                                                      int group_size, uint64_t y, int M, int N,
+                                                      int K);
+
+/* One-time int4 weight repack: uint32 [K, N/8] (reference nibble order) ->
+ * tiled[t][k][32 bytes] = bytes [32*t, 32*t+32) of row k, for 64-column tiles t
+ * (zero-padded past N).  qgemm_w4_tiled_bytes gives the buffer size. */
+QGEMM_API qgemm_status qgemm_w4_tiled_bytes(int K, int N, size_t* bytes);
+QGEMM_API qgemm_status qgemm_prepack_w4_tiled(qgemm_stream_t s, uint64_t wq, uint64_t dst, int K,
+                                              int N);
+
 /* One-time weight repack: int8 [K,N] (reference layout) -> [N,K] (K-major). */
 QGEMM_API qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src_kn, uint64_t dst_nk,
                                  int K, int N);

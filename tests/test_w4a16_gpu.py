@@ -27,6 +27,40 @@ def grouped(gpu, x, wq, sc, M, N, K, G, zp=8):
     return y.read(np.uint16, (M, N))
 
 
+def tiled(gpu, x, wq, sc, M, N, K, G, zp=8):
+    """Prepack once, then the tiled fast path."""
+    dev, st, ops = gpu
+    wt = Out(dev, st, ops.w4TiledBytes(K, N))
+    ops.prepackW4Tiled(dev_array(gpu, wq), wt, K, N)
+    y = Out(dev, st, M * N * 2)
+    ops.w4a16GemmGroupedTiled(dev_array(gpu, x), wt, dev_array(gpu, sc), y, M, N, K,
+                              zero_point=zp, group_size=G)
+    st.sync()
+    return y.read(np.uint16, (M, N))
+
+
+def tiled_layout_numpy(wq, K, N):
+    """The documented tiled layout: tiled[t][k][j] = byte 32*t + j of row k (64-column tiles)."""
+    rows = wq.view(np.uint8).reshape(K, N // 2)
+    nt = (N + 63) // 64
+    pad = np.zeros((K, nt * 32), np.uint8)
+    pad[:, : N // 2] = rows
+    return pad.reshape(K, nt, 32).transpose(1, 0, 2).copy()
+
+
+@pytest.mark.parametrize("K,N", [(64, 512), (48, 8 * 41), (16, 14336), (128, 264)])
+def test_prepack_w4_tiled_layout(gpu, K, N):
+    dev, st, ops = gpu
+    _, wq, _ = syn.w4a16_inputs(1, N, K, group=16, seed=K + N)
+    nbytes = ops.w4TiledBytes(K, N)
+    assert nbytes == ((N + 63) // 64) * K * 32
+    wt = Out(dev, st, nbytes)
+    ops.prepackW4Tiled(dev_array(gpu, wq), wt, K, N)
+    st.sync()
+    got = wt.read(np.uint8, ((N + 63) // 64, K, 32))
+    np.testing.assert_array_equal(got, tiled_layout_numpy(wq, K, N))
+
+
 def test_reference_entry_point(gpu, oracle):
     dev, st, ops = gpu
     M, N, K = 64, 512, 512
@@ -76,6 +110,41 @@ def test_grouped_fast_path_shapes(gpu, oracle, M, N, K, G, zp):
     assert err <= TOL_BF16, err
 
 
+@pytest.mark.parametrize("M,N,K,G,zp", [
+    (1, 32, 512, 16, 8),         # one partial tile, group 16 (32 scale rows per stage)
+    (5, 8192 + 32, 512, 16, 8),  # partial last tile
+    (16, 4096, 1024, 64, 4),     # few tiles: K split over a 2-CTA cluster
+    (2, 2048, 2048, 32, 8),      # 32 tiles: K split over a 4-CTA cluster
+    (7, 3072, 2048, 256, 8),     # group larger than a warp's rows
+    (2, 1024, 2048, 512, 8),     # group as large as a stage
+    (33, 512, 1024, 128, 8),     # three M passes (16 + 16 + 1)
+    (1, 14336, 4096, 128, 0),    # decode shape, other zero point
+    (4, 14336, 4096, 128, 8),
+    (16, 14336, 4096, 128, 8),
+    (3, 1000, 512, 64, 8),       # N not a multiple of 64
+])
+def test_grouped_tiled_path(gpu, oracle, M, N, K, G, zp):
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M * 3 + N + K + G)
+    y = tiled(gpu, x, wq, sc, M, N, K, G, zp)
+    ref, _ = oracle.w4a16_grouped(wq, sc, zp, G, x)
+    err = rel_err(syn.bf16_to_float(y), ref)
+    assert err <= TOL_BF16, err
+
+
+def test_grouped_tiled_repeat_counters_reset(gpu):
+    """Split-K arrival counters return to zero: repeated calls, alternating
+    shapes, give identical results."""
+    a = syn.w4a16_inputs(4, 14336, 4096, group=128, seed=60)
+    b = syn.w4a16_inputs(16, 6144, 2048, group=64, seed=61)
+    ya = [tiled(gpu, *a, 4, 14336, 4096, 128) for _ in range(2)]
+    yb = tiled(gpu, *b, 16, 6144, 2048, 64)
+    ya.append(tiled(gpu, *a, 4, 14336, 4096, 128))
+    yb2 = tiled(gpu, *b, 16, 6144, 2048, 64)
+    np.testing.assert_array_equal(ya[0], ya[1])
+    np.testing.assert_array_equal(ya[0], ya[2])
+    np.testing.assert_array_equal(yb, yb2)
+
+
 @pytest.mark.parametrize("M,N,K,G", [(2, 24, 40, 8), (3, 8, 16, 16), (1, 40, 30, 10)])
 def test_grouped_simt_path_exact(gpu, oracle, M, N, K, G):
     x, wq, _ = syn.w4a16_inputs(M, N, K, group=K, seed=7)
@@ -92,6 +161,28 @@ def test_grouped_deterministic(gpu):
     a = grouped(gpu, x, wq, sc, M, N, K, G)
     b = grouped(gpu, x, wq, sc, M, N, K, G)
     np.testing.assert_array_equal(a, b)
+
+
+def test_tiled_rejects_unsupported_shapes(gpu):
+    import qgemm
+    dev, st, ops = gpu
+    x, wq, sc = syn.w4a16_inputs(1, 256, 256, group=64, seed=63)
+    wt = Out(dev, st, ops.w4TiledBytes(256, 256))
+    ops.prepackW4Tiled(dev_array(gpu, wq), wt, 256, 256)
+    y = Out(dev, st, 256 * 2)
+    with pytest.raises(qgemm.QGemmError) as e:   # K % 512 != 0
+        ops.w4a16GemmGroupedTiled(dev_array(gpu, x), wt, dev_array(gpu, sc), y, 1, 256, 256,
+                                  group_size=64)
+    assert e.value.status == qgemm._lib.ERR_UNSUPPORTED
+    st.sync()
+
+
+def test_tiled_and_canonical_agree(gpu):
+    M, N, K, G = 8, 4096, 2048, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=62)
+    a = syn.bf16_to_float(tiled(gpu, x, wq, sc, M, N, K, G)).astype(np.float64)
+    b = syn.bf16_to_float(grouped(gpu, x, wq, sc, M, N, K, G)).astype(np.float64)
+    assert rel_err(a, b) <= TOL_BF16
 
 
 def test_grouped_rejects_bad_args(gpu):
