@@ -43,12 +43,16 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;     // 48 KB
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 2 * BN;                  // two accumulators
 constexpr int BAR_BYTES = 256;
+// Output staging for TMA stores: two 16 KB buffers of 128 rows x 128 bytes (64 bf16 or
+// 32 fp32 columns), 128-byte swizzled, placed right after the operand stages.
+constexpr int STG_BYTES = 2 * 128 * 128;
 // The whole opt-in shared memory of an SM (227 KB): STAGES * 48 KB of tiles plus
 // barriers and 1 KB of alignment slack, and headroom so that every address a
 // UMMA descriptor of the last stage can reach (under either reading of the
 // MN-major leading/stride offsets) stays inside this CTA's allocation.
 constexpr int SMEM_BYTES = 232448;
-static_assert(STAGES * STAGE_BYTES + BAR_BYTES + 1024 <= SMEM_BYTES, "shared memory budget");
+static_assert(STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024 <= SMEM_BYTES,
+              "shared memory budget");
 constexpr int GROUP_M = 16;                         // tile raster: 16 m-blocks per group
 
 struct Params {
@@ -63,7 +67,9 @@ struct Params {
   int* err;
   int out_vec;     // out base 16-byte aligned and rows a multiple of 16 bytes
   int acc_vec;     // same for the int32 accumulator output
+  int tma_store;   // the output is written with TMA bulk tensor stores (needs out_vec)
 };
+
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
   const int group_size = GROUP_M * p.num_n_blocks;
@@ -78,6 +84,15 @@ __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, 
 __device__ __forceinline__ void report(int* err, int code, volatile int* abort_flag) {
   *abort_flag = 1;
   if (err) atomicCAS(err, 0, code);
+}
+
+// As report(), and also raises the abort flag of the other CTA of the pair so that
+// its waits give up at once instead of each running to its time limit.
+__device__ __forceinline__ void report_pair(int* err, int code, volatile int* abort_flag,
+                                            uint32_t rank) {
+  report(err, code, abort_flag);
+  const uint32_t peer = ptx::map_to_rank(ptx::smem_u32(const_cast<int*>(abort_flag)), rank ^ 1u);
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer), "r"(1) : "memory");
 }
 
 // Epilogue for 32 consecutive columns of one row.
@@ -142,22 +157,120 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
   }
 }
 
+
+// Epilogue of one accumulator: this CTA's 128 rows (row0..row0+127) x 256 columns
+// (n0..n0+255) held in TMEM columns [acc_col, acc_col+256).  Warp q reads TMEM lanes
+// 32q..32q+31 (one output row per thread), dequantises, and writes 128-byte row pieces
+// into the swizzled staging buffer; one elected thread then stores each 128-row x
+// 128-byte block with a TMA bulk tensor store (clipped at the tensor edges).  `chunk_seq`
+// counts staging buffers used so far (identical in all epilogue threads).
+__device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tmO,
+                                              uint32_t tmem_base, uint32_t acc_col, int q,
+                                              int lane, int row0, int n0, uint32_t stg,
+                                              bool elected, int& chunk_seq, bool ok) {
+  const int row = row0 + q * 32 + lane;
+  const int rl = q * 32 + lane;  // row within the staging block
+  const float sa = (row < p.M) ? __ldg(p.sA + row) : 0.f;
+  if (!p.tma_store) {
+#pragma unroll 1
+    for (int c = 0; c < 256 / 32; ++c) {
+      uint32_t r[32];
+      __syncwarp();
+      if (!ok) return;
+      ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + c * 32, r);
+      ptx::tmem_wait_ld();
+      store_chunk(p, row, n0 + c * 32, sa, r);
+    }
+    return;
+  }
+  const bool bf16 = p.out_dtype == QGEMM_BF16;
+  const int cwe = bf16 ? 64 : 32;  // columns per 128-byte staging row
+#pragma unroll 1
+  for (int ch = 0; ch < 256 / cwe; ++ch, ++chunk_seq) {
+    const uint32_t buf = stg + (uint32_t)(chunk_seq & 1) * (128 * 128);
+    // the store issued two chunks ago (same buffer) must have finished reading it
+    if (elected) ptx::bulk_wait_group_read<1>();
+    ptx::named_bar_sync(1, 128);
+#pragma unroll 1
+    for (int sub = 0; sub < cwe / 32; ++sub) {
+      uint32_t r[32];
+      const int nc = n0 + ch * cwe + sub * 32;
+      __syncwarp();
+      if (ok) {
+        ptx::tmem_ld_32x32b_x32(
+            tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + (uint32_t)(ch * cwe + sub * 32), r);
+        ptx::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;  // a wait ran out: keep the barrier sequence
+      }
+      float sb[32];
+      if (nc + 32 <= p.N && ((reinterpret_cast<uintptr_t>(p.sB + nc) & 15) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(p.sB + nc + j));
+          sb[j] = v.x; sb[j + 1] = v.y; sb[j + 2] = v.z; sb[j + 3] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sb[j] = (nc + j < p.N) ? __ldg(p.sB + nc + j) : 0.f;
+      }
+      if (p.acc && row < p.M) {
+        int32_t* dst = p.acc + (size_t)row * p.N + nc;
+        for (int j = 0; j < 32 && nc + j < p.N; ++j) dst[j] = (int)r[j];
+      }
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
+      if (bf16) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // four 16-byte pieces = 32 bf16
+          uint32_t w[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * h], v[8 * j + 2 * h + 1]);
+            w[h] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          const int piece = sub * 4 + j;
+          ptx::st_shared_v4(buf + rl * 128 + ((piece ^ (rl & 7)) << 4), w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // eight 16-byte pieces = 32 fp32
+          ptx::st_shared_v4(buf + rl * 128 + ((j ^ (rl & 7)) << 4), __float_as_uint(v[4 * j]),
+                            __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                            __float_as_uint(v[4 * j + 3]));
+        }
+      }
+    }
+    ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
+    ptx::named_bar_sync(1, 128);
+    if (elected) {
+      ptx::tma_store_2d(tmO, buf, n0 + ch * cwe, row0);
+      ptx::bulk_commit_group();
+    }
+  }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const Params p) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmO, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: required by the 128-byte swizzle pattern of TMA and UMMA.
   const uint32_t raw_base = ptx::smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw_base);
 
-  const uint32_t bar_base = base + STAGES * STAGE_BYTES;
+  const uint32_t stg_base = base + STAGES * STAGE_BYTES;  // output staging (1024-aligned)
+  const uint32_t bar_base = stg_base + STG_BYTES;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
   auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + a); };
   auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + 2 + a); };
   const uint32_t drain_bar = bar_base + 8u * (2 * STAGES + 4);
-  uint8_t* gbar = gbase + STAGES * STAGE_BYTES;
+  uint8_t* gbar = gbase + STAGES * STAGE_BYTES + STG_BYTES;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbar + 8 * (2 * STAGES + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbar + 8 * (2 * STAGES + 5) + 4);
 
@@ -286,32 +399,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const bool elected = (warp == 2 && lane == 0);
+    int chunk_seq = 0;
     int it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int a = it & 1;
       const uint32_t aphase = (uint32_t)((it >> 1) & 1);
-      if (!ptx::mbar_wait(tfull_bar(a), aphase, abort_flag)) {
-        if (!*abort_flag) report(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag);
-        break;
-      }
+      bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is .sync.aligned
+      if (!ok && lane == 0 && !*abort_flag) report(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag);
       ptx::tc_fence_after();
-      const int row = mb * BM + q * 32 + lane;
-      const float sa = (row < p.M) ? __ldg(p.sA + row) : 0.f;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        const uint32_t taddr =
-            tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN + c * 32);
-        __syncwarp();
-        ptx::tmem_ld_32x32b_x32(taddr, r);
-        ptx::tmem_wait_ld();
-        store_chunk(p, row, nb * BN + c * 32, sa, r);
-      }
+      epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM, nb * BN, stg_base,
+                    elected, chunk_seq, ok);
       ptx::tc_fence_before();
       ptx::mbar_arrive(tempty_bar(a));
     }
+    if (elected) ptx::bulk_wait_group_all();
   }
 
   ptx::tc_fence_before();
@@ -320,6 +425,205 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     __syncwarp();
     ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------------
+// CTA-pair kernel: one 256 x 256 tile per cluster of two CTAs (tcgen05 cta_group::2).
+// CTA r of the pair loads A rows [256*mb + 128*r, +128) and B columns
+// [256*nb + 128*r, +128) into its own shared memory; both CTAs' copies complete on
+// the even CTA's "full" barrier.  The even CTA's MMA thread issues M=256 N=256 K=32
+// MMAs that read both CTAs' tiles and write rows 128*r.. of D into CTA r's TMEM, and
+// its commits arrive on the "empty"/"tfull" barriers of both CTAs.  Each CTA's
+// epilogue drains its own TMEM half and arrives on the even CTA's "tempty" barrier.
+// Per SM and 128-deep k-block this moves 32 KB through shared memory for 512 cycles
+// of MMA (the single-CTA 128 x 256 tile moves 48 KB), which is what lets the tensor
+// pipe run near its rate without exceeding shared-memory bandwidth.
+namespace pair {
+constexpr int BM = 256;                        // rows per pair tile (128 per CTA)
+constexpr int BN = 256;                        // columns per pair tile (128 of B per CTA)
+constexpr int STAGES = 6;
+constexpr int A_BYTES = 128 * BK;              // 16 KB
+constexpr int B_BYTES = 128 * BK;              // 16 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES; // 32 KB per CTA
+constexpr int SMEM_BYTES = 232448;
+static_assert(STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024 <= SMEM_BYTES,
+              "shared memory budget");
+}  // namespace pair
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    w8a8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                             const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmO, const Params p) {
+  constexpr int BM = pair::BM, BN = pair::BN, STAGES = pair::STAGES;
+  constexpr int A_BYTES = pair::A_BYTES, B_BYTES = pair::B_BYTES, STAGE_BYTES = pair::STAGE_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_base);
+
+  const uint32_t stg_base = base + STAGES * STAGE_BYTES;  // output staging (1024-aligned)
+  const uint32_t bar_base = stg_base + STG_BYTES;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * STAGES + 4);
+  uint8_t* gbar = gbase + STAGES * STAGE_BYTES + STG_BYTES;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbar + 8 * (2 * STAGES + 5));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbar + 8 * (2 * STAGES + 5) + 4);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = ptx::cluster_ctarank();   // 0: issues the MMAs
+  const int pair_id = blockIdx.x / 2;
+  const int npairs = gridDim.x / 2;
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;  // pair tiles
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(tfull_bar(a), 1);
+      ptx::mbar_init(tempty_bar(a), 2 * 128);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)), TMEM_COLS);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before();
+  ptx::cluster_sync_all();  // barriers of both CTAs initialised before any remote traffic
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += npairs) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+            if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_PRODUCER, abort_flag, rank);
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * STAGE_BYTES;
+          const uint32_t sb = sa + A_BYTES;
+          const uint32_t fb = ptx::map_to_rank(full_bar(stage), 0);
+          if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+          ptx::tma_load_2d_pair(sa, &tmA, fb, kb * BK, mb * BM + (int)rank * 128);
+          if (p.b_kn)
+            ptx::tma_load_2d_pair(sb, &tmB, fb, nb * BN + (int)rank * 128, kb * BK);
+          else
+            ptx::tma_load_2d_pair(sb, &tmB, fb, kb * BK, nb * BN + (int)rank * 128);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: the even CTA's full barriers count both CTAs' copies.
+      if (rank == 0) {
+        for (long long f = (issued > STAGES ? issued - STAGES : 0); f < issued; ++f) {
+          if (!ptx::mbar_wait(full_bar((int)(f % STAGES)), (uint32_t)((f / STAGES) & 1), nullptr)) {
+            report_pair(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag, rank);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += npairs, ++it) {
+        const int a = it & 1;
+        const uint32_t aphase = (uint32_t)((it >> 1) & 1);
+        if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag)) {
+          if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_MMA, abort_flag, rank);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(a * BN);
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag)) {
+            if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_MMA, abort_flag, rank);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = base + stage * STAGE_BYTES;
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t adesc = ptx::smem_desc_sw128(sa + kk * UMMA_K, 16, 1024);
+            // B per CTA: 128 columns = one 128-byte swizzle row in either layout.
+            const uint64_t bdesc = p.b_kn ? ptx::smem_desc_sw128(sb + kk * UMMA_K * 128, B_BYTES, 1024)
+                                          : ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
+            ptx::umma_i8_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          ptx::umma_commit_pair(empty_bar(stage), 0x3);
+          issued_any = true;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) ptx::umma_commit_pair(tfull_bar(a), 0x3);
+      }
+      if (!ok && issued_any) {
+        ptx::umma_commit_pair(drain_bar, 0x1);
+        if (!ptx::mbar_wait(drain_bar, 0, nullptr)) report_pair(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag, rank);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int q = warp & 3;
+    const bool elected = (warp == 2 && lane == 0);
+    int chunk_seq = 0;
+    const uint32_t te_leader0 = ptx::map_to_rank(tempty_bar(0), 0);
+    const uint32_t te_leader1 = ptx::map_to_rank(tempty_bar(1), 0);
+    int it = 0;
+    for (int tile = pair_id; tile < num_tiles; tile += npairs, ++it) {
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const int a = it & 1;
+      const uint32_t aphase = (uint32_t)((it >> 1) & 1);
+      bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is .sync.aligned
+      if (!ok && lane == 0 && !*abort_flag)
+        report_pair(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag, rank);
+      ptx::tc_fence_after();
+      epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM + (int)rank * 128,
+                    nb * BN, stg_base, elected, chunk_seq, ok);
+      ptx::tc_fence_before();
+      ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
+    }
+    if (elected) ptx::bulk_wait_group_all();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync_all();  // the pair's MMAs and remote arrivals are finished
+  ptx::tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -378,19 +682,24 @@ qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B
                                  const float* sA, const float* sB, void* out, int out_dtype,
                                  int ldc, int M, int N, int K, int32_t* acc) {
   using namespace w8a8;
+  // CTA pairs (256 x 256 tiles) whenever the problem has at least one full pair tile.
+  const bool use_pair = M >= 256 && N >= 256 && s->dev->sm_count >= 2;
+  const int bm = use_pair ? pair::BM : BM, bn = use_pair ? pair::BN : BN;
   CUtensorMap tmA, tmB;
-  if (!make_map_u8(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)K, BK, BM))
+  if (!make_map_u8(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)K, BK, 128))
     return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for A [%d,%d]", M, K);
+  // B boxes: [K,N] -> 128 columns x 128 k-rows; [N,K] -> 128 k-bytes x (bn per CTA) rows.
+  const uint32_t nk_rows = use_pair ? 128 : BN;
   bool okb = b_kn ? make_map_u8(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)N, 128, BK)
-                  : make_map_u8(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK, BN);
+                  : make_map_u8(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK, nk_rows);
   if (!okb) return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for B");
 
   Params p;
   p.M = M; p.N = N; p.K = K; p.ldc = ldc;
   p.out_dtype = out_dtype;
   p.b_kn = b_kn;
-  p.num_m_blocks = (M + BM - 1) / BM;
-  p.num_n_blocks = (N + BN - 1) / BN;
+  p.num_m_blocks = (M + bm - 1) / bm;
+  p.num_n_blocks = (N + bn - 1) / bn;
   p.num_k_blocks = (K + BK - 1) / BK;
   p.num_tiles = p.num_m_blocks * p.num_n_blocks;
   p.sA = sA; p.sB = sB; p.out = out; p.acc = acc;
@@ -398,19 +707,47 @@ qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B
   const int esize = out_dtype == QGEMM_BF16 ? 2 : 4;
   p.out_vec = aligned((uint64_t)out, 16) && ((uint64_t)ldc * esize) % 16 == 0;
   p.acc_vec = acc != nullptr && aligned((uint64_t)acc, 16) && N % 4 == 0;
-
-  static bool attr_set[64] = {false};
-  const int ord = s->dev->ordinal;
-  if (ord >= 0 && ord < 64 && !attr_set[ord]) {
-    cudaError_t e = cudaFuncSetAttribute(w8a8_tcgen05_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8a8_tcgen05)");
-    attr_set[ord] = true;
+  // Output tensor map for TMA stores: [M rows, N columns] with row pitch ldc, boxes of
+  // 128 rows x 128 bytes, 128-byte swizzle (matching the staging buffer).
+  CUtensorMap tmO;
+  memset(&tmO, 0, sizeof(tmO));
+  p.tma_store = 0;
+  if (p.out_vec) {
+    EncodeTiledFn enc = get_encode_fn();
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)ldc * esize};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / esize), 128};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc && enc(&tmO, out_dtype == QGEMM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                   2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      p.tma_store = 1;
   }
-  const int grid = p.num_tiles < s->dev->sm_count ? p.num_tiles : s->dev->sm_count;
-  w8a8_tcgen05_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s->stream>>>(tmA, tmB, p);
+
+  static bool attr_set[64][2] = {};
+  const int ord = s->dev->ordinal;
+  if (ord >= 0 && ord < 64 && !attr_set[ord][use_pair]) {
+    cudaError_t e = use_pair
+        ? cudaFuncSetAttribute(w8a8_tcgen05_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               pair::SMEM_BYTES)
+        : cudaFuncSetAttribute(w8a8_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8a8_tcgen05)");
+    attr_set[ord][use_pair] = true;
+  }
+  if (use_pair) {
+    const int max_pairs = s->dev->sm_count / 2;
+    const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
+    w8a8_tcgen05_pair_kernel<<<2 * pairs, NUM_THREADS, pair::SMEM_BYTES, s->stream>>>(tmA, tmB, tmO,
+                                                                                     p);
+  } else {
+    const int grid = p.num_tiles < s->dev->sm_count ? p.num_tiles : s->dev->sm_count;
+    w8a8_tcgen05_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s->stream>>>(tmA, tmB, tmO, p);
+  }
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "w8a8_tcgen05_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "w8a8_tcgen05 launch");
   return QGEMM_OK;
 }
 

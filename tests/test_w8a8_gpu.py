@@ -71,6 +71,22 @@ def test_tcgen05_ragged_shapes(gpu, oracle, M, N, K, layout):
     check_exact(oracle, A, B, sA, sB, y, acc, qgemm.BF16)
 
 
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (512, 768, 4096), (1000, 1040, 272),
+                                   (4096, 256, 1024), (257, 4096, 512)])
+@pytest.mark.parametrize("layout", [qgemm.B_KN, qgemm.B_NK])
+def test_tcgen05_cta_pair_shapes(gpu, oracle, M, N, K, layout):
+    """Shapes with at least one full 256 x 256 tile run on CTA pairs (cta_group::2)."""
+    A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + 3 * N + 7 * K)
+    y, acc = run(gpu, A, B, sA, sB, layout=layout, algo=qgemm.ALGO_TCGEN05)
+    check_exact(oracle, A, B, sA, sB, y, acc, qgemm.BF16)
+
+
+def test_tcgen05_cta_pair_ldc_f32(gpu, oracle):
+    A, B, sA, sB = syn.w8a8_inputs(384, 512, 640, seed=17)
+    y, acc = run(gpu, A, B, sA, sB, out_dtype=qgemm.F32, ldc=520, algo=qgemm.ALGO_TCGEN05)
+    check_exact(oracle, A, B, sA, sB, y, acc, qgemm.F32)
+
+
 def test_tcgen05_extreme_values(gpu, oracle):
     """-128 * -128 everywhere: the largest int32 sums the operand range allows."""
     M, N, K = 128, 256, 8192
