@@ -37,10 +37,10 @@ for _p in (ROOT, PKG):
 
 METRIC = "W8A8 GEMM TOPS & W4A16 GEMV HBM GB/s at 1/2/4/8 B200, % of roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes per launch of w8a8_tcgen05 at 4096^3 from ncu (profiles/w8a8_tcgen05_4096.md);
-# None until a capture exists.
-NCU_TRAFFIC_W8A8_4096 = None
-NCU_TRAFFIC_W4A16_M1 = None
+# DRAM bytes (read + write) per launch from one `ncu --set full` capture of the same
+# kernel on the same workload (profiles/w8a8_tcgen05_pair_4096.md, profiles/w4a16_tile_m1.md).
+NCU_TRAFFIC_W8A8_4096 = 33626112 + 2321920
+NCU_TRAFFIC_W4A16_M1 = 30312704 + 256
 
 
 def parse_args():
@@ -53,6 +53,9 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large"], default="all",
                    help="run one workload alone (for profiling); prints its own JSON line")
+    p.add_argument("--profile", action="store_true",
+                   help="with --only w8a8|w4a16: warmup + steps plain launches and nothing "
+                        "else (no sustained clock window, no graphs), for ncu captures")
     return p.parse_args()
 
 
@@ -200,7 +203,7 @@ def timed(fn, steps, world):
     return max_over_ranks(local, world), local
 
 
-def w8a8_headline(ops, st, rank, world, steps, warmup, clocks):
+def w8a8_headline(ops, st, rank, world, steps, warmup, clocks, sustain=True):
     """M = K = 4096, 4096 weight columns per rank, 8 rotating input sets."""
     import torch
     import qgemm
@@ -226,7 +229,7 @@ def w8a8_headline(ops, st, rank, world, steps, warmup, clocks):
     with clocks:
         t0 = time.time()
         i = 0
-        while time.time() - t0 < 1.0:
+        while sustain and time.time() - t0 < 1.0:
             step(i)
             i += 1
             if i % 64 == 0:
@@ -240,35 +243,116 @@ def w8a8_headline(ops, st, rank, world, steps, warmup, clocks):
 
 
 def w8a8_e2e(ops, st, hb, rank, world, steps):
-    """The headline GEMM through the C-ABI with host buffers: per step H2D of the
-    activations A and per-token scales sA from pinned memory, the GEMM on the
-    resident weights, D2H of the bf16 output into pinned memory."""
+    """The headline GEMM through the C-ABI with host buffers.  Every step copies
+    that step's activations A and per-token scales sA from pinned host memory,
+    runs the GEMM on the resident weights and copies the bf16 output back to
+    pinned host memory.  Copies in, GEMMs and copies out run on three streams
+    with double-buffered device buffers, so step i's GEMM overlaps step i+1's
+    upload and step i-1's download (PCIe is full duplex)."""
     import torch
     import qgemm
     M, N, K = hb["M"], hb["N"], hb["K"]
-    hA = hb["A"][0].cpu().pin_memory()
-    hsA = hb["sA"][0].cpu().pin_memory()
-    hout = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-    dA = torch.empty_like(hb["A"][0])
-    dsA = torch.empty_like(hb["sA"][0])
-    dout = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    NB = 2
+    hA = [hb["A"][j].cpu().pin_memory() for j in range(NB)]
+    hsA = [hb["sA"][j].cpu().pin_memory() for j in range(NB)]
+    hout = [torch.empty((M, N), dtype=torch.bfloat16).pin_memory() for _ in range(NB)]
+    dA = [torch.empty_like(hb["A"][0]) for _ in range(NB)]
+    dsA = [torch.empty_like(hb["sA"][0]) for _ in range(NB)]
+    dout = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda") for _ in range(NB)]
     B, sB = hb["B"][0], hb["sB"][0]
+    s_in, s_mm, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    q_in, q_mm, q_out = (st.dev.wrap_stream(x.cuda_stream) for x in (s_in, s_mm, s_out))
+    mm_ops = type(ops)(q_mm)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    uploaded = [ev() for _ in range(NB)]
+    computed = [ev() for _ in range(NB)]
+    downloaded = [ev() for _ in range(NB)]
+    consumed = [ev() for _ in range(NB)]   # GEMM finished reading dA/dsA[j]
+    used = [False] * NB
 
     def step(i):
-        st.h2d_ptr(dA.data_ptr(), hA.data_ptr(), hA.numel())
-        st.h2d_ptr(dsA.data_ptr(), hsA.data_ptr(), hsA.numel() * 4)
-        ops.w8a8Gemm(dA, B, dsA, sB, dout, M, N, K, b_layout=qgemm.B_KN, out_dtype=qgemm.BF16,
-                     algo=qgemm.ALGO_TCGEN05)
-        st.d2h_ptr(hout.data_ptr(), dout.data_ptr(), M * N * 2)
+        j = i % NB
+        if used[j]:
+            s_in.wait_event(consumed[j])
+            s_mm.wait_event(downloaded[j])
+        q_in.h2d_ptr(dA[j].data_ptr(), hA[j].data_ptr(), hA[j].numel())
+        q_in.h2d_ptr(dsA[j].data_ptr(), hsA[j].data_ptr(), hsA[j].numel() * 4)
+        uploaded[j].record(s_in)
+        s_mm.wait_event(uploaded[j])
+        mm_ops.w8a8Gemm(dA[j], B, dsA[j], sB, dout[j], M, N, K, b_layout=qgemm.B_KN,
+                        out_dtype=qgemm.BF16, algo=qgemm.ALGO_TCGEN05)
+        computed[j].record(s_mm)
+        consumed[j].record(s_mm)
+        s_out.wait_event(computed[j])
+        q_out.d2h_ptr(hout[j].data_ptr(), dout[j].data_ptr(), M * N * 2)
+        downloaded[j].record(s_out)
+        used[j] = True
 
-    for i in range(3):
-        step(i)
+    def run(n):
+        cur = torch.cuda.current_stream()
+        for x in (s_in, s_mm, s_out):
+            x.wait_stream(cur)
+        for i in range(n):
+            step(i)
+        for x in (s_in, s_mm, s_out):
+            cur.wait_stream(x)
+
+    run(4)
     torch.cuda.synchronize()
-    t_max, _ = timed(step, steps, world)
+    t_max, _ = timed(lambda i: run(steps) if i == 0 else None, 1, world)
+    for q in (q_in, q_mm, q_out):
+        q.destroy()
     value = 2.0 * M * N * K * world * steps / t_max / 1e12
     return {"value": value, "unit": "TOPS", "h2d_bytes_per_step": M * K + M * 4,
             "d2h_bytes_per_step": M * N * 2, "ms_per_step": t_max / steps * 1e3,
+            "pipelining": "H2D / GEMM / D2H on three streams, double-buffered",
             "resident": "weights B [K,N] int8 and sB (loaded once, as model weights)"}
+
+
+def library_int8_context(hb, steps):
+    """cuBLASLt int8 GEMM (torch._int_mm: int32 output, no scales, no bf16
+    epilogue) on the same rotating inputs right after the timed region: context
+    for the headline, never part of it."""
+    import torch
+    try:
+        A, B = hb["A"], hb["B"]
+        R = len(A)
+        for i in range(3):
+            torch._int_mm(A[i % R], B[i % R])
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(steps):
+            torch._int_mm(A[i % R], B[i % R])
+        e.record()
+        torch.cuda.synchronize()
+        t = s.elapsed_time(e) / 1e3 / steps
+        return {"cublaslt_int_mm_TOPS": 2.0 * hb["M"] * hb["N"] * hb["K"] / t / 1e12,
+                "note": "int32 out, no dequant epilogue; same inputs, same box"}
+    except Exception as ex:  # context only
+        return {"cublaslt_int_mm_TOPS": None, "note": f"unavailable: {ex}"}
+
+
+def w4a16_profile(ops, steps, warmup):
+    """The M = 1 decode GEMV as warmup + steps plain launches (no graph), for ncu."""
+    import torch
+    N, K, G, R = 14336, 4096, 128, 8
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(77)
+    wq = []
+    for _ in range(R):
+        w0 = torch.randint(-2**31, 2**31 - 1, (K, N // 8), dtype=torch.int32, device="cuda",
+                           generator=gen)
+        wq.append(torch.empty(ops.w4TiledBytes(K, N), dtype=torch.uint8, device="cuda"))
+        ops.prepackW4Tiled(w0, wq[-1], K, N)
+    sc = [(torch.rand((K // G, N), device="cuda", generator=gen) * 0.015 + 0.005).to(torch.bfloat16)
+          for _ in range(R)]
+    x = torch.randn((1, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y = torch.empty((1, N), dtype=torch.bfloat16, device="cuda")
+    for i in range(warmup + steps):
+        ops.w4a16GemmGroupedTiled(x, wq[i % R], sc[i % R], y, 1, N, K, zero_point=8, group_size=G)
+    torch.cuda.synchronize()
+    return {"launches": warmup + steps, "M": 1, "N": N, "K": K}
 
 
 def w4a16_decode(ops, peaks):
@@ -282,7 +366,7 @@ def w4a16_decode(ops, peaks):
     gen.manual_seed(77)
     wq0 = [torch.randint(-2**31, 2**31 - 1, (K, N // 8), dtype=torch.int32, device="cuda",
                          generator=gen) for _ in range(R)]
-    # one-time prepack of the static weights into 256-column tiles (not timed)
+    # one-time prepack of the static weights into 64-column tiles (not timed)
     wq = [torch.empty(ops.w4TiledBytes(K, N), dtype=torch.uint8, device="cuda") for _ in range(R)]
     for a, b in zip(wq0, wq):
         ops.prepackW4Tiled(a, b, K, N)
@@ -406,27 +490,27 @@ def gather_output(st, out, rank, world, M, NL):
 
 def cpu_w8a8_sample(target_s: float = 10.0):
     """The CPU restatement of w8a32Gemm (oracle, OpenMP over all host threads)
-    on a bounded row sample of the 4096^3 workload."""
-    import numpy as np
+    on a bounded sample of the 4096^3 workload: a row slice, or the whole GEMM
+    repeated, sized to about target_s seconds."""
     import qgemm.synthetic as syn
     from oracle import oracle
     M = N = K = 4096
     A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=2, sa=(0.001, 0.01), sb=(0.0005, 0.005))
     threads = oracle.max_threads()
     t0 = time.perf_counter()
-    oracle.w8a8_gemm_rows(B, sB, A, sA, 0, 8, threads=threads, want_f32=False)
-    per_row = (time.perf_counter() - t0) / 8
-    rows = int(max(8, min(M, target_s / max(per_row, 1e-9))))
-    rows = max(threads, rows // threads * threads) if rows >= threads else rows
-    rows = min(rows, M)
+    oracle.w8a8_gemm_rows(B, sB, A, sA, 0, threads, threads=threads, want_f32=False)
+    per_row = (time.perf_counter() - t0) / threads
+    rows = int(max(threads, min(M, target_s / max(per_row, 1e-9))))
+    rows = min(M, max(threads, rows // threads * threads))
+    reps = 1 if rows < M else max(1, int(round(target_s / (per_row * M))))
     t0 = time.perf_counter()
-    oracle.w8a8_gemm_rows(B, sB, A, sA, 0, rows, threads=threads, want_f32=False)
+    for _ in range(reps):
+        oracle.w8a8_gemm_rows(B, sB, A, sA, 0, rows, threads=threads, want_f32=False)
     dt = time.perf_counter() - t0
-    _ = np
-    return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": "TOPS", "cores": threads,
+    what = (f"rows 0..{rows - 1} of" if rows < M else f"{reps} x the whole")
+    return {"value": 2.0 * rows * N * K * reps / dt / 1e12, "unit": "TOPS", "cores": threads,
             "kind": "port", "seconds": dt,
-            "sample": f"rows 0..{rows - 1} of the 4096^3 W8A8 GEMM (bf16 out), "
-                      f"{threads} OpenMP threads"}
+            "sample": f"{what} 4096^3 W8A8 GEMM (bf16 out), {threads} OpenMP threads"}
 
 
 def reference_arm(args):
@@ -488,7 +572,7 @@ def main():
 
     if args.only == "w4a16":
         log("w4a16 decode (only)")
-        r = w4a16_decode(ops, peaks)
+        r = w4a16_profile(ops, K, W) if args.profile else w4a16_decode(ops, peaks)
         if rank == 0:
             print(json.dumps({"only": "w4a16", "w4a16_decode": r}), flush=True)
         return 0
@@ -502,23 +586,29 @@ def main():
             dist.destroy_process_group()
         return 0
     log("w8a8 headline")
-    hb = w8a8_headline(ops, st, rank, world, K, W, clocks)
+    hb = w8a8_headline(ops, st, rank, world, K, W, clocks,
+                       sustain=not (args.profile and args.only == "w8a8"))
     if args.only == "w8a8":
         if rank == 0:
             print(json.dumps({"only": "w8a8", "TOPS": hb["value"],
                               "us_per_launch": hb["per_launch_s"] * 1e6}), flush=True)
         return 0
     int8_peak = 2.0 * peaks["bf16_tflops"]
+    int8_sustained = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     achieved = hb["ops_per_launch"] / hb["per_launch_s"] / 1e12
-    roofline = {"bound": "tensor", "kernel": "w8a8_tcgen05", "achieved": achieved,
+    roofline = {"bound": "tensor", "kernel": "w8a8_tcgen05_pair_kernel", "achieved": achieved,
                 "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
                 "traffic": NCU_TRAFFIC_W8A8_4096,
                 "algorithmic_ops_per_launch": hb["ops_per_launch"],
+                "algorithmic_bytes_per_launch": hb["M"] * hb["K"] + hb["K"] * hb["N"]
+                + 2 * hb["M"] * hb["N"] + 4 * (hb["M"] + hb["N"]),
                 "peak_basis": f"2 x bf16_tflops ({peak_src}, burst cuBLAS bf16): dense int8 "
-                              f"runs at twice the bf16 rate on B200"}
+                              f"runs at twice the bf16 rate on B200",
+                "frac_of_sustained_peak": achieved / int8_sustained}
+    libctx = library_int8_context(hb, K) if rank == 0 else None
     log("e2e")
     e2e = w8a8_e2e(ops, st, hb, rank, world, max(10, min(K, 50)))
-    extra = {}
+    extra = {"library_context": libctx} if libctx else {}
     if world == 1 and rank == 0:
         log("w4a16 decode")
         extra["w4a16_decode"] = w4a16_decode(ops, peaks)

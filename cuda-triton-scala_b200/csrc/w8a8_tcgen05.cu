@@ -6,14 +6,23 @@
 //     y[m,n]   = (float(acc) * sB[n]) * sA[m]      (fp32, two roundings, in order)
 // with y stored as fp32 or as bf16 (round to nearest even).
 //
-// Design (one persistent CTA per SM, 6 warps):
-//   warp 0      TMA producer: A tile [128 x 128 B] and B tile [256 x 128 B] per stage,
-//               128-byte swizzle, STAGES-deep ring of shared-memory buffers.
-//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma kind::i8
-//               (M=128, N=256, K=32) into one of two 256-column TMEM accumulators.
+// Two persistent kernels, 6 warps per CTA, one CTA per SM:
+//   w8a8_tcgen05_pair_kernel  (M >= 256 and N >= 256) CTA pairs of a 2-CTA cluster
+//       share one 256 x 256 output tile through tcgen05.mma.cta_group::2 (M=256,
+//       N=256, K=32): each CTA loads half of A (128 rows) and half of B (128
+//       columns) per stage, so per-SM shared-memory traffic per MMA is half that of
+//       a 1-CTA 128 x 256 tile.  6-stage ring of 32 KB stages.
+//   w8a8_tcgen05_kernel       1-CTA 128 x 256 tiles, 4-stage ring of 48 KB stages,
+//       for shapes with fewer than 256 rows or columns.
+// Warp roles in both:
+//   warp 0      TMA producer: 128-byte-swizzled tiles into the shared-memory ring.
+//   warp 1      allocates 512 TMEM columns (two 256-column accumulators); one
+//               thread issues tcgen05.mma kind::i8 (in a pair: the even CTA only).
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output
-//               row per thread), dequant with the two scales, global stores.  The
-//               two accumulators let the epilogue of tile i overlap the MMAs of i+1.
+//               row per thread), dequant with the two scales, 128-byte-swizzled
+//               staging in shared memory, TMA bulk tensor stores of the output.
+//               The two accumulators let the epilogue of tile i overlap the MMAs
+//               of tile i+1.
 // B is read either in the reference layout [K,N] (MN-major UMMA operand) or as
 // [N,K] (K-major).  Every barrier wait is bounded (ptx::mbar_wait); a wait that
 // runs out records an error code in the device error word and the CTA drains

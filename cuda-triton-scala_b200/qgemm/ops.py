@@ -88,7 +88,7 @@ class QuantizedGemmOps:
         return n.value
 
     def prepackW4Tiled(self, wq, dst, K: int, N: int):
-        """uint32 [K, N/8] reference-order int4 weights -> 256-column tiles (one time)."""
+        """uint32 [K, N/8] reference-order int4 weights -> 64-column tiles (one time)."""
         L.call("qgemm_prepack_w4_tiled", self._h, L.addr(wq), L.addr(dst), K, N)
 
     def prepackW8NK(self, src_kn, dst_nk, K: int, N: int):
