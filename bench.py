@@ -378,23 +378,24 @@ def w4a16_decode(ops, peaks):
         x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
         y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
         launches = 64
+        # one stream handle for warm-up and capture: its scratch is made by the
+        # first (uncaptured) call
+        cap = torch.cuda.Stream()
+        q = ops.stream.dev.wrap_stream(cap.cuda_stream)
+        o = type(ops)(q)
 
         def body():
-            # bind to whichever stream is current (the capture stream inside the graph)
-            o = type(ops)(ops.stream.dev.wrap_stream(torch.cuda.current_stream().cuda_stream))
             for i in range(launches):
                 o.w4a16GemmGroupedTiled(x, wq[i % R], sc[i % R], y, M, N, K, zero_point=8,
                                         group_size=G)
-            o.stream.destroy()
 
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
             body()  # warm-up outside capture (also sets kernel attributes)
-        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.current_stream().wait_stream(cap)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with torch.cuda.graph(g, stream=cap):
             body()
         for _ in range(3):
             g.replay()
@@ -413,6 +414,7 @@ def w4a16_decode(ops, peaks):
                         "frac_of_hbm": gbs / peaks["hbm_gbs"],
                         "tflops": 2.0 * M * N * K / per / 1e12}
         del g
+        q.destroy()
     _ = syn
     return res
 

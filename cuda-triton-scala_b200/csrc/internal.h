@@ -25,6 +25,10 @@ struct qgemm_stream_s {
   qgemm_device_s* dev = nullptr;
   cudaStream_t stream = nullptr;
   bool owned = false;
+  // Scratch of the split-tile reductions (W4A16 tiled path), allocated by the first
+  // call that needs it on this handle and zeroed then; kernels leave it zeroed.
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
 };
 
 namespace qg {
@@ -37,6 +41,10 @@ qgemm_status cuda_fail(cudaError_t e, const char* what);
 qgemm_status enter(qgemm_stream_t s);
 
 inline bool aligned(uint64_t p, uint64_t a) { return (p % a) == 0; }
+
+// The stream handle's scratch, at least `bytes` long and zero-filled when first
+// made.  Allocating is refused while the stream is being captured into a graph.
+qgemm_status stream_workspace(qgemm_stream_s* s, size_t bytes, void** out);
 
 // Error codes a kernel writes into qgemm_device_s::d_err.
 enum : int {

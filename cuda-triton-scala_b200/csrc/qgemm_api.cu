@@ -61,6 +61,44 @@ static qgemm_status need_align(uint64_t p, uint64_t a, const char* name) {
   return QGEMM_OK;
 }
 
+namespace qg {
+qgemm_status stream_workspace(qgemm_stream_s* s, size_t bytes, void** out) {
+  if (s->ws && s->ws_bytes >= bytes) {
+    *out = s->ws;
+    return QGEMM_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s->stream, &cs);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(QGEMM_ERR_UNSUPPORTED,
+                "this call needs the stream handle's scratch (%zu bytes), which is made by the "
+                "first such call on the handle: make one call before capturing the stream",
+                bytes);
+  if (s->ws) {
+    cudaStreamSynchronize(s->stream);
+    cudaFree(s->ws);
+    s->ws = nullptr;
+    s->ws_bytes = 0;
+  }
+  void* p = nullptr;
+  e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(QGEMM_ERR_OOM, "scratch allocation of %zu bytes failed", bytes);
+  }
+  e = cudaMemsetAsync(p, 0, bytes, s->stream);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "zeroing the scratch");
+  }
+  s->ws = p;
+  s->ws_bytes = bytes;
+  *out = p;
+  return QGEMM_OK;
+}
+}  // namespace qg
+
 extern "C" {
 
 const char* qgemm_last_error(void) { return g_last_error; }
@@ -188,13 +226,19 @@ qgemm_status qgemm_stream_wrap(qgemm_device_t d, void* cuda_stream, qgemm_stream
 
 qgemm_status qgemm_stream_destroy(qgemm_stream_t s) {
   if (!s) return fail(QGEMM_ERR_BAD_HANDLE, "null stream");
-  if (s->owned && s->dev && s->dev->open) {
+  if (s->dev && s->dev->open) {
     cudaSetDevice(s->dev->ordinal);
-    cudaStreamDestroy(s->stream);
+    if (s->ws) {
+      // kernels of this handle may still be using the scratch
+      cudaStreamSynchronize(s->stream);
+      cudaFree(s->ws);
+    }
+    if (s->owned) cudaStreamDestroy(s->stream);
   }
   delete s;
   return QGEMM_OK;
 }
+
 
 qgemm_status qgemm_stream_sync(qgemm_stream_t s) {
   QG_TRY(enter(s));
@@ -207,6 +251,8 @@ qgemm_status qgemm_stream_sync(qgemm_stream_t s) {
   if (err != DEVERR_NONE) {
     const int zero = 0;
     cudaMemcpyAsync(s->dev->d_err, &zero, sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    // a kernel that gave up may have left split-tile counters raised
+    if (s->ws) cudaMemsetAsync(s->ws, 0, s->ws_bytes, s->stream);
     cudaStreamSynchronize(s->stream);
     return fail(QGEMM_ERR_TIMEOUT, "a device-side wait ran out (code %d)", err);
   }
