@@ -62,6 +62,12 @@ qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B
 bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int b_kn,
                             uint64_t out, int out_dtype, int ldc, int M, int N, int K,
                             const char** why);
+// bf16 GEMM on the same tcgen05 kernels: out[M, ldc] (bf16, RNE) = A[M,K] * B[N,K]^T,
+// fp32 accumulation.  A and B bf16, K-major; K % 8 == 0; 16-byte aligned A and B.
+// a_repeat = r > 1: B rows hold r blocks of K values, each padded with zeros to a
+// multiple of 64, and out = sum_i A * B_i^T.
+qgemm_status launch_bf16_gemm_nk(qgemm_stream_s* s, const void* A, const void* B, void* out,
+                                 int ldc, int M, int N, int K, int a_repeat = 1);
 qgemm_status launch_w8a8_simt(qgemm_stream_s* s, const int8_t* A, const int8_t* B, int b_kn,
                               const float* sA, const float* sB, void* out, int out_dtype,
                               int ldc, int M, int N, int K, int32_t* acc);
@@ -85,6 +91,10 @@ qgemm_status launch_w4a16_tile(qgemm_stream_s* s, const void* x, const uint8_t* 
 size_t w4_tiled_bytes(int K, int N);
 qgemm_status launch_prepack_w4_tiled(qgemm_stream_s* s, const uint32_t* src, uint8_t* dst, int K,
                                      int N);
+size_t w4a16_prefill_workspace_bytes(int K, int N);
+qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
+                                  const void* scales, int zp, int G, void* y, int M, int N,
+                                  int K, void* ws, size_t ws_bytes);
 qgemm_status launch_w4a16_grouped(qgemm_stream_s* s, const void* x, const uint32_t* wq,
                                   const void* scales, int zp, int group, void* y, int M,
                                   int N, int K);

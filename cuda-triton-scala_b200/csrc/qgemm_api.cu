@@ -443,6 +443,56 @@ qgemm_status qgemm_w4a16_grouped_gemm_tiled(qgemm_stream_t s, uint64_t x, uint64
                           reinterpret_cast<void*>(y), M, N, K);
 }
 
+qgemm_status qgemm_w4a16_prefill_workspace_bytes(int K, int N, size_t* bytes) {
+  if (!bytes) return fail(QGEMM_ERR_INVALID_ARG, "bytes is null");
+  if (K < 0 || N < 0) return fail(QGEMM_ERR_INVALID_ARG, "negative size K=%d N=%d", K, N);
+  *bytes = w4a16_prefill_workspace_bytes(K, N);
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint64_t wt,
+                                              uint64_t scales, int zero_point, int group_size,
+                                              uint64_t y, int M, int N, int K, uint64_t workspace,
+                                              size_t workspace_bytes) {
+  QG_TRY(enter(s));
+  QG_TRY(check_dims(M, N, K));
+  if (group_size <= 0) return fail(QGEMM_ERR_INVALID_ARG, "group_size %d <= 0", group_size);
+  if (zero_point < 0 || zero_point > 15)
+    return fail(QGEMM_ERR_INVALID_ARG, "zero_point %d outside [0,15]", zero_point);
+  if (N % 8 != 0) return fail(QGEMM_ERR_INVALID_ARG, "N %d is not a multiple of 8", N);
+  if (K % group_size != 0)
+    return fail(QGEMM_ERR_INVALID_ARG, "K %d is not a multiple of group_size %d", K, group_size);
+  if (M == 0 || N == 0) return QGEMM_OK;
+  if (K == 0) return fail(QGEMM_ERR_UNSUPPORTED, "K == 0 on the prefill path");
+  if (K % 8 != 0) return fail(QGEMM_ERR_UNSUPPORTED, "K %d is not a multiple of 8", K);
+  if (!s->dev->tcgen05) return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
+  QG_TRY(need(x, "x")); QG_TRY(need(wt, "wt")); QG_TRY(need(scales, "scales"));
+  QG_TRY(need(y, "y")); QG_TRY(need(workspace, "workspace"));
+  QG_TRY(need_align(x, 16, "x")); QG_TRY(need_align(wt, 16, "wt"));
+  QG_TRY(need_align(scales, 2, "scales")); QG_TRY(need_align(y, 16, "y"));
+  QG_TRY(need_align(workspace, 16, "workspace"));
+  return launch_w4a16_prefill(s, reinterpret_cast<const void*>(x),
+                              reinterpret_cast<const uint8_t*>(wt),
+                              reinterpret_cast<const void*>(scales), zero_point, group_size,
+                              reinterpret_cast<void*>(y), M, N, K,
+                              reinterpret_cast<void*>(workspace), workspace_bytes);
+}
+
+qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t out, int ldc,
+                                int M, int N, int K) {
+  QG_TRY(enter(s));
+  QG_TRY(check_dims(M, N, K));
+  if (ldc < N) return fail(QGEMM_ERR_INVALID_ARG, "ldc %d < N %d", ldc, N);
+  if (M == 0 || N == 0) return QGEMM_OK;
+  if (K == 0 || K % 8 != 0) return fail(QGEMM_ERR_UNSUPPORTED, "K %d is not a positive multiple of 8", K);
+  if (ldc % 8 != 0) return fail(QGEMM_ERR_UNSUPPORTED, "ldc %d is not a multiple of 8", ldc);
+  if (!s->dev->tcgen05) return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
+  QG_TRY(need(A, "A")); QG_TRY(need(B, "B")); QG_TRY(need(out, "out"));
+  QG_TRY(need_align(A, 16, "A")); QG_TRY(need_align(B, 16, "B")); QG_TRY(need_align(out, 16, "out"));
+  return launch_bf16_gemm_nk(s, reinterpret_cast<const void*>(A), reinterpret_cast<const void*>(B),
+                             reinterpret_cast<void*>(out), ldc, M, N, K);
+}
+
 // ---- W8A16 ----
 
 qgemm_status qgemm_w8a16_gemm(qgemm_stream_t s, uint64_t wInt8, uint64_t scalesW, uint64_t x,

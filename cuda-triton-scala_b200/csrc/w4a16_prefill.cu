@@ -1,0 +1,127 @@
+// w4a16_prefill.cu -- group-wise W4A16 GEMM for prefill-sized M.
+//
+// Arithmetic (QuantizedGemmOps.scala:229-245 generalised to groups and a zero point):
+//     y[m,n] = sum_k x[m,k] * w[k,n],   w[k,n] = (q[k,n] - zp) * s[k/G, n]
+//
+// When M is large every weight is used by many rows, so the weights are expanded once
+// per call instead of once per output tile: a slab of columns is dequantised into a
+// bf16 buffer (K-major, the B operand layout of the tensor-core GEMM), then the bf16
+// tcgen05 GEMM (the kernels of w8a8_tcgen05.cu in bf16 mode) multiplies the
+// activations by it, and the next slab follows.
+//
+// Exactness: w = (q - zp) * s has up to 12 significant bits (a 4-bit integer times an
+// 8-bit bf16 significand), more than bf16 holds.  Each weight is therefore written as
+// two bf16 values, hi = bf16(w) and lo = w - hi (exact: at most 4 bits remain), in two
+// K-blocks of the same slab row, and the GEMM reads the activations twice along K:
+//     y = x * hi^T + x * lo^T,  with exact products and fp32 sums,
+// so the only roundings are those of the fp32 accumulation and of the bf16 output,
+// as on the decode path.  This doubles the tensor work; the expansion itself costs
+// 4.5 bytes of HBM traffic per weight against 4 * M multiply-adds.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "internal.h"
+
+namespace qg {
+namespace w4p {
+
+constexpr int TW = 64;    // columns per tile of the tiled int4 layout
+constexpr int TWB = 32;   // bytes of a tile row
+constexpr int KR = 128;   // weight rows per CTA
+constexpr int PAD = 8;    // bf16 padding per transposed row (keeps rows 16-byte aligned)
+
+// One CTA: one 64-column tile x 128 rows of the tiled weights -> rows n of the slab,
+// dst[n - n0][k] = hi and dst[n - n0][Kp + k] = lo (bf16, row pitch 2 * Kp, Kp = K
+// rounded up to 64, zeros in between).  Thread t dequantises half a row (32 columns,
+// one 16-byte load) into two transposed shared tiles; then each warp writes eight
+// slab rows, 256 bytes of hi and 256 bytes of lo each.
+__global__ void __launch_bounds__(256) dequant_slab_kernel(
+    const uint8_t* __restrict__ wt, const __nv_bfloat16* __restrict__ scales, int zp, int G,
+    __nv_bfloat16* __restrict__ dst, int K, int Kp, int N, int n0, int ncols) {
+  __shared__ __align__(16) __nv_bfloat16 tr[2][TW][KR + PAD];  // 34.8 KB
+  const int tile = n0 / TW + blockIdx.x;
+  const int k0 = blockIdx.y * KR;
+  const int r = threadIdx.x & (KR - 1), half = threadIdx.x >> 7;
+  const int k = k0 + r;
+  if (k < K) {
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(wt + ((size_t)tile * K + k) * TWB) + half);
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    const __nv_bfloat16* srow = scales + (size_t)(k / G) * N + tile * TW + 32 * half;
+    const float fzp = (float)zp;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {       // word j holds columns 8j .. 8j+7 of this half
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = 32 * half + 8 * j + e;
+        float v = 0.f;
+        if (tile * TW + c < N) {
+          const float q = (float)((wv[j] >> (4 * e)) & 0xFu);
+          v = (q - fzp) * __bfloat162float(srow[8 * j + e]);  // exact in fp32
+        }
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        tr[0][c][r] = hi;
+        tr[1][c][r] = __float2bfloat16_rn(v - __bfloat162float(hi));  // exact
+      }
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = lane >> 4;                  // lanes 0-15 write hi, 16-31 write lo
+  const int kk = 8 * (lane & 15);           // this lane's 8 elements (16 bytes)
+#pragma unroll
+  for (int i = 0; i < TW / 8; ++i) {
+    const int c = warp * (TW / 8) + i;
+    const int n = tile * TW + c - n0;       // slab row
+    if (n >= ncols || k0 + kk >= Kp) continue;  // Kp % 64 == 0: whole 16-byte pieces
+    __nv_bfloat16* drow = dst + (size_t)n * 2 * Kp + (size_t)h * Kp + k0 + kk;
+    if (k0 + kk + 8 <= K) {
+      *reinterpret_cast<uint4*>(drow) = *reinterpret_cast<const uint4*>(&tr[h][c][kk]);
+    } else {  // the tail of K and the zero padding up to Kp
+      for (int e = 0; e < 8; ++e)
+        drow[e] = (k0 + kk + e < K) ? tr[h][c][kk + e] : __float2bfloat16_rn(0.f);
+    }
+  }
+}
+
+}  // namespace w4p
+
+static size_t padded_k(int K) { return ((size_t)K + 63) / 64 * 64; }
+
+size_t w4a16_prefill_workspace_bytes(int K, int N) {
+  const size_t ncols = ((size_t)N + 255) / 256 * 256;
+  return ncols * padded_k(K) * 4;  // hi and lo per weight
+}
+
+qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
+                                  const void* scales, int zp, int G, void* y, int M, int N,
+                                  int K, void* ws, size_t ws_bytes) {
+  using namespace w4p;
+  // slab width: as many columns as the workspace holds, a multiple of 256 (so that
+  // every slab but the last fills whole 256-column GEMM tiles)
+  const size_t Kp = padded_k(K);
+  const size_t row_bytes = Kp * 4;  // hi and lo
+  size_t cols = ws_bytes / row_bytes;
+  cols = cols / 256 * 256;
+  if (cols == 0) {
+    if ((size_t)N * row_bytes <= ws_bytes) cols = (size_t)N;
+    else return fail(QGEMM_ERR_INVALID_ARG,
+                     "workspace of %zu bytes is smaller than one 256-column slab (%zu bytes)",
+                     ws_bytes, (size_t)256 * row_bytes);
+  }
+  __nv_bfloat16* slab = static_cast<__nv_bfloat16*>(ws);
+  for (size_t n0 = 0; n0 < (size_t)N; n0 += cols) {
+    const int ncols = (int)(((size_t)N - n0) < cols ? ((size_t)N - n0) : cols);
+    dim3 grid2((ncols + TW - 1) / TW, (unsigned)((Kp + KR - 1) / KR));
+    dequant_slab_kernel<<<grid2, 256, 0, s->stream>>>(
+        wt, static_cast<const __nv_bfloat16*>(scales), zp, G, slab, K, (int)Kp, N, (int)n0,
+        ncols);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "dequant_slab launch");
+    const qgemm_status st = launch_bf16_gemm_nk(
+        s, x, slab, static_cast<__nv_bfloat16*>(y) + n0, N, M, ncols, K, 2);
+    if (st != QGEMM_OK) return st;
+  }
+  return QGEMM_OK;
+}
+
+}  // namespace qg

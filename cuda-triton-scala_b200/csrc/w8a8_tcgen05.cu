@@ -77,6 +77,10 @@ struct Params {
   int out_vec;     // out base 16-byte aligned and rows a multiple of 16 bytes
   int acc_vec;     // same for the int32 accumulator output
   int tma_store;   // the output is written with TMA bulk tensor stores (needs out_vec)
+  int bf16;        // 1: A and B are bf16 (K counted in bytes), fp32 accumulators written
+                   // as they are (no scales, no int32 output)
+  int a_kblocks;   // k-block b of A is read at b % a_kblocks (A repeated along K);
+                   // equal to num_k_blocks for an ordinary product
 };
 
 
@@ -110,7 +114,10 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
   if (row >= p.M || n0 >= p.N) return;
   const bool full = (n0 + 32 <= p.N);
   float sb[32];
-  if (full && ((reinterpret_cast<uintptr_t>(p.sB + n0) & 15) == 0)) {
+  if (p.bf16) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sb[j] = 1.f;
+  } else if (full && ((reinterpret_cast<uintptr_t>(p.sB + n0) & 15) == 0)) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       const float4 v = __ldg(reinterpret_cast<const float4*>(p.sB + n0 + j));
@@ -134,7 +141,8 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j)
-    v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
+    v[j] = p.bf16 ? __uint_as_float(r[j])
+                  : __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
   if (p.out_dtype == QGEMM_BF16) {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldc + n0;
     if (full && p.out_vec) {
@@ -179,7 +187,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
                                               bool elected, int& chunk_seq, bool ok) {
   const int row = row0 + q * 32 + lane;
   const int rl = q * 32 + lane;  // row within the staging block
-  const float sa = (row < p.M) ? __ldg(p.sA + row) : 0.f;
+  const float sa = (!p.bf16 && row < p.M) ? __ldg(p.sA + row) : 0.f;
   if (!p.tma_store) {
 #pragma unroll 1
     for (int c = 0; c < 256 / 32; ++c) {
@@ -214,7 +222,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         for (int j = 0; j < 32; ++j) r[j] = 0u;  // a wait ran out: keep the barrier sequence
       }
       float sb[32];
-      if (nc + 32 <= p.N && ((reinterpret_cast<uintptr_t>(p.sB + nc) & 15) == 0)) {
+      if (p.bf16) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sb[j] = 1.f;
+      } else if (nc + 32 <= p.N && ((reinterpret_cast<uintptr_t>(p.sB + nc) & 15) == 0)) {
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 v = __ldg(reinterpret_cast<const float4*>(p.sB + nc + j));
@@ -231,7 +242,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
+        v[j] = p.bf16 ? __uint_as_float(r[j])
+                      : __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
       if (bf16) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {  // four 16-byte pieces = 32 bf16
@@ -329,7 +341,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t sa = base + stage * STAGE_BYTES;
           const uint32_t sb = sa + A_BYTES;
           ptx::mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
-          ptx::tma_load_2d(sa, &tmA, full_bar(stage), kb * BK, mb * BM);
+          ptx::tma_load_2d(sa, &tmA, full_bar(stage), (kb % p.a_kblocks) * BK, mb * BM);
           if (p.b_kn) {
             ptx::tma_load_2d(sb, &tmB, full_bar(stage), nb * BN, kb * BK);
             ptx::tma_load_2d(sb + B_BYTES / 2, &tmB, full_bar(stage), nb * BN + 128, kb * BK);
@@ -353,7 +365,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc = p.bf16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -391,7 +403,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             } else {
               bdesc = ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
             }
-            ptx::umma_i8(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if (p.bf16)
+              ptx::umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              ptx::umma_i8(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           ptx::umma_commit(empty_bar(stage));
           issued_any = true;
@@ -534,7 +549,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t sb = sa + A_BYTES;
           const uint32_t fb = ptx::map_to_rank(full_bar(stage), 0);
           if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
-          ptx::tma_load_2d_pair(sa, &tmA, fb, kb * BK, mb * BM + (int)rank * 128);
+          ptx::tma_load_2d_pair(sa, &tmA, fb, (kb % p.a_kblocks) * BK, mb * BM + (int)rank * 128);
           if (p.b_kn)
             ptx::tma_load_2d_pair(sb, &tmB, fb, nb * BN + (int)rank * 128, kb * BK);
           else
@@ -556,7 +571,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA) ----------------
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc = p.bf16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -587,7 +602,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             // B per CTA: 128 columns = one 128-byte swizzle row in either layout.
             const uint64_t bdesc = p.b_kn ? ptx::smem_desc_sw128(sb + kk * UMMA_K * 128, B_BYTES, 1024)
                                           : ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
-            ptx::umma_i8_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if (p.bf16)
+              ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              ptx::umma_i8_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           ptx::umma_commit_pair(empty_bar(stage), 0x3);
           issued_any = true;
@@ -687,9 +705,14 @@ bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int
   return true;
 }
 
-qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
-                                 const float* sA, const float* sB, void* out, int out_dtype,
-                                 int ldc, int M, int N, int K, int32_t* acc) {
+// The tcgen05 GEMM behind both the W8A8 and the bf16 entry points.  K is in bytes of
+// a row of A (and of B in the [N,K] layout): int8 elements, or twice the bf16 count.
+// With a_repeat = r > 1, each row of B holds r blocks of ceil(K / 128) * 128 bytes
+// (zero past K) and A is read r times along K: out = sum_i A * B_i^T.
+static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, const void* B,
+                                   int b_kn, const float* sA, const float* sB, void* out,
+                                   int out_dtype, int ldc, int M, int N, int K, int32_t* acc,
+                                   int a_repeat = 1) {
   using namespace w8a8;
   // CTA pairs (256 x 256 tiles) whenever the problem has at least one full pair tile.
   const bool use_pair = M >= 256 && N >= 256 && s->dev->sm_count >= 2;
@@ -699,8 +722,12 @@ qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B
     return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for A [%d,%d]", M, K);
   // B boxes: [K,N] -> 128 columns x 128 k-rows; [N,K] -> 128 k-bytes x (bn per CTA) rows.
   const uint32_t nk_rows = use_pair ? 128 : BN;
+  // B row length in bytes: with A repeated, each of the a_repeat blocks of a B row is
+  // padded to whole k-blocks so that block i starts at k-block i * ceil(K / BK)
+  const uint64_t kblk = (uint64_t)((K + BK - 1) / BK);
+  const uint64_t kb_bytes = a_repeat > 1 ? kblk * BK * a_repeat : (uint64_t)K;
   bool okb = b_kn ? make_map_u8(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)N, 128, BK)
-                  : make_map_u8(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK, nk_rows);
+                  : make_map_u8(&tmB, B, kb_bytes, (uint64_t)N, kb_bytes, BK, nk_rows);
   if (!okb) return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for B");
 
   Params p;
@@ -709,9 +736,11 @@ qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B
   p.b_kn = b_kn;
   p.num_m_blocks = (M + bm - 1) / bm;
   p.num_n_blocks = (N + bn - 1) / bn;
-  p.num_k_blocks = (K + BK - 1) / BK;
+  p.a_kblocks = (K + BK - 1) / BK;
+  p.num_k_blocks = p.a_kblocks * a_repeat;
   p.num_tiles = p.num_m_blocks * p.num_n_blocks;
   p.sA = sA; p.sB = sB; p.out = out; p.acc = acc;
+  p.bf16 = bf16;
   p.err = s->dev->d_err;
   const int esize = out_dtype == QGEMM_BF16 ? 2 : 4;
   p.out_vec = aligned((uint64_t)out, 16) && ((uint64_t)ldc * esize) % 16 == 0;
@@ -758,6 +787,18 @@ qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "w8a8_tcgen05 launch");
   return QGEMM_OK;
+}
+
+qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
+                                 const float* sA, const float* sB, void* out, int out_dtype,
+                                 int ldc, int M, int N, int K, int32_t* acc) {
+  return launch_tc_gemm(s, 0, A, B, b_kn, sA, sB, out, out_dtype, ldc, M, N, K, acc);
+}
+
+qgemm_status launch_bf16_gemm_nk(qgemm_stream_s* s, const void* A, const void* B, void* out,
+                                 int ldc, int M, int N, int K, int a_repeat) {
+  return launch_tc_gemm(s, 1, A, B, 0, nullptr, nullptr, out, QGEMM_BF16, ldc, M, N, 2 * K,
+                        nullptr, a_repeat);
 }
 
 }  // namespace qg

@@ -82,6 +82,26 @@ class QuantizedGemmOps:
                zero_point, group_size, L.addr(y), M, N, K)
 
     @staticmethod
+    def w4PrefillWorkspaceBytes(K: int, N: int) -> int:
+        n = ctypes.c_size_t(0)
+        L.call("qgemm_w4a16_prefill_workspace_bytes", K, N, ctypes.byref(n))
+        return n.value
+
+    def w4a16GemmGroupedPrefill(self, x, wt, scales, y, M: int, N: int, K: int, workspace,
+                                workspace_bytes: int, *, zero_point: int = 8,
+                                group_size: int = 128):
+        """Group-wise W4A16 for prefill-sized M on prepackW4Tiled weights: bf16 slabs
+        expanded in `workspace`, then the tensor-core bf16 GEMM."""
+        L.call("qgemm_w4a16_grouped_gemm_prefill", self._h, L.addr(x), L.addr(wt),
+               L.addr(scales), zero_point, group_size, L.addr(y), M, N, K, L.addr(workspace),
+               workspace_bytes)
+
+    def gemmBf16NK(self, A, B, out, M: int, N: int, K: int, *, ldc: int | None = None):
+        """out[M, ldc] bf16 = A[M,K] (bf16) x B[N,K]^T (bf16), fp32 sums."""
+        L.call("qgemm_gemm_bf16_nk", self._h, L.addr(A), L.addr(B), L.addr(out),
+               N if ldc is None else ldc, M, N, K)
+
+    @staticmethod
     def w4TiledBytes(K: int, N: int) -> int:
         n = ctypes.c_size_t(0)
         L.call("qgemm_w4_tiled_bytes", K, N, ctypes.byref(n))

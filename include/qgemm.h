@@ -195,6 +195,29 @@ QGEMM_API qgemm_status qgemm_w4_tiled_bytes(int K, int N, size_t* bytes);
 QGEMM_API qgemm_status qgemm_prepack_w4_tiled(qgemm_stream_t s, uint64_t wq, uint64_t dst, int K,
                                               int N);
 
+/* Group-wise W4A16 GEMM for prefill-sized M (the same arithmetic as
+ * qgemm_w4a16_grouped_gemm on the same prepacked weights `wt`): the weights are
+ * expanded slab by slab into the caller's workspace as bf16 (q - zero_point) *
+ * scale, rounded once, and multiplied on the tensor cores with fp32 sums.  Any M;
+ * meant for M in the hundreds and above, where the expansion is a few percent of
+ * the call.  workspace: 16-byte aligned, at least 512 * K bytes (one 256-column
+ * slab); qgemm_w4a16_prefill_workspace_bytes gives the size that holds all of N in
+ * one slab.  Requires sm_100, K % 8 == 0, K % group_size == 0, N % 8 == 0 and
+ * 16-byte aligned x, wt, scales, y.  Deterministic. */
+QGEMM_API qgemm_status qgemm_w4a16_prefill_workspace_bytes(int K, int N, size_t* bytes);
+QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint64_t wt,
+                                                        uint64_t scales, int zero_point,
+                                                        int group_size, uint64_t y, int M, int N,
+                                                        int K, uint64_t workspace,
+                                                        size_t workspace_bytes);
+
+/* bf16 GEMM on the tcgen05 kernels (no counterpart among the reference's quantized
+ * operators; it is the multiply of the W4A16 prefill path):
+ *   out[M, ldc] (bf16, RNE) = A[M,K] * B[N,K]^T with fp32 sums; A, B bf16 K-major.
+ * Requires sm_100, K % 8 == 0, ldc >= N, ldc % 8 == 0, 16-byte aligned A, B, out. */
+QGEMM_API qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t out,
+                                          int ldc, int M, int N, int K);
+
 /* One-time weight repack: int8 [K,N] (reference layout) -> [N,K] (K-major). */
 QGEMM_API qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src_kn, uint64_t dst_nk,
                                  int K, int N);
