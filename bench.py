@@ -51,7 +51,8 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-large", action="store_true", help="skip the sharded large GEMM")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large"], default="all",
+    p.add_argument("--no-llama", action="store_true", help="skip the Llama-shaped W4A16 stack")
+    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large", "llama"], default="all",
                    help="run one workload alone (for profiling); prints its own JSON line")
     p.add_argument("--profile", action="store_true",
                    help="with --only w8a8|w4a16: warmup + steps plain launches and nothing "
@@ -419,6 +420,110 @@ def w4a16_decode(ops, peaks):
     return res
 
 
+LLAMA_LINEARS = (("qkv", 4096, 12288), ("o", 4096, 4096), ("gate_up", 4096, 22016),
+                 ("down", 11008, 4096))
+
+
+def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
+    """Quantized linear stack of a Llama-2-7B-shaped decoder: `layers` x {qkv
+    4096->12288, o 4096->4096, gate+up 4096->22016, down 11008->4096}, random-init
+    int4 group-128 weights (zero point 8, bf16 scales ~U[0.005, 0.02]), bf16
+    activations ~N(0,1).  Prefill: batch x seq = 32 x 512 = 16384 rows through the
+    prefill path; decode: 32 rows through the decode kernel (one CUDA graph per step).
+    One step = every linear of every layer once."""
+    import torch
+    G = 128
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2024)
+    W = []  # (name, K, N, tiled weights, scales)
+    for _ in range(layers):
+        for name, K, N in LLAMA_LINEARS:
+            q = torch.randint(-2**31, 2**31 - 1, (K, N // 8), dtype=torch.int32, device="cuda",
+                              generator=gen)
+            wt = torch.empty(ops.w4TiledBytes(K, N), dtype=torch.uint8, device="cuda")
+            ops.prepackW4Tiled(q, wt, K, N)
+            sc = (torch.rand((K // G, N), device="cuda", generator=gen) * 0.015 + 0.005).to(
+                torch.bfloat16)
+            W.append((name, K, N, wt, sc))
+            del q
+    torch.cuda.synchronize()
+    weights_bytes = sum(K * N // 2 + (K // G) * N * 2 for _, K, N, _, _ in W)
+    flops_per_row = sum(2.0 * K * N for _, K, N, _, _ in W)
+    res = {"layers": layers, "group_size": G, "weight_bytes": weights_bytes}
+
+    # ---- prefill ----
+    M = 16384
+    xs = {K: torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+          for K in (4096, 11008)}
+    ys = {N: torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+          for N in (12288, 4096, 22016)}
+    ws_bytes = max(ops.w4PrefillWorkspaceBytes(K, N) for _, K, N in LLAMA_LINEARS)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+
+    def prefill_step():
+        for _, K, N, wt, sc in W:
+            ops.w4a16GemmGroupedPrefill(xs[K], wt, sc, ys[N], M, N, K, ws, ws_bytes,
+                                        zero_point=8, group_size=G)
+
+    prefill_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(prefill_steps):
+        prefill_step()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / prefill_steps
+    flops = flops_per_row * M
+    res["prefill"] = {"M": M, "ms_per_step": t * 1e3, "TFLOPs": flops / t / 1e12,
+                      "algorithmic_flop_per_step": flops,
+                      "frac_of_bf16_peak": flops / t / 1e12 / peaks["bf16_tflops"],
+                      "tensor_work_factor": 2,
+                      "note": "exact weights: each int4 weight is expanded to two bf16 terms "
+                              "(hi + lo), so the tensor cores do twice the algorithmic work"}
+    del xs, ys, ws
+    torch.cuda.empty_cache()
+
+    # ---- decode (one graph per step) ----
+    M = 32
+    xd = {K: torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+          for K in (4096, 11008)}
+    yd = {N: torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+          for N in (12288, 4096, 22016)}
+    cap = torch.cuda.Stream()
+    q = ops.stream.dev.wrap_stream(cap.cuda_stream)
+    o = type(ops)(q)
+
+    def decode_step():
+        for _, K, N, wt, sc in W:
+            o.w4a16GemmGroupedTiled(xd[K], wt, sc, yd[N], M, N, K, zero_point=8, group_size=G)
+
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        decode_step()
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=cap):
+        decode_step()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(decode_steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / decode_steps
+    bytes_step = weights_bytes + sum(M * K * 2 + M * N * 2 for _, K, N, _, _ in W)
+    res["decode"] = {"M": M, "ms_per_step": t * 1e3, "GB_s": bytes_step / t / 1e9,
+                     "frac_of_hbm": bytes_step / t / 1e9 / peaks["hbm_gbs"],
+                     "bytes_per_step": bytes_step}
+    del g
+    q.destroy()
+    return res
+
+
 def w8a8_large(ops, st, rank, world, steps, warmup):
     """M=16384, N=28672, K=8192, column-sharded (strong scaling) + optional gather."""
     import torch
@@ -578,6 +683,12 @@ def main():
         if rank == 0:
             print(json.dumps({"only": "w4a16", "w4a16_decode": r}), flush=True)
         return 0
+    if args.only == "llama":
+        log("llama stack (only)")
+        r = llama_stack(ops, peaks)
+        if rank == 0:
+            print(json.dumps({"only": "llama", "llama2_7b_w4a16_stack": r}), flush=True)
+        return 0
     if args.only == "large":
         log("w8a8 large (only)")
         r = w8a8_large(ops, st, rank, world, K, W)
@@ -620,6 +731,10 @@ def main():
     for k in ("A", "B", "sA", "sB"):
         hb.pop(k)
     torch.cuda.empty_cache()
+    if world == 1 and rank == 0 and not args.no_llama:
+        log("llama stack")
+        extra["llama2_7b_w4a16_stack"] = llama_stack(ops, peaks)
+        torch.cuda.empty_cache()
     if not args.no_large:
         log("w8a8 large")
         extra["w8a8_large"] = w8a8_large(ops, st, rank, world, 10, 3)

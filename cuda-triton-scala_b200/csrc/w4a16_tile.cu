@@ -64,7 +64,8 @@ struct Params {
   int M, N, K, G, zp;
   int m0, mrows;      // activation rows of this pass
   int KS;             // k-split (cluster size)
-  int kc;             // weight rows per CTA (= K / KS, a multiple of SR)
+  int kc;             // weight rows per CTA (a multiple of SR; the last CTA's share may
+                      // run past K)
   int pdl;
   const uint8_t* wt;  // tiled weights
   __nv_bfloat16* y;
@@ -131,7 +132,8 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int ks = blockIdx.x;          // k-split index == rank in the cluster
   const int tile = blockIdx.y;
   const int kbeg = ks * p.kc;
-  const int nstages = p.kc / SR;
+  const int krows = (p.K - kbeg) < p.kc ? (p.K - kbeg) : p.kc;  // rows of K this CTA owns
+  const int nstages = krows > 0 ? (krows + SR - 1) / SR : 0;
   const int gpr = SR / p.G > 0 ? SR / p.G : 1;  // scale rows per stage
 
   if (threadIdx.x == 0) {
@@ -145,7 +147,14 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
   __syncthreads();
 
-  const uint32_t tx_bytes = (uint32_t)(W_BYTES + gpr * TW * 2 + 2 * (SR / 2) * MR * 2);
+  // The last stage of a CTA may hold fewer than SR rows: only those are copied.  The
+  // rest of the stage keeps older bytes, which dequantise to finite values and meet
+  // activations that TMA zero-fills past K, so they add exactly zero.
+  const uint32_t sx_bytes = (uint32_t)(gpr * TW * 2 + 2 * (SR / 2) * MR * 2);
+  auto wbytes = [&](int i) {
+    const int rows = krows - i * SR;
+    return (uint32_t)((rows < SR ? rows : SR) * TWB);
+  };
 
   if (warp == NCW) {
     // ---------------- producer ----------------
@@ -158,8 +167,8 @@ __global__ void __launch_bounds__(THREADS, 2)
       for (int i = 0; i < pre; ++i) {
         const uint32_t sw = base + i * C::STAGE_BYTES;
         const int k0 = kbeg + i * SR;
-        ptx::mbar_arrive_expect_tx(full_bar(i), tx_bytes);
-        ptx::bulk_load(sw, wsrc + (size_t)i * W_BYTES, W_BYTES, full_bar(i));
+        ptx::mbar_arrive_expect_tx(full_bar(i), wbytes(i) + sx_bytes);
+        ptx::bulk_load(sw, wsrc + (size_t)i * W_BYTES, wbytes(i), full_bar(i));
         ptx::tma_load_2d(sw + W_BYTES, &tmS, full_bar(i), tile * TW, k0 / p.G);
       }
       if (p.pdl) ptx::grid_dependency_wait();
@@ -174,8 +183,8 @@ __global__ void __launch_bounds__(THREADS, 2)
             if (!*abort_flag) { *abort_flag = 1; if (p.err) atomicCAS(p.err, 0, DEVERR_TIMEOUT_PRODUCER); }
             break;
           }
-          ptx::mbar_arrive_expect_tx(full_bar(stage), tx_bytes);
-          ptx::bulk_load(sw, wsrc + (size_t)i * W_BYTES, W_BYTES, full_bar(stage));
+          ptx::mbar_arrive_expect_tx(full_bar(stage), wbytes(i) + sx_bytes);
+          ptx::bulk_load(sw, wsrc + (size_t)i * W_BYTES, wbytes(i), full_bar(stage));
           ptx::tma_load_2d(sw + W_BYTES, &tmS, full_bar(stage), tile * TW, k0 / p.G);
         }
         const uint32_t sx = sw + W_BYTES + S_BYTES;
@@ -374,10 +383,11 @@ bool w4a16_tile_supported(const qgemm_device_s* d, uint64_t x, uint64_t wt, uint
   if (!d->tcgen05) return no("device is not sm_100");
   const int smem = M > 8 ? w4x::Cfg<2>::SMEM_BYTES : w4x::Cfg<1>::SMEM_BYTES;
   if (d->smem_optin < (size_t)smem) return no("not enough shared memory per block");
-  if (K % w4x::SR != 0) return no("K must be a multiple of 512");
-  if (G % 16 != 0 || !(G % w4x::WR == 0 || w4x::WR % G == 0))
-    return no("group_size must divide 128 or be a multiple of it (and a multiple of 16)");
-  if (w4x::SR / G > 32) return no("group_size too small");
+  if (K % 16 != 0) return no("K must be a multiple of 16");
+  // every 512-row stage starts on a group boundary and every 16-row chunk lies in
+  // one group
+  if (G % 16 != 0 || !(w4x::SR % G == 0 || G % w4x::SR == 0))
+    return no("group_size must be a multiple of 16 that divides 512 or a multiple of 512");
   if (N % 8 != 0) return no("N must be a multiple of 8");
   if (!aligned(x, 16) || !aligned(wt, 16) || !aligned(sc, 16))
     return no("x, weights and scales must be 16-byte aligned");
@@ -398,8 +408,9 @@ qgemm_status launch_w4a16_tile(qgemm_stream_s* s, const void* x, const uint8_t* 
   const int ntiles = (N + TW - 1) / TW;
   Params p;
   p.M = M; p.N = N; p.K = K; p.G = G; p.zp = zp;
-  p.KS = choose_ks(ntiles, K, d->sm_count);
-  p.kc = K / p.KS;
+  const int Kr = (K + SR - 1) / SR * SR;  // K rounded up to whole stages
+  p.KS = choose_ks(ntiles, Kr, d->sm_count);
+  p.kc = Kr / p.KS;
   p.pdl = 1;
   p.wt = wt;
   p.y = static_cast<__nv_bfloat16*>(y);

@@ -180,8 +180,8 @@ QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm(qgemm_stream_t s, uint64_t x, ui
 
 /* The same group-wise W4A16 on weights repacked once by qgemm_prepack_w4_tiled
  * (64-column tiles, each tile's rows contiguous, so every CTA streams one block of
- * memory: the fast decode path).  Requires sm_100, K % 512 == 0, group_size a
- * multiple of 16 that divides 128 or is a multiple of 128, N % 8 == 0 and 16-byte
+ * memory: the fast decode path).  Requires sm_100, K % 16 == 0, group_size a
+ * multiple of 16 that divides 512 or is a multiple of 512, N % 8 == 0 and 16-byte
  * aligned x, wt and scales; otherwise QGEMM_ERR_UNSUPPORTED.  Deterministic. */
 QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_tiled(qgemm_stream_t s, uint64_t x, uint64_t wt,
                                                       uint64_t scales, int zero_point,

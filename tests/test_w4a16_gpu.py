@@ -122,6 +122,10 @@ def test_grouped_fast_path_shapes(gpu, oracle, M, N, K, G, zp):
     (4, 14336, 4096, 128, 8),
     (16, 14336, 4096, 128, 8),
     (3, 1000, 512, 64, 8),       # N not a multiple of 64
+    (1, 4096, 11008, 128, 8),    # Llama-2-7B down projection: K not a multiple of 512
+    (32, 4096, 11008, 128, 8),   # two 16-row passes
+    (2, 264, 1040, 16, 8),       # 16-row last stage, group 16
+    (1, 11008, 4096, 128, 8),
 ])
 def test_grouped_tiled_path(gpu, oracle, M, N, K, G, zp):
     x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M * 3 + N + K + G)
@@ -163,16 +167,18 @@ def test_grouped_deterministic(gpu):
     np.testing.assert_array_equal(a, b)
 
 
-def test_tiled_rejects_unsupported_shapes(gpu):
+@pytest.mark.parametrize("K,G", [(480, 48), (768, 192)])
+def test_tiled_rejects_unsupported_shapes(gpu, K, G):
+    """Groups that do not tile 512-row stages (48, 192) are refused, not miscomputed."""
     import qgemm
     dev, st, ops = gpu
-    x, wq, sc = syn.w4a16_inputs(1, 256, 256, group=64, seed=63)
-    wt = Out(dev, st, ops.w4TiledBytes(256, 256))
-    ops.prepackW4Tiled(dev_array(gpu, wq), wt, 256, 256)
+    x, wq, sc = syn.w4a16_inputs(1, 256, K, group=G, seed=63)
+    wt = Out(dev, st, ops.w4TiledBytes(K, 256))
+    ops.prepackW4Tiled(dev_array(gpu, wq), wt, K, 256)
     y = Out(dev, st, 256 * 2)
-    with pytest.raises(qgemm.QGemmError) as e:   # K % 512 != 0
-        ops.w4a16GemmGroupedTiled(dev_array(gpu, x), wt, dev_array(gpu, sc), y, 1, 256, 256,
-                                  group_size=64)
+    with pytest.raises(qgemm.QGemmError) as e:
+        ops.w4a16GemmGroupedTiled(dev_array(gpu, x), wt, dev_array(gpu, sc), y, 1, 256, K,
+                                  group_size=G)
     assert e.value.status == qgemm._lib.ERR_UNSUPPORTED
     st.sync()
 
