@@ -420,6 +420,49 @@ def w4a16_decode(ops, peaks):
     return res
 
 
+def w8a8_pipeline(ops, hb, steps, peaks):
+    """bf16 activations -> per-token int8 quantisation (qgemm_quantize_per_token) -> the
+    headline W8A8 GEMM, on device: the quantiser alone (GB/s of x read + q written) and
+    the two kernels back to back (TOPS of the GEMM's 2*M*N*K)."""
+    import torch
+    import qgemm
+    M, N, K = hb["M"], hb["N"], hb["K"]
+    R = 4  # 4 x 32 MB of bf16 activations rotating
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(99)
+    xs = [torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16) for _ in range(R)]
+    q = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    sA = torch.empty((M,), dtype=torch.float32, device="cuda")
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    B, sB = hb["B"][0], hb["sB"][0]
+
+    def quant(i):
+        ops.quantizePerToken(xs[i % R], q, sA, M, K, in_dtype=qgemm.BF16)
+
+    def both(i):
+        quant(i)
+        ops.w8a8Gemm(q, B, sA, sB, out, M, N, K, b_layout=qgemm.B_KN, out_dtype=qgemm.BF16,
+                     algo=qgemm.ALGO_TCGEN05)
+
+    res = {}
+    for name, fn in (("quantize", quant), ("quantize_plus_gemm", both)):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / 1e3 / steps
+    qb = M * K * 2 + M * K + M * 4
+    return {"quantize_us": res["quantize"] * 1e6, "quantize_GB_s": qb / res["quantize"] / 1e9,
+            "quantize_frac_of_hbm": qb / res["quantize"] / 1e9 / peaks["hbm_gbs"],
+            "quantize_plus_gemm_us": res["quantize_plus_gemm"] * 1e6,
+            "quantize_plus_gemm_TOPS": 2.0 * M * N * K / res["quantize_plus_gemm"] / 1e12}
+
+
 LLAMA_LINEARS = (("qkv", 4096, 12288), ("o", 4096, 4096), ("gate_up", 4096, 22016),
                  ("down", 11008, 4096))
 
@@ -719,9 +762,12 @@ def main():
                               f"runs at twice the bf16 rate on B200",
                 "frac_of_sustained_peak": achieved / int8_sustained}
     libctx = library_int8_context(hb, K) if rank == 0 else None
+    pipe = w8a8_pipeline(ops, hb, max(10, min(K, 50)), peaks) if rank == 0 else None
     log("e2e")
     e2e = w8a8_e2e(ops, st, hb, rank, world, max(10, min(K, 50)))
     extra = {"library_context": libctx} if libctx else {}
+    if pipe:
+        extra["w8a8_pipeline_bf16_in"] = pipe
     if world == 1 and rank == 0:
         log("w4a16 decode")
         extra["w4a16_decode"] = w4a16_decode(ops, peaks)

@@ -78,6 +78,8 @@ qgemm_status launch_w8a16_ref(qgemm_stream_s* s, const int8_t* w, const float* s
                               int K, int hasBias, int rowwise);
 qgemm_status launch_quantize(qgemm_stream_s* s, const float* w, float* scales, int8_t* q,
                              int8_t* zeros, int K, int N, int qBits);
+qgemm_status launch_quantize_tokens(qgemm_stream_s* s, const void* x, int in_dtype, int8_t* q,
+                                    float* sA, int M, int K);
 qgemm_status launch_dequantize(qgemm_stream_s* s, const int8_t* q, const float* scales,
                                float* w, int K, int N);
 qgemm_status launch_prepack_w8_nk(qgemm_stream_s* s, const int8_t* src, int8_t* dst, int K,

@@ -493,6 +493,23 @@ qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t B, uint64
                              reinterpret_cast<void*>(out), ldc, M, N, K);
 }
 
+qgemm_status qgemm_quantize_per_token(qgemm_stream_t s, uint64_t x, int in_dtype, uint64_t q,
+                                      uint64_t sA, int M, int K) {
+  QG_TRY(enter(s));
+  QG_TRY(check_dims(M, 0, K));
+  if (in_dtype != QGEMM_F32 && in_dtype != QGEMM_BF16)
+    return fail(QGEMM_ERR_INVALID_ARG, "in_dtype %d is neither QGEMM_F32 nor QGEMM_BF16", in_dtype);
+  if (M == 0) return QGEMM_OK;
+  QG_TRY(need(sA, "sA"));
+  QG_TRY(need_align(sA, 4, "sA"));
+  if (K > 0) {
+    QG_TRY(need(x, "x")); QG_TRY(need(q, "q"));
+    QG_TRY(need_align(x, in_dtype == QGEMM_BF16 ? 2 : 4, "x"));
+  }
+  return launch_quantize_tokens(s, reinterpret_cast<const void*>(x), in_dtype,
+                                reinterpret_cast<int8_t*>(q), reinterpret_cast<float*>(sA), M, K);
+}
+
 // ---- W8A16 ----
 
 qgemm_status qgemm_w8a16_gemm(qgemm_stream_t s, uint64_t wInt8, uint64_t scalesW, uint64_t x,

@@ -274,6 +274,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
   }
 }
 
+// BF16 selects the MMA kind at compile time: a run-time choice inside the issue loop
+// cost a fifth of the tensor throughput.
+template <bool BF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -365,7 +368,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = p.bf16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc = BF16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -403,7 +406,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             } else {
               bdesc = ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
             }
-            if (p.bf16)
+            if constexpr (BF16)
               ptx::umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
             else
               ptx::umma_i8(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
@@ -476,6 +479,7 @@ static_assert(STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024 <= SMEM_BYTES,
               "shared memory budget");
 }  // namespace pair
 
+template <bool BF16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
@@ -571,7 +575,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA) ----------------
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = p.bf16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc = BF16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -602,7 +606,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             // B per CTA: 128 columns = one 128-byte swizzle row in either layout.
             const uint64_t bdesc = p.b_kn ? ptx::smem_desc_sw128(sb + kk * UMMA_K * 128, B_BYTES, 1024)
                                           : ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
-            if (p.bf16)
+            if constexpr (BF16)
               ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
             else
               ptx::umma_i8_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
@@ -764,25 +768,24 @@ static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, c
       p.tma_store = 1;
   }
 
-  static bool attr_set[64][2] = {};
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params);
+  const Kern kern = use_pair ? (bf16 ? w8a8_tcgen05_pair_kernel<true> : w8a8_tcgen05_pair_kernel<false>)
+                             : (bf16 ? w8a8_tcgen05_kernel<true> : w8a8_tcgen05_kernel<false>);
+  const int smem = use_pair ? pair::SMEM_BYTES : SMEM_BYTES;
+  static bool attr_set[64][2][2] = {};
   const int ord = s->dev->ordinal;
-  if (ord >= 0 && ord < 64 && !attr_set[ord][use_pair]) {
-    cudaError_t e = use_pair
-        ? cudaFuncSetAttribute(w8a8_tcgen05_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               pair::SMEM_BYTES)
-        : cudaFuncSetAttribute(w8a8_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SMEM_BYTES);
+  if (ord < 0 || ord >= 64 || !attr_set[ord][use_pair][bf16 ? 1 : 0]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8a8_tcgen05)");
-    attr_set[ord][use_pair] = true;
+    if (ord >= 0 && ord < 64) attr_set[ord][use_pair][bf16 ? 1 : 0] = true;
   }
   if (use_pair) {
     const int max_pairs = s->dev->sm_count / 2;
     const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
-    w8a8_tcgen05_pair_kernel<<<2 * pairs, NUM_THREADS, pair::SMEM_BYTES, s->stream>>>(tmA, tmB, tmO,
-                                                                                     p);
+    kern<<<2 * pairs, NUM_THREADS, smem, s->stream>>>(tmA, tmB, tmO, p);
   } else {
     const int grid = p.num_tiles < s->dev->sm_count ? p.num_tiles : s->dev->sm_count;
-    w8a8_tcgen05_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s->stream>>>(tmA, tmB, tmO, p);
+    kern<<<grid, NUM_THREADS, smem, s->stream>>>(tmA, tmB, tmO, p);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "w8a8_tcgen05 launch");

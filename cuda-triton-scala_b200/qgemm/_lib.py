@@ -76,6 +76,7 @@ SIGNATURES = {
     "qgemm_w4a16_grouped_gemm_prefill": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I,
                                                _U64, _SZ]),
     "qgemm_gemm_bf16_nk": (_S, [_P, _U64, _U64, _U64, _I, _I, _I, _I]),
+    "qgemm_quantize_per_token": (_S, [_P, _U64, _I, _U64, _U64, _I, _I]),
     "qgemm_prepack_w8_nk": (_S, [_P, _U64, _U64, _I, _I]),
     "qgemm_launch_by_name": (_S, [_P, ctypes.c_char_p, ctypes.POINTER(_U64), _I,
                                   ctypes.POINTER(_I), _I]),

@@ -111,6 +111,11 @@ class QuantizedGemmOps:
         """uint32 [K, N/8] reference-order int4 weights -> 64-column tiles (one time)."""
         L.call("qgemm_prepack_w4_tiled", self._h, L.addr(wq), L.addr(dst), K, N)
 
+    def quantizePerToken(self, x, q, sA, M: int, K: int, *, in_dtype: int = L.BF16):
+        """dynamicQuantize along rows: x [M,K] (bf16 or fp32) -> int8 q [M,K], sA [M]."""
+        L.call("qgemm_quantize_per_token", self._h, L.addr(x), in_dtype, L.addr(q), L.addr(sA),
+               M, K)
+
     def prepackW8NK(self, src_kn, dst_nk, K: int, N: int):
         L.call("qgemm_prepack_w8_nk", self._h, L.addr(src_kn), L.addr(dst_nk), K, N)
 

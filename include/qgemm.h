@@ -218,6 +218,15 @@ QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64
 QGEMM_API qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t out,
                                           int ldc, int M, int N, int K);
 
+/* Dynamic per-token int8 quantisation of activations: the arithmetic of
+ * QuantizedGemmOps.dynamicQuantize (QuantizedGemmOps.scala:121-157) applied to each
+ * row of x (a token) instead of each column of a weight.  x [M,K] fp32 or bf16
+ * (in_dtype QGEMM_F32 / QGEMM_BF16), q int8 [M,K], sA f32 [M] = maxAbs / 127: the A
+ * operand and per-token scales of qgemm_w8a8_gemm.  Bit-exact with the reference
+ * arithmetic (NaN ignored by the max, Scala toInt truncation and saturation). */
+QGEMM_API qgemm_status qgemm_quantize_per_token(qgemm_stream_t s, uint64_t x, int in_dtype,
+                                                uint64_t q, uint64_t sA, int M, int K);
+
 /* One-time weight repack: int8 [K,N] (reference layout) -> [N,K] (K-major). */
 QGEMM_API qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src_kn, uint64_t dst_nk,
                                  int K, int N);

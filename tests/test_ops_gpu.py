@@ -124,3 +124,50 @@ def test_unshard_columns(gpu, world, M, ncols):
     st.sync()
     np.testing.assert_array_equal(out.read(np.uint16, (M, world * ncols)),
                                   np.concatenate(list(g), axis=1))
+
+
+@pytest.mark.parametrize("M,K,dt", [(7, 300, "f32"), (64, 4096, "bf16"), (3, 13, "f32"),
+                                    (129, 1024, "bf16")])
+def test_quantize_per_token_matches_reference_rows(gpu, oracle, M, K, dt):
+    """Per-token quantisation == the reference dynamicQuantize applied to x^T, bit for bit
+    (scales and int8 values), for fp32 and bf16 activations."""
+    import qgemm
+    dev, st, ops = gpu
+    rng = np.random.default_rng(M * K)
+    xf = (rng.standard_normal((M, K)) * rng.uniform(0.1, 10, (M, 1))).astype(np.float32)
+    xf[0, :] = 0.0                      # an all-zero row: scale 0, mul 1
+    if K > 5:
+        xf[1, 3] = np.nan               # NaN is ignored by the max and quantises to 0
+        xf[2 % M, 5] = 1e30             # saturation
+    if dt == "bf16":
+        xb = syn.bf16_bits(xf)
+        x_dev, x_ref, in_dtype = dev_array(gpu, xb), syn.bf16_to_float(xb), qgemm.BF16
+    else:
+        x_dev, x_ref, in_dtype = dev_array(gpu, xf), xf, qgemm.F32
+    q = Out(dev, st, M * K)
+    s = Out(dev, st, M * 4)
+    ops.quantizePerToken(x_dev, q, s, M, K, in_dtype=in_dtype)
+    st.sync()
+    ref_s, ref_q = oracle.dynamic_quantize(np.ascontiguousarray(x_ref.T), 8)
+    np.testing.assert_array_equal(q.read(np.int8, (M, K)), ref_q.T)
+    np.testing.assert_array_equal(s.read(np.uint32, (M,)), ref_s.view(np.uint32))
+
+
+def test_quantize_then_w8a8_pipeline(gpu, oracle):
+    """bf16 activations -> per-token int8 + sA -> W8A8 GEMM, against the oracle."""
+    import qgemm
+    dev, st, ops = gpu
+    M, N, K = 256, 512, 768
+    rng = np.random.default_rng(9)
+    xb = syn.bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+    _, B, _, sB = syn.w8a8_inputs(M, N, K, seed=10)
+    q = Out(dev, st, M * K)
+    sA = Out(dev, st, M * 4)
+    ops.quantizePerToken(dev_array(gpu, xb), q, sA, M, K, in_dtype=qgemm.BF16)
+    y = Out(dev, st, M * N * 2)
+    ops.w8a8Gemm(q, dev_array(gpu, B), sA, dev_array(gpu, sB), y, M, N, K,
+                 algo=qgemm.ALGO_TCGEN05)
+    st.sync()
+    ref_s, ref_q = oracle.dynamic_quantize(np.ascontiguousarray(syn.bf16_to_float(xb).T), 8)
+    yo, _ = oracle.w8a32_gemm(B, sB, np.ascontiguousarray(ref_q.T), ref_s)
+    np.testing.assert_array_equal(y.read(np.uint16, (M, N)), oracle.bf16_rne(yo))
