@@ -313,6 +313,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
+    // The next kernel on the stream may start its own set-up on SMs this grid has
+    // finished with; every global access below waits for the previous kernel.
+    ptx::grid_launch_dependents();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
   }
@@ -328,6 +331,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      ptx::grid_dependency_wait();
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -425,6 +429,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    ptx::grid_dependency_wait();  // scales and the output belong to the previous kernel until it ends
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const bool elected = (warp == 2 && lane == 0);
     int chunk_seq = 0;
@@ -521,6 +526,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
+    // The next kernel on the stream may start its own set-up on SMs this grid has
+    // finished with; every global access below waits for the previous kernel.
+    ptx::grid_launch_dependents();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
   }
@@ -536,6 +544,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
+      ptx::grid_dependency_wait();
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -624,6 +633,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    ptx::grid_dependency_wait();  // scales and the output belong to the previous kernel until it ends
     const int q = warp & 3;
     const bool elected = (warp == 2 && lane == 0);
     int chunk_seq = 0;
@@ -779,15 +789,24 @@ static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, c
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8a8_tcgen05)");
     if (ord >= 0 && ord < 64) attr_set[ord][use_pair][bf16 ? 1 : 0] = true;
   }
+  int grid;
   if (use_pair) {
     const int max_pairs = s->dev->sm_count / 2;
-    const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
-    kern<<<2 * pairs, NUM_THREADS, smem, s->stream>>>(tmA, tmB, tmO, p);
+    grid = 2 * (p.num_tiles < max_pairs ? p.num_tiles : max_pairs);
   } else {
-    const int grid = p.num_tiles < s->dev->sm_count ? p.num_tiles : s->dev->sm_count;
-    kern<<<grid, NUM_THREADS, smem, s->stream>>>(tmA, tmB, tmO, p);
+    grid = p.num_tiles < s->dev->sm_count ? p.num_tiles : s->dev->sm_count;
   }
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, p);
   if (e != cudaSuccess) return cuda_fail(e, "w8a8_tcgen05 launch");
   return QGEMM_OK;
 }
