@@ -81,7 +81,37 @@ struct Params {
                    // as they are (no scales, no int32 output)
   int a_kblocks;   // k-block b of A is read at b % a_kblocks (A repeated along K);
                    // equal to num_k_blocks for an ordinary product
+  // Last-wave split of the CTA-pair kernel: the first split_w tiles are done whole,
+  // one per pair per round; each of the remaining tiles is cut along K into split_s
+  // parts that run on different pairs at once.  A part writes its int32 partial sums
+  // to `part`; the part that counts in last on `cnt` adds them all (in part order;
+  // integer sums, so any order gives the same bits) and runs the epilogue.
+  int split_w, split_s;
+  int32_t* part;   // [(tail tile * 2 + rank) * split_s + part][128 x 256 int32, part_index]
+  int* cnt;        // [tail tile * 2 + rank], zero between launches
 };
+
+// Work item i of pair `pair`: a whole tile, or one K part of a tail tile.  Returns
+// false when the pair has no item i.
+__device__ __forceinline__ bool pair_item(const Params& p, int pair, int npairs, int i,
+                                          int& tile, int& kb0, int& kb1, int& part) {
+  const int T = p.num_m_blocks * p.num_n_blocks;
+  const int rounds = p.split_w / npairs;  // split_w is a multiple of npairs when splitting
+  if (p.split_s <= 1 || i < rounds) {
+    tile = pair + i * npairs;
+    if (tile >= (p.split_s <= 1 ? T : p.split_w)) return false;
+    kb0 = 0;
+    kb1 = p.num_k_blocks;
+    part = -1;
+    return true;
+  }
+  if (i > rounds || pair >= (T - p.split_w) * p.split_s) return false;
+  tile = p.split_w + pair / p.split_s;
+  part = pair % p.split_s;
+  kb0 = (int)((long long)p.num_k_blocks * part / p.split_s);
+  kb1 = (int)((long long)p.num_k_blocks * (part + 1) / p.split_s);
+  return true;
+}
 
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
@@ -181,10 +211,36 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
 // into the swizzled staging buffer; one elected thread then stores each 128-row x
 // 128-byte block with a TMA bulk tensor store (clipped at the tensor edges).  `chunk_seq`
 // counts staging buffers used so far (identical in all epilogue threads).
+// Partial tiles of the last-wave split: 128 rows x 256 int32 columns of one CTA, stored
+// so that the 32 rows a warp holds are contiguous: 16-byte piece v (columns 4v..4v+3)
+// of 32-column chunk c of row rl sits at int4 index (c * 8 + v) * 128 + rl.
+__device__ __forceinline__ size_t part_index(int c, int v, int rl) {
+  return ((size_t)(c * 8 + v) * 128 + rl);
+}
+
+// With `parts` set, the accumulators are not read from TMEM but summed from `nparts`
+// partial tiles, `part_stride` ints apart (in part order).
+__device__ __forceinline__ void sum_parts(const int32_t* parts, int nparts, size_t part_stride,
+                                          int rl, int col, uint32_t (&r)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) r[j] = 0u;
+  for (int pp = 0; pp < nparts; ++pp) {
+    const int4* src = reinterpret_cast<const int4*>(parts + pp * part_stride);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const int4 x = __ldcg(src + part_index(col / 32, v, rl));
+      r[4 * v] += (uint32_t)x.x; r[4 * v + 1] += (uint32_t)x.y;
+      r[4 * v + 2] += (uint32_t)x.z; r[4 * v + 3] += (uint32_t)x.w;
+    }
+  }
+}
+
 __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tmO,
                                               uint32_t tmem_base, uint32_t acc_col, int q,
                                               int lane, int row0, int n0, uint32_t stg,
-                                              bool elected, int& chunk_seq, bool ok) {
+                                              bool elected, int& chunk_seq, bool ok,
+                                              const int32_t* parts = nullptr, int nparts = 0,
+                                              size_t part_stride = 0) {
   const int row = row0 + q * 32 + lane;
   const int rl = q * 32 + lane;  // row within the staging block
   const float sa = (!p.bf16 && row < p.M) ? __ldg(p.sA + row) : 0.f;
@@ -194,8 +250,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       uint32_t r[32];
       __syncwarp();
       if (!ok) return;
-      ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + c * 32, r);
-      ptx::tmem_wait_ld();
+      if (parts) {
+        sum_parts(parts, nparts, part_stride, rl, c * 32, r);
+      } else {
+        ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + c * 32, r);
+        ptx::tmem_wait_ld();
+      }
       store_chunk(p, row, n0 + c * 32, sa, r);
     }
     return;
@@ -213,7 +273,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       uint32_t r[32];
       const int nc = n0 + ch * cwe + sub * 32;
       __syncwarp();
-      if (ok) {
+      if (ok && parts) {
+        sum_parts(parts, nparts, part_stride, rl, ch * cwe + sub * 32, r);
+      } else if (ok) {
         ptx::tmem_ld_32x32b_x32(
             tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + (uint32_t)(ch * cwe + sub * 32), r);
         ptx::tmem_wait_ld();
@@ -512,7 +574,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t rank = ptx::cluster_ctarank();   // 0: issues the MMAs
   const int pair_id = blockIdx.x / 2;
   const int npairs = gridDim.x / 2;
-  const int num_tiles = p.num_m_blocks * p.num_n_blocks;  // pair tiles
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -549,10 +610,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int tile = pair_id; tile < num_tiles && ok; tile += npairs) {
+      int tile, kb0, kb1, part;
+      for (int item = 0; ok && pair_item(p, pair_id, npairs, item, tile, kb0, kb1, part); ++item) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
             if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_PRODUCER, abort_flag, rank);
             ok = false;
@@ -590,7 +652,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int tile = pair_id; tile < num_tiles && ok; tile += npairs, ++it) {
+      int tile, kb0, kb1, part;
+      for (; ok && pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part); ++it) {
         const int a = it & 1;
         const uint32_t aphase = (uint32_t)((it >> 1) & 1);
         if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag)) {
@@ -600,7 +663,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(a * BN);
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag)) {
             if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_MMA, abort_flag, rank);
             ok = false;
@@ -615,10 +678,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             // B per CTA: 128 columns = one 128-byte swizzle row in either layout.
             const uint64_t bdesc = p.b_kn ? ptx::smem_desc_sw128(sb + kk * UMMA_K * 128, B_BYTES, 1024)
                                           : ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
+            const uint32_t accum = (kb != kb0 || kk != 0) ? 1u : 0u;
             if constexpr (BF16)
-              ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+              ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, accum);
             else
-              ptx::umma_i8_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+              ptx::umma_i8_pair(d_tmem, adesc, bdesc, idesc, accum);
           }
           ptx::umma_commit_pair(empty_bar(stage), 0x3);
           issued_any = true;
@@ -639,8 +703,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     int chunk_seq = 0;
     const uint32_t te_leader0 = ptx::map_to_rank(tempty_bar(0), 0);
     const uint32_t te_leader1 = ptx::map_to_rank(tempty_bar(1), 0);
+    volatile int* last_flag = abort_flag + 1;
+    const int rl = q * 32 + lane;  // row of this CTA's half-tile
     int it = 0;
-    for (int tile = pair_id; tile < num_tiles; tile += npairs, ++it) {
+    int tile, kb0, kb1, part;
+    for (; pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part); ++it) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int a = it & 1;
@@ -650,10 +717,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (!ok && lane == 0 && !*abort_flag)
         report_pair(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag, rank);
       ptx::tc_fence_after();
-      epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM + (int)rank * 128,
-                    nb * BN, stg_base, elected, chunk_seq, ok);
+      if (part < 0) {
+        epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM + (int)rank * 128,
+                      nb * BN, stg_base, elected, chunk_seq, ok);
+        ptx::tc_fence_before();
+        ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
+        continue;
+      }
+      // A K part of a tail tile: park the int32 partial sums of this CTA's 128 rows,
+      // then count in; the last part of the tile adds all parts and stores the tile.
+      const size_t slot_ints = (size_t)128 * 256;
+      const int tt = (tile - p.split_w) * 2 + (int)rank;
+      int4* mine = reinterpret_cast<int4*>(p.part + ((size_t)tt * p.split_s + part) * slot_ints);
+#pragma unroll 1
+      for (int c = 0; c < 256 / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();
+        if (ok) {
+          ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN + c * 32), r);
+          ptx::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          mine[part_index(c, v, rl)] =
+              make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
+      }
       ptx::tc_fence_before();
-      ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
+      ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);  // TMEM is free again
+      __threadfence();
+      ptx::named_bar_sync(1, 128);
+      if (elected) *last_flag = atomicAdd(p.cnt + tt, 1) == p.split_s - 1;
+      ptx::named_bar_sync(1, 128);
+      if (*last_flag) {
+        __threadfence();
+        epilogue_tile(p, &tmO, tmem_base, 0u, q, lane, mb * BM + (int)rank * 128, nb * BN,
+                      stg_base, elected, chunk_seq, ok,
+                      p.part + (size_t)tt * p.split_s * slot_ints, p.split_s, slot_ints);
+        if (elected) p.cnt[tt] = 0;
+      }
+      ptx::named_bar_sync(1, 128);  // the flag is rewritten only after everyone read it
     }
     if (elected) ptx::bulk_wait_group_all();
   }
@@ -723,10 +828,13 @@ bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int
 // a row of A (and of B in the [N,K] layout): int8 elements, or twice the bf16 count.
 // With a_repeat = r > 1, each row of B holds r blocks of ceil(K / 128) * 128 bytes
 // (zero past K) and A is read r times along K: out = sum_i A * B_i^T.
+// `scratch`: caller-provided scratch for the last-wave split (null: the stream handle's
+// own scratch, made on first use).
 static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, const void* B,
                                    int b_kn, const float* sA, const float* sB, void* out,
                                    int out_dtype, int ldc, int M, int N, int K, int32_t* acc,
-                                   int a_repeat = 1) {
+                                   int a_repeat = 1, void* scratch = nullptr,
+                                   size_t scratch_bytes = 0) {
   using namespace w8a8;
   // CTA pairs (256 x 256 tiles) whenever the problem has at least one full pair tile.
   const bool use_pair = M >= 256 && N >= 256 && s->dev->sm_count >= 2;
@@ -790,9 +898,43 @@ static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, c
     if (ord >= 0 && ord < 64) attr_set[ord][use_pair][bf16 ? 1 : 0] = true;
   }
   int grid;
+  p.split_w = p.num_tiles;
+  p.split_s = 1;
+  p.part = nullptr;
+  p.cnt = nullptr;
   if (use_pair) {
     const int max_pairs = s->dev->sm_count / 2;
-    grid = 2 * (p.num_tiles < max_pairs ? p.num_tiles : max_pairs);
+    const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
+    grid = 2 * pairs;
+    // Last-wave split: when the final round would leave at least three quarters of the
+    // pairs idle, cut each leftover tile along K into 4 parts (at least two k-blocks
+    // each).  Measured: a K part runs at about 0.27 of a tile plus its share of the
+    // k-blocks and the partial sums add about a quarter of a tile, so two-way splits
+    // (4096^3: 34 leftover tiles on 74 pairs) lose and four-way ones win.
+    const int rounds = p.num_tiles / pairs, rest = p.num_tiles - rounds * pairs;
+    int parts = (rest > 0 && rest * 4 <= pairs) ? 4 : 1;
+    while (parts > 1 && p.num_k_blocks / parts < 2) --parts;
+    if (parts < 4) parts = 1;
+    if (rounds >= 1 && parts >= 2) {
+      // Scratch layout, fixed for every call on the handle: counters for up to
+      // 2 * max_pairs half-tiles (rest < max_pairs), then the partial sums.  The counters
+      // must sit at the same place in every call: they are zero between calls only
+      // because each call returns the ones it used to zero.
+      void* ws = nullptr;
+      const size_t part_bytes = (size_t)rest * 2 * parts * 128 * 256 * sizeof(int32_t);
+      const size_t cnt_bytes = ((size_t)max_pairs * 2 * sizeof(int) + 255) & ~(size_t)255;
+      if (scratch) {
+        if (scratch_bytes >= cnt_bytes + part_bytes) ws = scratch;
+      } else if (stream_workspace(s, cnt_bytes + part_bytes, &ws) != QGEMM_OK) {
+        ws = nullptr;  // e.g. under graph capture: run the last round unsplit
+      }
+      if (ws) {
+        p.split_w = rounds * pairs;
+        p.split_s = parts;
+        p.cnt = static_cast<int*>(ws);
+        p.part = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + cnt_bytes);
+      }
+    }
   } else {
     grid = p.num_tiles < s->dev->sm_count ? p.num_tiles : s->dev->sm_count;
   }

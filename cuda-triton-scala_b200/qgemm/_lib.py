@@ -33,6 +33,20 @@ ALGO_AUTO = 0
 ALGO_TCGEN05 = 1
 ALGO_SIMT = 2
 
+BLOB_VERSION = 1
+BLOB_W4_TILED = 1
+BLOB_W8_KN = 2
+BLOB_W8_NK = 3
+
+
+class BlobInfo(ctypes.Structure):
+    """qgemm_blob_info (include/qgemm.h)."""
+    _fields_ = [("version", ctypes.c_uint32), ("kind", ctypes.c_int32), ("K", ctypes.c_int32),
+                ("N", ctypes.c_int32), ("group_size", ctypes.c_int32),
+                ("zero_point", ctypes.c_int32), ("weight_bytes", ctypes.c_uint64),
+                ("scale_bytes", ctypes.c_uint64)]
+
+
 _S = ctypes.c_int32
 _P = ctypes.c_void_p
 _U64 = ctypes.c_uint64
@@ -80,6 +94,10 @@ SIGNATURES = {
     "qgemm_prepack_w8_nk": (_S, [_P, _U64, _U64, _I, _I]),
     "qgemm_launch_by_name": (_S, [_P, ctypes.c_char_p, ctypes.POINTER(_U64), _I,
                                   ctypes.POINTER(_I), _I]),
+    "qgemm_blob_save": (_S, [ctypes.c_char_p, ctypes.POINTER(BlobInfo), _P, _P]),
+    "qgemm_blob_info_read": (_S, [ctypes.c_char_p, ctypes.POINTER(BlobInfo)]),
+    "qgemm_blob_load": (_S, [ctypes.c_char_p, _P, _SZ, _P, _SZ]),
+    "qgemm_blob_load_device": (_S, [_P, ctypes.c_char_p, _U64, _SZ, _U64, _SZ]),
     "qgemm_shard_columns": (_S, [_I, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "qgemm_comm_unique_id": (_S, [_P]),
     "qgemm_comm_init": (_S, [_P, _P, _I, _I, ctypes.POINTER(_P)]),

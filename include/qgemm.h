@@ -242,6 +242,45 @@ QGEMM_API qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name,
                                   const uint64_t* bufs, int nbufs,
                                   const int* ints, int nints);
 
+/* ---- weight blobs ------------------------------------------------------------
+ * A versioned file holding quantised weights already in a kernel layout, with
+ * their scales, so that a model loads straight into device memory (no repack).
+ * No counterpart in the reference, whose weights live in host arrays.  The int4
+ * layout of the reference's w4a16Gemm (two nibbles per byte along the flattened
+ * (k, n) index, low nibble first; QuantizedGemmOps.scala:234-238) is, for even N,
+ * byte for byte the uint32 [K, N/8] layout of qgemm_w4a16_grouped_gemm, so
+ * reference weights import with qgemm_prepack_w4_tiled and no other conversion.
+ * Every read checks the magic, the version, the sizes against the shape and a
+ * CRC-32 of each section; a mismatch is QGEMM_ERR_INVALID_ARG, another version
+ * QGEMM_ERR_UNSUPPORTED. */
+#define QGEMM_BLOB_VERSION 1
+enum {
+  QGEMM_BLOB_W4_TILED = 1,  /* qgemm_prepack_w4_tiled layout + bf16 scales [K/G, N]   */
+  QGEMM_BLOB_W8_KN = 2,     /* int8 [K, N] (reference wInt8 layout) + f32 scales [N]  */
+  QGEMM_BLOB_W8_NK = 3      /* int8 [N, K] + f32 scales [N]                           */
+};
+typedef struct qgemm_blob_info {
+  uint32_t version;      /* filled in by qgemm_blob_info_read                         */
+  int32_t kind;
+  int32_t K, N;
+  int32_t group_size;    /* int4: rows per scale group; int8: 0                       */
+  int32_t zero_point;    /* int4: 0..15; int8: 0                                      */
+  uint64_t weight_bytes; /* filled in by qgemm_blob_info_read                         */
+  uint64_t scale_bytes;  /* filled in by qgemm_blob_info_read                         */
+} qgemm_blob_info;
+/* Writes host buffers (sizes implied by kind and shape) to `path`. */
+QGEMM_API qgemm_status qgemm_blob_save(const char* path, const qgemm_blob_info* info,
+                                       const void* weights, const void* scales);
+QGEMM_API qgemm_status qgemm_blob_info_read(const char* path, qgemm_blob_info* info);
+/* Reads and verifies both sections into host buffers of at least the given sizes. */
+QGEMM_API qgemm_status qgemm_blob_load(const char* path, void* weights, size_t weight_bytes,
+                                       void* scales, size_t scale_bytes);
+/* Verifies the whole file, then copies both sections to device buffers (returns
+ * after the copies have finished). */
+QGEMM_API qgemm_status qgemm_blob_load_device(qgemm_stream_t s, const char* path, uint64_t weights,
+                                              size_t weight_bytes, uint64_t scales,
+                                              size_t scale_bytes);
+
 /* ---- column sharding and the output all-gather ----------------------------
  * The reference has only a host-array NCCL wrapper (nccl/NCCLCommunicator.scala:
  * 35-92, 151-163, 302-320) with no unique-id exchange.  Here rank r holds the

@@ -204,3 +204,28 @@ def test_grouped_rejects_bad_args(gpu):
         ops.w4a16GemmGrouped(8, 8, 8, 8, 1, 16, 64, group_size=64, zero_point=16)
     assert e.value.status == qgemm._lib.ERR_INVALID_ARG
     st.sync()
+
+
+def test_blob_round_trip_through_the_device(gpu, tmp_path):
+    """Prepacked weights saved as a blob and loaded straight into device memory run
+    the tiled GEMM to the same bits as the freshly prepacked ones."""
+    from qgemm import blob
+    dev, st, ops = gpu
+    M, N, K, G = 4, 1024, 2048, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=81)
+    nbytes = ops.w4TiledBytes(K, N)
+    wt = Out(dev, st, nbytes)
+    ops.prepackW4Tiled(dev_array(gpu, wq), wt, K, N)
+    st.sync()
+    p = str(tmp_path / "layer.qgb")
+    blob.save(p, "w4_tiled", K, N, wt.read(np.uint8, (nbytes,)), sc, group_size=G, zero_point=8)
+    wt2 = Out(dev, st, nbytes)
+    sc2 = Out(dev, st, sc.nbytes)
+    blob.load_to_device(st, p, wt2, nbytes, sc2, sc.nbytes)
+    ys = []
+    for w_, s_ in ((wt, dev_array(gpu, sc)), (wt2, sc2)):
+        y = Out(dev, st, M * N * 2)
+        ops.w4a16GemmGroupedTiled(dev_array(gpu, x), w_, s_, y, M, N, K, group_size=G)
+        st.sync()
+        ys.append(y.read(np.uint16, (M, N)).copy())
+    np.testing.assert_array_equal(ys[0], ys[1])

@@ -81,6 +81,32 @@ def test_tcgen05_cta_pair_shapes(gpu, oracle, M, N, K, layout):
     check_exact(oracle, A, B, sA, sB, y, acc, qgemm.BF16)
 
 
+@pytest.mark.parametrize("M,N,K,layout,out_dtype,ldc", [
+    (3840, 1280, 1024, qgemm.B_KN, qgemm.BF16, None),   # 75 pair tiles: one tile in 4 K parts
+    (3840, 1536, 1024, qgemm.B_NK, qgemm.BF16, None),   # 90 tiles: 16 leftover tiles in 4 parts
+    (3840, 1280, 1024, qgemm.B_KN, qgemm.F32, 1281),    # parts summed on the plain-store path
+    (4096, 4096, 512, qgemm.B_NK, qgemm.BF16, None),    # 256 tiles: last round left whole
+])
+def test_tcgen05_last_wave_split(gpu, oracle, M, N, K, layout, out_dtype, ldc):
+    """The last-wave split (tail tiles cut along K over idle CTA pairs, int32 partials
+    summed by the last part) gives the same bits as the CUDA-core kernel, and the
+    sampled rows equal the oracle; run twice to check that the counters reset."""
+    A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K + 5)
+    y1, a1 = run(gpu, A, B, sA, sB, layout=layout, out_dtype=out_dtype, ldc=ldc,
+                 algo=qgemm.ALGO_TCGEN05)
+    y2, a2 = run(gpu, A, B, sA, sB, layout=layout, out_dtype=out_dtype, ldc=ldc,
+                 algo=qgemm.ALGO_TCGEN05)
+    ys, as_ = run(gpu, A, B, sA, sB, layout=layout, out_dtype=out_dtype, ldc=ldc,
+                  algo=qgemm.ALGO_SIMT)
+    np.testing.assert_array_equal(a1, as_)
+    np.testing.assert_array_equal(y1, ys)
+    np.testing.assert_array_equal(a2, as_)
+    np.testing.assert_array_equal(y2, ys)
+    rows = np.unique(np.concatenate([np.random.default_rng(1).choice(M, 12, replace=False),
+                                     [0, M - 1]]))
+    check_exact(oracle, A, B, sA, sB, y1, a1, out_dtype, rows=rows)
+
+
 def test_tcgen05_cta_pair_ldc_f32(gpu, oracle):
     A, B, sA, sB = syn.w8a8_inputs(384, 512, 640, seed=17)
     y, acc = run(gpu, A, B, sA, sB, out_dtype=qgemm.F32, ldc=520, algo=qgemm.ALGO_TCGEN05)
