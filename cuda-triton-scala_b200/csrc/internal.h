@@ -59,6 +59,10 @@ enum : int {
 qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
                                  const float* sA, const float* sB, void* out, int out_dtype,
                                  int ldc, int M, int N, int K, int32_t* acc);
+// As launch_w8a8_tcgen05, with the last-wave split's scratch in a static device array.
+qgemm_status launch_w8a8_tcgen05_static(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
+                                        const float* sA, const float* sB, void* out, int out_dtype,
+                                        int ldc, int M, int N, int K, int32_t* acc);
 bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int b_kn,
                             uint64_t out, int out_dtype, int ldc, int M, int N, int K,
                             const char** why);

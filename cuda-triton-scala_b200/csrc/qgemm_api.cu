@@ -357,6 +357,46 @@ qgemm_status qgemm_w8a8_gemm(qgemm_stream_t s, uint64_t A, uint64_t B, int b_lay
                           reinterpret_cast<int32_t*>(acc_i32));
 }
 
+qgemm_status qgemm_w8a8_gemm_static_scratch(qgemm_stream_t s, uint64_t A, uint64_t B,
+                                            int b_layout, uint64_t sA, uint64_t sB, uint64_t out,
+                                            int out_dtype, int ldc, int M, int N, int K,
+                                            uint64_t acc_i32, int algo) {
+  QG_TRY(enter(s));
+  QG_TRY(check_dims(M, N, K));
+  if (b_layout != QGEMM_B_KN && b_layout != QGEMM_B_NK)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad b_layout %d", b_layout);
+  if (out_dtype != QGEMM_F32 && out_dtype != QGEMM_BF16)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad out_dtype %d", out_dtype);
+  if (algo < QGEMM_ALGO_AUTO || algo > QGEMM_ALGO_SIMT)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad algo %d", algo);
+  if (M == 0 || N == 0) return QGEMM_OK;
+  if (ldc < N) return fail(QGEMM_ERR_INVALID_ARG, "ldc %d < N %d", ldc, N);
+  QG_TRY(need(A, "A")); QG_TRY(need(B, "B")); QG_TRY(need(sA, "sA"));
+  QG_TRY(need(sB, "sB")); QG_TRY(need(out, "out"));
+  QG_TRY(need_align(sA, 4, "sA")); QG_TRY(need_align(sB, 4, "sB"));
+  QG_TRY(need_align(out, out_dtype == QGEMM_F32 ? 4 : 2, "out"));
+  QG_TRY(need_align(acc_i32, 4, "acc_i32"));
+  const int b_kn = b_layout == QGEMM_B_KN;
+  const char* why = nullptr;
+  const bool tc = K > 0 && w8a8_tcgen05_supported(s->dev, A, B, b_kn, out, out_dtype, ldc, M,
+                                                  N, K, &why);
+  if (algo == QGEMM_ALGO_TCGEN05 && !tc)
+    return fail(QGEMM_ERR_UNSUPPORTED, "tcgen05 W8A8 path unavailable: %s",
+                why ? why : "K == 0");
+  if (algo != QGEMM_ALGO_SIMT && tc)
+    return launch_w8a8_tcgen05_static(s, reinterpret_cast<const void*>(A),
+                                      reinterpret_cast<const void*>(B), b_kn,
+                                      reinterpret_cast<const float*>(sA),
+                                      reinterpret_cast<const float*>(sB),
+                                      reinterpret_cast<void*>(out), out_dtype, ldc, M, N, K,
+                                      reinterpret_cast<int32_t*>(acc_i32));
+  return launch_w8a8_simt(s, reinterpret_cast<const int8_t*>(A),
+                          reinterpret_cast<const int8_t*>(B), b_kn,
+                          reinterpret_cast<const float*>(sA), reinterpret_cast<const float*>(sB),
+                          reinterpret_cast<void*>(out), out_dtype, ldc, M, N, K,
+                          reinterpret_cast<int32_t*>(acc_i32));
+}
+
 qgemm_status qgemm_w8a32_gemm(qgemm_stream_t s, uint64_t wInt8, uint64_t scalesW, uint64_t x,
                               uint64_t scalesX, uint64_t y, int M, int N, int K) {
   return qgemm_w8a8_gemm(s, x, wInt8, QGEMM_B_KN, scalesX, scalesW, y, QGEMM_F32, N, M, N, K, 0,

@@ -924,7 +924,11 @@ static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, c
       const size_t part_bytes = (size_t)rest * 2 * parts * 128 * 256 * sizeof(int32_t);
       const size_t cnt_bytes = ((size_t)max_pairs * 2 * sizeof(int) + 255) & ~(size_t)255;
       if (scratch) {
-        if (scratch_bytes >= cnt_bytes + part_bytes) ws = scratch;
+        if (scratch_bytes < cnt_bytes + part_bytes)
+          return fail(QGEMM_ERR_UNSUPPORTED,
+                      "this shape's last-wave split needs %zu bytes of scratch; the static "
+                      "scratch holds %zu", cnt_bytes + part_bytes, scratch_bytes);
+        ws = scratch;
       } else if (stream_workspace(s, cnt_bytes + part_bytes, &ws) != QGEMM_OK) {
         ws = nullptr;  // e.g. under graph capture: run the last round unsplit
       }
@@ -963,6 +967,44 @@ qgemm_status launch_bf16_gemm_nk(qgemm_stream_s* s, const void* A, const void* B
                                  int ldc, int M, int N, int K, int a_repeat) {
   return launch_tc_gemm(s, 1, A, B, 0, nullptr, nullptr, out, QGEMM_BF16, ldc, M, N, 2 * K,
                         nullptr, a_repeat);
+}
+
+// ---- the W8A8 GEMM with a static scratch (qgemm_w8a8_gemm_static_scratch) ----------
+// The last-wave split's counters and partial tiles live in this file-scope device
+// array instead of scratch made on the stream handle, so the call never allocates.
+// 4 KiB of counters (up to 512 CTA pairs) + 20 MiB of partial tiles: four int32
+// 128 x 256 parts per half of up to 20 leftover pair tiles, the most a four-way split
+// can leave on a GPU of up to 160 SMs.  Shared by every call on the device.
+constexpr size_t STATIC_CNT_BYTES = 4096;
+constexpr size_t STATIC_SCRATCH_BYTES = STATIC_CNT_BYTES + ((size_t)20 << 20);
+static __device__ __align__(256) uint8_t g_static_scratch[STATIC_SCRATCH_BYTES];
+
+static qgemm_status static_scratch(const qgemm_device_s* d, void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  if (d->ordinal < 0 || d->ordinal >= 64) return fail(QGEMM_ERR_UNSUPPORTED, "device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[d->ordinal]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    addr[d->ordinal] = p;
+  }
+  *out = addr[d->ordinal];
+  return QGEMM_OK;
+}
+
+qgemm_status launch_w8a8_tcgen05_static(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
+                                        const float* sA, const float* sB, void* out, int out_dtype,
+                                        int ldc, int M, int N, int K, int32_t* acc) {
+  void* ws = nullptr;
+  const qgemm_status st = static_scratch(s->dev, &ws);
+  if (st != QGEMM_OK) return st;
+  // the counters must be zero when the kernel starts
+  const cudaError_t e = cudaMemsetAsync(ws, 0, STATIC_CNT_BYTES, s->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the static scratch counters");
+  return launch_tc_gemm(s, 0, A, B, b_kn, sA, sB, out, out_dtype, ldc, M, N, K, acc, 1, ws,
+                        STATIC_SCRATCH_BYTES);
 }
 
 }  // namespace qg

@@ -82,6 +82,8 @@ SIGNATURES = {
     "qgemm_weight_only_quantize_per_channel": (_S, [_P, _U64, _U64, _U64, _U64, _I, _I]),
     "qgemm_dequantize": (_S, [_P, _U64, _U64, _U64, _I, _I]),
     "qgemm_w8a8_gemm": (_S, [_P, _U64, _U64, _I, _U64, _U64, _U64, _I, _I, _I, _I, _I, _U64, _I]),
+    "qgemm_w8a8_gemm_static_scratch": (_S, [_P, _U64, _U64, _I, _U64, _U64, _U64, _I, _I, _I, _I,
+                                             _I, _U64, _I]),
     "qgemm_w4a16_grouped_gemm": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I]),
     "qgemm_w4a16_grouped_gemm_tiled": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I]),
     "qgemm_w4_tiled_bytes": (_S, [_I, _I, ctypes.POINTER(_SZ)]),

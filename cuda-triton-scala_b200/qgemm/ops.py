@@ -68,6 +68,14 @@ class QuantizedGemmOps:
                L.addr(sB), L.addr(out), out_dtype, N if ldc is None else ldc, M, N, K,
                L.addr(acc_i32), algo)
 
+    def w8a8GemmStaticScratch(self, A, B, sA, sB, out, M: int, N: int, K: int, *,
+                              b_layout: int = L.B_KN, out_dtype: int = L.BF16,
+                              ldc: int | None = None, acc_i32=None, algo: int = L.ALGO_AUTO):
+        """w8a8Gemm that never allocates: its split scratch is a static device array."""
+        L.call("qgemm_w8a8_gemm_static_scratch", self._h, L.addr(A), L.addr(B), b_layout,
+               L.addr(sA), L.addr(sB), L.addr(out), out_dtype, N if ldc is None else ldc, M, N,
+               K, L.addr(acc_i32), algo)
+
     def w4a16GemmGrouped(self, x, wq, scales, y, M: int, N: int, K: int, *,
                          zero_point: int = 8, group_size: int = 128):
         """Group-wise W4A16: x bf16 [M,K], wq uint32 [K,N/8] (reference nibble order),

@@ -167,6 +167,25 @@ QGEMM_API qgemm_status qgemm_w8a8_gemm(qgemm_stream_t s, uint64_t A, uint64_t B,
                              uint64_t sA, uint64_t sB, uint64_t out, int out_dtype,
                              int ldc, int M, int N, int K, uint64_t acc_i32, int algo);
 
+/* qgemm_w8a8_gemm for callers that must not allocate device memory during the call
+ * (no counterpart in the reference).  qgemm_w8a8_gemm may make scratch on the stream
+ * handle the first time a shape's last tile round is split along K; this variant
+ * takes that scratch from a 20 MiB static array inside the library instead, so a
+ * serving loop with a fixed memory budget, or a host that accounts for every device
+ * allocation, can call it at any time.  Same arguments, same results (bit for bit).
+ * - Nothing is allocated.  The array's address is looked up once per device, on the
+ *   first call there; make that first call during set-up.
+ * - Its 4 KiB of counters must be zero when a GEMM starts; each call clears them
+ *   on the stream before its kernel (and leaves them zero).
+ * - One array per device: calls whose GEMMs could overlap (different streams, no
+ *   ordering between them) race on it.  Issue them on one stream, or order them.
+ * - A split larger than the array (more than 20 leftover pair tiles, i.e. GPUs with
+ *   more than 160 SMs) is refused with QGEMM_ERR_UNSUPPORTED. */
+QGEMM_API qgemm_status qgemm_w8a8_gemm_static_scratch(qgemm_stream_t s, uint64_t A, uint64_t B,
+                                                      int b_layout, uint64_t sA, uint64_t sB,
+                                                      uint64_t out, int out_dtype, int ldc, int M,
+                                                      int N, int K, uint64_t acc_i32, int algo);
+
 /* Group-wise W4A16 GEMV/GEMM for decode (the w4a16Gemm arithmetic,
  * QuantizedGemmOps.scala:229-245, with a zero point and per-group scales):
  *   x   bf16 [M,K];  wq uint32 [K, N/8]: nibble j of word (k, c) is q[k][8c+j]
