@@ -25,8 +25,10 @@ struct qgemm_stream_s {
   qgemm_device_s* dev = nullptr;
   cudaStream_t stream = nullptr;
   bool owned = false;
-  // Scratch of the split-tile reductions (W4A16 tiled path), allocated by the first
-  // call that needs it on this handle and zeroed then; kernels leave it zeroed.
+  // Scratch of the tcgen05 GEMM's last-wave split (a counter block at offset 0 that
+  // every kernel leaves zeroed, then partial tiles) and of the fp32 GEMM's split
+  // operands; allocated by the first call that needs it on this handle, zeroed then,
+  // and grown (outside graph capture) when a call needs more.
   void* ws = nullptr;
   size_t ws_bytes = 0;
 };
@@ -55,6 +57,48 @@ enum : int {
   DEVERR_TIMEOUT_DRAIN = 4,
 };
 
+// ---- the tcgen05 GEMM (w8a8_tcgen05.cu) ----
+// MMA kinds of the tcgen05 GEMM kernels.
+enum : int { KIND_I8 = 0, KIND_BF16 = 1, KIND_TF32 = 2 };
+
+// One tcgen05 GEMM launch: out[M, ldc] = sum over K segments of A_seg * B_seg^T.
+struct TcArgs {
+  int kind = KIND_I8;
+  const void* A = nullptr;  // [M rows, a_pitch bytes], K-major
+  const void* B = nullptr;  // [N rows, b_pitch bytes] K-major, or [K, N] int8 (b_kn)
+  int b_kn = 0;             // B in [K,N] (MN-major operand): KIND_I8 with nseg = 1 only
+  int M = 0, N = 0;
+  int K = 0;                // bytes of K in one segment
+  // nseg segments of ceil(K / 128) k-blocks each.  Segment s reads the first
+  // ceil(K / 128) * 128 bytes of A's rows, or the next as many when bit s of a_seg is
+  // set; likewise for B with b_seg.  Bytes past K inside a block must be zero (TMA
+  // fills zeros past the row's end).
+  int nseg = 1;
+  uint32_t a_seg = 0, b_seg = 0;
+  uint64_t a_pitch = 0, b_pitch = 0;  // row pitch in bytes, also the rows' extent (0: K)
+  const float* sA = nullptr;          // KIND_I8: y = (float(acc) * sB[n]) * sA[m]
+  const float* sB = nullptr;
+  int32_t* acc = nullptr;             // KIND_I8: optional int32 accumulators [M, N]
+  void* out = nullptr;
+  int out_dtype = QGEMM_F32;
+  int ldc = 0;
+  // bf16 / tf32 kinds: v = acc; v = alpha * v (ep_alpha); v += bias[n] (bias);
+  // v += beta * out[m, n] (ep_beta, fp32 out), each step rounded on its own.
+  float alpha = 1.f, beta = 0.f;
+  const float* bias = nullptr;
+  int ep_alpha = 0, ep_beta = 0;
+  // Device word read by the epilogue: non-zero -> store nothing.
+  const int* skip_flag = nullptr;
+  // Last-wave split scratch: counters (zero) at offset 0, partial tiles after them;
+  // null: the stream handle's scratch.
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+};
+qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a);
+// Scratch bytes a launch of this shape uses for its last-wave split: the counter block
+// (always counted) and the partial tiles.
+size_t tc_gemm_scratch_bytes(const qgemm_device_s* d, int M, int N, int num_k_blocks);
+
 // ---- launchers (each returns a status and never throws) ----
 qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
                                  const float* sA, const float* sB, void* out, int out_dtype,
@@ -72,6 +116,16 @@ bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int
 // multiple of 64, and out = sum_i A * B_i^T.
 qgemm_status launch_bf16_gemm_nk(qgemm_stream_s* s, const void* A, const void* B, void* out,
                                  int ldc, int M, int N, int K, int a_repeat = 1);
+// fp32 entry points (f32_gemm.cu).  C [M,N] = A [M,K] x B [K,N], all fp32 row-major,
+// through three tf32 tensor-core products per fp32 product; the split operands live in
+// the stream's scratch after the GEMM's counter block.
+enum : int { F32_MATMUL = 0, F32_MATMUL_BIAS = 1, F32_SGEMM = 2 };
+size_t f32_gemm_workspace_bytes(const qgemm_device_s* d, int M, int N, int K);
+qgemm_status launch_f32_gemm(qgemm_stream_s* s, const float* A, const float* B,
+                             const float* bias, float* C, int M, int N, int K, float alpha,
+                             float beta, int mode);
+qgemm_status launch_f32_gemv(qgemm_stream_s* s, const float* A, const float* x, float* y, int M,
+                             int N);
 qgemm_status launch_w8a8_simt(qgemm_stream_s* s, const int8_t* A, const int8_t* B, int b_kn,
                               const float* sA, const float* sB, void* out, int out_dtype,
                               int ldc, int M, int N, int K, int32_t* acc);

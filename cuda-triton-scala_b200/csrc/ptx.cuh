@@ -416,5 +416,37 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);    // M / 16
 }
 
+// Instruction descriptor for kind::tf32: tf32 A and B (fp32 words whose low 13 mantissa
+// bits the tensor core does not use), fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4)                        // D format: f32
+         | (2u << 7)                      // A format: tf32
+         | (2u << 10)                     // B format: tf32
+         | ((uint32_t)(N >> 3) << 17)     // N / 8
+         | ((uint32_t)(M >> 4) << 24);    // M / 16
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], tf32 x tf32 -> fp32, K = 8, one CTA.
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The CTA-pair form of umma_tf32 (issued by one thread of the even CTA).
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 }  // namespace ptx
 }  // namespace qg

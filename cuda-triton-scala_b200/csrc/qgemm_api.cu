@@ -634,6 +634,53 @@ qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src, uint64_t dst, i
                               reinterpret_cast<int8_t*>(dst), K, N);
 }
 
+// ---- fp32 entry points (MatrixOps / BLASOps) ----
+
+static qgemm_status f32_gemm_entry(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t bias,
+                                   uint64_t C, int M, int N, int K, float alpha, float beta,
+                                   int mode) {
+  QG_TRY(enter(s));
+  QG_TRY(check_dims(M, N, K));
+  if (M == 0 || N == 0) return QGEMM_OK;
+  if (!s->dev->tcgen05) return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
+  if (K > 0) { QG_TRY(need(A, "A")); QG_TRY(need(B, "B")); }
+  QG_TRY(need(C, "C"));
+  if (mode == F32_MATMUL_BIAS) QG_TRY(need(bias, "bias"));
+  QG_TRY(need_align(A, 4, "A")); QG_TRY(need_align(B, 4, "B"));
+  QG_TRY(need_align(C, 4, "C")); QG_TRY(need_align(bias, 4, "bias"));
+  if (K > 0 && (M > (1 << 28) / ((K + 31) / 32) || N > (1 << 28) / ((K + 31) / 32)))
+    return fail(QGEMM_ERR_UNSUPPORTED, "a split operand of M=%d N=%d K=%d would exceed 64 GiB", M, N, K);
+  return launch_f32_gemm(s, reinterpret_cast<const float*>(A), reinterpret_cast<const float*>(B),
+                         reinterpret_cast<const float*>(bias), reinterpret_cast<float*>(C), M, N,
+                         K, alpha, beta, mode);
+}
+
+qgemm_status qgemm_matmul_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t C, int M, int N,
+                              int K) {
+  return f32_gemm_entry(s, A, B, 0, C, M, N, K, 1.f, 0.f, F32_MATMUL);
+}
+
+qgemm_status qgemm_matmul_add_bias_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t bias,
+                                       uint64_t C, int M, int N, int K) {
+  return f32_gemm_entry(s, A, B, bias, C, M, N, K, 1.f, 0.f, F32_MATMUL_BIAS);
+}
+
+qgemm_status qgemm_sgemm(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t C, int M, int N, int K,
+                         float alpha, float beta) {
+  return f32_gemm_entry(s, A, B, 0, C, M, N, K, alpha, beta, F32_SGEMM);
+}
+
+qgemm_status qgemm_gemv_f32(qgemm_stream_t s, uint64_t A, uint64_t x, uint64_t y, int M, int N) {
+  QG_TRY(enter(s));
+  QG_TRY(check_dims(M, N, 0));
+  if (M == 0) return QGEMM_OK;
+  if (N > 0) { QG_TRY(need(A, "A")); QG_TRY(need(x, "x")); }
+  QG_TRY(need(y, "y"));
+  QG_TRY(need_align(A, 4, "A")); QG_TRY(need_align(x, 4, "x")); QG_TRY(need_align(y, 4, "y"));
+  return launch_f32_gemv(s, reinterpret_cast<const float*>(A), reinterpret_cast<const float*>(x),
+                         reinterpret_cast<float*>(y), M, N);
+}
+
 // ---- by-name launch ----
 
 qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name, const uint64_t* b,
@@ -677,6 +724,18 @@ qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name, const uint
   if (!strcmp(name, "dequantize")) {
     QG_TRY(want(3, 2));
     return qgemm_dequantize(s, b[0], b[1], b[2], v[0], v[1]);
+  }
+  if (!strcmp(name, "matmul")) {
+    QG_TRY(want(3, 3));
+    return qgemm_matmul_f32(s, b[0], b[1], b[2], v[0], v[1], v[2]);
+  }
+  if (!strcmp(name, "matmulAddBias")) {
+    QG_TRY(want(4, 3));
+    return qgemm_matmul_add_bias_f32(s, b[0], b[1], b[2], b[3], v[0], v[1], v[2]);
+  }
+  if (!strcmp(name, "gemv")) {
+    QG_TRY(want(3, 2));
+    return qgemm_gemv_f32(s, b[0], b[1], b[2], v[0], v[1]);
   }
   return fail(QGEMM_ERR_INVALID_ARG, "unknown kernel name '%s'", name);
 }

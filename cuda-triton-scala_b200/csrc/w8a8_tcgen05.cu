@@ -44,7 +44,7 @@ namespace w8a8 {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
-constexpr int UMMA_K = 32;
+constexpr int UMMA_K = 32;  // bytes of K per MMA: 32 int8, 16 bf16 or 8 tf32 values
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK;                   // 16 KB
 constexpr int B_BYTES = BN * BK;                   // 32 KB
@@ -77,17 +77,31 @@ struct Params {
   int out_vec;     // out base 16-byte aligned and rows a multiple of 16 bytes
   int acc_vec;     // same for the int32 accumulator output
   int tma_store;   // the output is written with TMA bulk tensor stores (needs out_vec)
-  int bf16;        // 1: A and B are bf16 (K counted in bytes), fp32 accumulators written
-                   // as they are (no scales, no int32 output)
-  int a_kblocks;   // k-block b of A is read at b % a_kblocks (A repeated along K);
-                   // equal to num_k_blocks for an ordinary product
+  int fp_acc;      // 1: bf16 or tf32 operands (K counted in bytes), fp32 accumulators;
+                   // no scales and no int32 output, the fp32 epilogue below instead
+  // K is walked in segments of seg_kblocks k-blocks (one segment for an ordinary
+  // product).  K-block r of segment s reads k-block r of A's row, or k-block
+  // seg_kblocks + r when bit s of a_seg is set; likewise for B with b_seg.  The product
+  // is the sum over the segments.
+  int seg_kblocks;
+  uint32_t a_seg, b_seg;
+  // fp32 epilogue (fp_acc): v = acc; v = alpha * v (ep_alpha); v = v + bias[n] (bias);
+  // v = v + beta * out[m, n] (ep_beta: out is read before it is written), each step
+  // rounded on its own.
+  float alpha, beta;
+  const float* bias;
+  int ep_alpha, ep_beta;
+  // When set and *skip_flag != 0 at the epilogue, no output is stored (a later kernel
+  // writes the whole output instead).
+  const int* skip_flag;
   // Last-wave split of the CTA-pair kernel: the first split_w tiles are done whole,
   // one per pair per round; each of the remaining tiles is cut along K into split_s
-  // parts that run on different pairs at once.  A part writes its int32 partial sums
-  // to `part`; the part that counts in last on `cnt` adds them all (in part order;
-  // integer sums, so any order gives the same bits) and runs the epilogue.
+  // parts that run on different pairs at once.  A part writes its partial sums (int32,
+  // or fp32 with fp_acc) to `part`; the part that counts in last on `cnt` adds them all
+  // in part order (a fixed order, so the fp32 sums are deterministic too) and runs the
+  // epilogue.
   int split_w, split_s;
-  int32_t* part;   // [(tail tile * 2 + rank) * split_s + part][128 x 256 int32, part_index]
+  int32_t* part;   // [(tail tile * 2 + rank) * split_s + part][128 x 256 words, part_index]
   int* cnt;        // [tail tile * 2 + rank], zero between launches
 };
 
@@ -113,6 +127,44 @@ __device__ __forceinline__ bool pair_item(const Params& p, int pair, int npairs,
   return true;
 }
 
+
+// The k-blocks of A and of B that k-block kb of the K walk reads.
+__device__ __forceinline__ void seg_blocks(const Params& p, int kb, int& akb, int& bkb) {
+  const int s = kb / p.seg_kblocks;
+  const int r = kb - s * p.seg_kblocks;
+  akb = r + (int)((p.a_seg >> s) & 1u) * p.seg_kblocks;
+  bkb = r + (int)((p.b_seg >> s) & 1u) * p.seg_kblocks;
+}
+
+// The fp32 epilogue steps after the accumulator (fp_acc): 32 columns n0.. of row `row`.
+__device__ __forceinline__ void fp_epilogue(const Params& p, int row, int n0, float (&v)[32]) {
+  if (p.ep_alpha) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(p.alpha, v[j]);
+  }
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < p.N) v[j] = __fadd_rn(v[j], __ldg(p.bias + n0 + j));
+  }
+  if (p.ep_beta && row < p.M) {
+    const float* c = reinterpret_cast<const float*>(p.out) + (size_t)row * p.ldc + n0;
+    if (n0 + 32 <= p.N && p.out_vec) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 o = *reinterpret_cast<const float4*>(c + j);
+        v[j] = __fadd_rn(v[j], __fmul_rn(p.beta, o.x));
+        v[j + 1] = __fadd_rn(v[j + 1], __fmul_rn(p.beta, o.y));
+        v[j + 2] = __fadd_rn(v[j + 2], __fmul_rn(p.beta, o.z));
+        v[j + 3] = __fadd_rn(v[j + 3], __fmul_rn(p.beta, o.w));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) v[j] = __fadd_rn(v[j], __fmul_rn(p.beta, c[j]));
+    }
+  }
+}
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
   const int group_size = GROUP_M * p.num_n_blocks;
@@ -144,7 +196,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
   if (row >= p.M || n0 >= p.N) return;
   const bool full = (n0 + 32 <= p.N);
   float sb[32];
-  if (p.bf16) {
+  if (p.fp_acc) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) sb[j] = 1.f;
   } else if (full && ((reinterpret_cast<uintptr_t>(p.sB + n0) & 15) == 0)) {
@@ -171,8 +223,9 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j)
-    v[j] = p.bf16 ? __uint_as_float(r[j])
-                  : __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
+    v[j] = p.fp_acc ? __uint_as_float(r[j])
+                    : __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
+  if (p.fp_acc) fp_epilogue(p, row, n0, v);
   if (p.out_dtype == QGEMM_BF16) {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldc + n0;
     if (full && p.out_vec) {
@@ -219,18 +272,25 @@ __device__ __forceinline__ size_t part_index(int c, int v, int rl) {
 }
 
 // With `parts` set, the accumulators are not read from TMEM but summed from `nparts`
-// partial tiles, `part_stride` ints apart (in part order).
+// partial tiles, `part_stride` words apart, in part order: int32 sums, or fp32 sums
+// when `fp` (the words are then fp32 accumulators).
+__device__ __forceinline__ uint32_t add_word(uint32_t a, int b, bool fp) {
+  return fp ? __float_as_uint(__fadd_rn(__uint_as_float(a), __int_as_float(b))) : a + (uint32_t)b;
+}
+
 __device__ __forceinline__ void sum_parts(const int32_t* parts, int nparts, size_t part_stride,
-                                          int rl, int col, uint32_t (&r)[32]) {
+                                          int rl, int col, bool fp, uint32_t (&r)[32]) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) r[j] = 0u;
+  for (int j = 0; j < 32; ++j) r[j] = 0u;  // also fp32 +0
   for (int pp = 0; pp < nparts; ++pp) {
     const int4* src = reinterpret_cast<const int4*>(parts + pp * part_stride);
 #pragma unroll
     for (int v = 0; v < 8; ++v) {
       const int4 x = __ldcg(src + part_index(col / 32, v, rl));
-      r[4 * v] += (uint32_t)x.x; r[4 * v + 1] += (uint32_t)x.y;
-      r[4 * v + 2] += (uint32_t)x.z; r[4 * v + 3] += (uint32_t)x.w;
+      r[4 * v] = add_word(r[4 * v], x.x, fp);
+      r[4 * v + 1] = add_word(r[4 * v + 1], x.y, fp);
+      r[4 * v + 2] = add_word(r[4 * v + 2], x.z, fp);
+      r[4 * v + 3] = add_word(r[4 * v + 3], x.w, fp);
     }
   }
 }
@@ -243,7 +303,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
                                               size_t part_stride = 0) {
   const int row = row0 + q * 32 + lane;
   const int rl = q * 32 + lane;  // row within the staging block
-  const float sa = (!p.bf16 && row < p.M) ? __ldg(p.sA + row) : 0.f;
+  const float sa = (!p.fp_acc && row < p.M) ? __ldg(p.sA + row) : 0.f;
+  const bool skip = p.skip_flag != nullptr && *reinterpret_cast<const volatile int*>(p.skip_flag) != 0;
   if (!p.tma_store) {
 #pragma unroll 1
     for (int c = 0; c < 256 / 32; ++c) {
@@ -251,12 +312,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       __syncwarp();
       if (!ok) return;
       if (parts) {
-        sum_parts(parts, nparts, part_stride, rl, c * 32, r);
+        sum_parts(parts, nparts, part_stride, rl, c * 32, p.fp_acc != 0, r);
       } else {
         ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + c * 32, r);
         ptx::tmem_wait_ld();
       }
-      store_chunk(p, row, n0 + c * 32, sa, r);
+      if (!skip) store_chunk(p, row, n0 + c * 32, sa, r);
     }
     return;
   }
@@ -274,7 +335,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       const int nc = n0 + ch * cwe + sub * 32;
       __syncwarp();
       if (ok && parts) {
-        sum_parts(parts, nparts, part_stride, rl, ch * cwe + sub * 32, r);
+        sum_parts(parts, nparts, part_stride, rl, ch * cwe + sub * 32, p.fp_acc != 0, r);
       } else if (ok) {
         ptx::tmem_ld_32x32b_x32(
             tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + (uint32_t)(ch * cwe + sub * 32), r);
@@ -284,7 +345,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         for (int j = 0; j < 32; ++j) r[j] = 0u;  // a wait ran out: keep the barrier sequence
       }
       float sb[32];
-      if (p.bf16) {
+      if (p.fp_acc) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) sb[j] = 1.f;
       } else if (nc + 32 <= p.N && ((reinterpret_cast<uintptr_t>(p.sB + nc) & 15) == 0)) {
@@ -304,8 +365,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        v[j] = p.bf16 ? __uint_as_float(r[j])
-                      : __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
+        v[j] = p.fp_acc ? __uint_as_float(r[j])
+                        : __fmul_rn(__fmul_rn(__int2float_rn((int)r[j]), sb[j]), sa);
+      if (p.fp_acc) fp_epilogue(p, row, nc, v);
       if (bf16) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {  // four 16-byte pieces = 32 bf16
@@ -329,16 +391,16 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
     }
     ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
     ptx::named_bar_sync(1, 128);
-    if (elected) {
+    if (elected && !skip) {
       ptx::tma_store_2d(tmO, buf, n0 + ch * cwe, row0);
       ptx::bulk_commit_group();
     }
   }
 }
 
-// BF16 selects the MMA kind at compile time: a run-time choice inside the issue loop
+// KIND selects the MMA kind at compile time: a run-time choice inside the issue loop
 // cost a fifth of the tensor throughput.
-template <bool BF16>
+template <int KIND>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -409,13 +471,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           const uint32_t sa = base + stage * STAGE_BYTES;
           const uint32_t sb = sa + A_BYTES;
+          int akb, bkb;
+          seg_blocks(p, kb, akb, bkb);
           ptx::mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
-          ptx::tma_load_2d(sa, &tmA, full_bar(stage), (kb % p.a_kblocks) * BK, mb * BM);
+          ptx::tma_load_2d(sa, &tmA, full_bar(stage), akb * BK, mb * BM);
           if (p.b_kn) {
             ptx::tma_load_2d(sb, &tmB, full_bar(stage), nb * BN, kb * BK);
             ptx::tma_load_2d(sb + B_BYTES / 2, &tmB, full_bar(stage), nb * BN + 128, kb * BK);
           } else {
-            ptx::tma_load_2d(sb, &tmB, full_bar(stage), kb * BK, nb * BN);
+            ptx::tma_load_2d(sb, &tmB, full_bar(stage), bkb * BK, nb * BN);
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -434,7 +498,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = BF16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc = KIND == KIND_BF16   ? ptx::idesc_bf16(BM, BN)
+                             : KIND == KIND_TF32 ? ptx::idesc_tf32(BM, BN)
+                                                 : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -472,8 +538,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             } else {
               bdesc = ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
             }
-            if constexpr (BF16)
+            if constexpr (KIND == KIND_BF16)
               ptx::umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else if constexpr (KIND == KIND_TF32)
+              ptx::umma_tf32(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
             else
               ptx::umma_i8(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
@@ -546,7 +614,7 @@ static_assert(STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024 <= SMEM_BYTES,
               "shared memory budget");
 }  // namespace pair
 
-template <bool BF16>
+template <int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
@@ -623,12 +691,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t sa = base + stage * STAGE_BYTES;
           const uint32_t sb = sa + A_BYTES;
           const uint32_t fb = ptx::map_to_rank(full_bar(stage), 0);
+          int akb, bkb;
+          seg_blocks(p, kb, akb, bkb);
           if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
-          ptx::tma_load_2d_pair(sa, &tmA, fb, (kb % p.a_kblocks) * BK, mb * BM + (int)rank * 128);
+          ptx::tma_load_2d_pair(sa, &tmA, fb, akb * BK, mb * BM + (int)rank * 128);
           if (p.b_kn)
             ptx::tma_load_2d_pair(sb, &tmB, fb, nb * BN + (int)rank * 128, kb * BK);
           else
-            ptx::tma_load_2d_pair(sb, &tmB, fb, kb * BK, nb * BN + (int)rank * 128);
+            ptx::tma_load_2d_pair(sb, &tmB, fb, bkb * BK, nb * BN + (int)rank * 128);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -646,7 +716,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA) ----------------
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = BF16 ? ptx::idesc_bf16(BM, BN) : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc = KIND == KIND_BF16   ? ptx::idesc_bf16(BM, BN)
+                             : KIND == KIND_TF32 ? ptx::idesc_tf32(BM, BN)
+                                                 : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -679,8 +751,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const uint64_t bdesc = p.b_kn ? ptx::smem_desc_sw128(sb + kk * UMMA_K * 128, B_BYTES, 1024)
                                           : ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
             const uint32_t accum = (kb != kb0 || kk != 0) ? 1u : 0u;
-            if constexpr (BF16)
+            if constexpr (KIND == KIND_BF16)
               ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, accum);
+            else if constexpr (KIND == KIND_TF32)
+              ptx::umma_tf32_pair(d_tmem, adesc, bdesc, idesc, accum);
             else
               ptx::umma_i8_pair(d_tmem, adesc, bdesc, idesc, accum);
           }
@@ -824,49 +898,103 @@ bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int
   return true;
 }
 
-// The tcgen05 GEMM behind both the W8A8 and the bf16 entry points.  K is in bytes of
-// a row of A (and of B in the [N,K] layout): int8 elements, or twice the bf16 count.
-// With a_repeat = r > 1, each row of B holds r blocks of ceil(K / 128) * 128 bytes
-// (zero past K) and A is read r times along K: out = sum_i A * B_i^T.
-// `scratch`: caller-provided scratch for the last-wave split (null: the stream handle's
-// own scratch, made on first use).
-static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, const void* B,
-                                   int b_kn, const float* sA, const float* sB, void* out,
-                                   int out_dtype, int ldc, int M, int N, int K, int32_t* acc,
-                                   int a_repeat = 1, void* scratch = nullptr,
-                                   size_t scratch_bytes = 0) {
+// Grid and last-wave split of one tcgen05 GEMM launch; a function of the shape and the
+// device only, so callers can size the scratch before the launch.
+struct TcPlan {
+  bool use_pair;
+  int grid;
+  int num_tiles;
+  int split_w, split_s;   // as in Params; split_s = 1: no split
+  size_t cnt_bytes;       // counter block at the start of the scratch
+  size_t part_bytes;      // partial tiles after it (0: no split)
+};
+
+static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks) {
   using namespace w8a8;
+  TcPlan t;
   // CTA pairs (256 x 256 tiles) whenever the problem has at least one full pair tile.
-  const bool use_pair = M >= 256 && N >= 256 && s->dev->sm_count >= 2;
+  t.use_pair = M >= 256 && N >= 256 && d->sm_count >= 2;
+  const int bm = t.use_pair ? pair::BM : BM, bn = t.use_pair ? pair::BN : BN;
+  t.num_tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+  t.split_w = t.num_tiles;
+  t.split_s = 1;
+  // The counter block has one fixed size on a device (counters for up to
+  // 2 * max_pairs half-tiles; rest < max_pairs) and is counted in every plan, so that
+  // callers which carve their own buffers out of the stream's scratch never place them
+  // over it: the counters must sit at the same place in every call, as they are zero
+  // between calls only because each call returns the ones it used to zero.
+  const int max_pairs = d->sm_count / 2 > 0 ? d->sm_count / 2 : 1;
+  t.cnt_bytes = ((size_t)max_pairs * 2 * sizeof(int) + 255) & ~(size_t)255;
+  t.part_bytes = 0;
+  if (!t.use_pair) {
+    t.grid = t.num_tiles < d->sm_count ? t.num_tiles : d->sm_count;
+    return t;
+  }
+  const int pairs = t.num_tiles < max_pairs ? t.num_tiles : max_pairs;
+  t.grid = 2 * pairs;
+  // Last-wave split: when the final round would leave at least three quarters of the
+  // pairs idle, cut each leftover tile along K into 4 parts (at least two k-blocks
+  // each).  Measured: a K part runs at about 0.27 of a tile plus its share of the
+  // k-blocks and the partial sums add about a quarter of a tile, so two-way splits
+  // (4096^3: 34 leftover tiles on 74 pairs) lose and four-way ones win.
+  const int rounds = t.num_tiles / pairs, rest = t.num_tiles - rounds * pairs;
+  int parts = (rest > 0 && rest * 4 <= pairs) ? 4 : 1;
+  while (parts > 1 && num_k_blocks / parts < 2) --parts;
+  if (parts < 4) parts = 1;
+  if (rounds >= 1 && parts >= 2) {
+    t.split_w = rounds * pairs;
+    t.split_s = parts;
+    t.part_bytes = (size_t)rest * 2 * parts * 128 * 256 * sizeof(int32_t);
+  }
+  return t;
+}
+
+size_t tc_gemm_scratch_bytes(const qgemm_device_s* d, int M, int N, int num_k_blocks) {
+  const TcPlan t = tc_plan(d, M, N, num_k_blocks);
+  return t.cnt_bytes + t.part_bytes;
+}
+
+// The tcgen05 GEMM behind the W8A8, bf16 and fp32 entry points (TcArgs in internal.h).
+qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
+  using namespace w8a8;
+  if (a.kind < KIND_I8 || a.kind > KIND_TF32) return fail(QGEMM_ERR_INVALID_ARG, "MMA kind %d", a.kind);
+  const int M = a.M, N = a.N, K = a.K;
+  const uint64_t kblk = (uint64_t)((K + BK - 1) / BK);
+  const int num_k_blocks = (int)kblk * a.nseg;
+  const TcPlan t = tc_plan(s->dev, M, N, num_k_blocks);
+  const bool use_pair = t.use_pair;
   const int bm = use_pair ? pair::BM : BM, bn = use_pair ? pair::BN : BN;
+  const uint64_t a_pitch = a.a_pitch ? a.a_pitch : (uint64_t)K;
+  const uint64_t b_pitch = a.b_pitch ? a.b_pitch : (uint64_t)K;
   CUtensorMap tmA, tmB;
-  if (!make_map_u8(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)K, BK, 128))
+  if (!make_map_u8(&tmA, a.A, a_pitch, (uint64_t)M, a_pitch, BK, 128))
     return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for A [%d,%d]", M, K);
   // B boxes: [K,N] -> 128 columns x 128 k-rows; [N,K] -> 128 k-bytes x (bn per CTA) rows.
   const uint32_t nk_rows = use_pair ? 128 : BN;
-  // B row length in bytes: with A repeated, each of the a_repeat blocks of a B row is
-  // padded to whole k-blocks so that block i starts at k-block i * ceil(K / BK)
-  const uint64_t kblk = (uint64_t)((K + BK - 1) / BK);
-  const uint64_t kb_bytes = a_repeat > 1 ? kblk * BK * a_repeat : (uint64_t)K;
-  bool okb = b_kn ? make_map_u8(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)N, 128, BK)
-                  : make_map_u8(&tmB, B, kb_bytes, (uint64_t)N, kb_bytes, BK, nk_rows);
+  bool okb = a.b_kn ? make_map_u8(&tmB, a.B, (uint64_t)N, (uint64_t)K, (uint64_t)N, 128, BK)
+                    : make_map_u8(&tmB, a.B, b_pitch, (uint64_t)N, b_pitch, BK, nk_rows);
   if (!okb) return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for B");
 
   Params p;
-  p.M = M; p.N = N; p.K = K; p.ldc = ldc;
-  p.out_dtype = out_dtype;
-  p.b_kn = b_kn;
+  p.M = M; p.N = N; p.K = K; p.ldc = a.ldc;
+  p.out_dtype = a.out_dtype;
+  p.b_kn = a.b_kn;
   p.num_m_blocks = (M + bm - 1) / bm;
   p.num_n_blocks = (N + bn - 1) / bn;
-  p.a_kblocks = (K + BK - 1) / BK;
-  p.num_k_blocks = p.a_kblocks * a_repeat;
-  p.num_tiles = p.num_m_blocks * p.num_n_blocks;
-  p.sA = sA; p.sB = sB; p.out = out; p.acc = acc;
-  p.bf16 = bf16;
+  p.num_k_blocks = num_k_blocks;
+  p.seg_kblocks = (int)kblk;
+  p.a_seg = a.a_seg;
+  p.b_seg = a.b_seg;
+  p.num_tiles = t.num_tiles;
+  p.sA = a.sA; p.sB = a.sB; p.out = a.out; p.acc = a.acc;
+  p.fp_acc = a.kind != KIND_I8;
+  p.alpha = a.alpha; p.beta = a.beta; p.bias = a.bias;
+  p.ep_alpha = a.ep_alpha; p.ep_beta = a.ep_beta;
+  p.skip_flag = a.skip_flag;
   p.err = s->dev->d_err;
-  const int esize = out_dtype == QGEMM_BF16 ? 2 : 4;
-  p.out_vec = aligned((uint64_t)out, 16) && ((uint64_t)ldc * esize) % 16 == 0;
-  p.acc_vec = acc != nullptr && aligned((uint64_t)acc, 16) && N % 4 == 0;
+  const int esize = a.out_dtype == QGEMM_BF16 ? 2 : 4;
+  p.out_vec = aligned((uint64_t)a.out, 16) && ((uint64_t)a.ldc * esize) % 16 == 0;
+  p.acc_vec = a.acc != nullptr && aligned((uint64_t)a.acc, 16) && N % 4 == 0;
   // Output tensor map for TMA stores: [M rows, N columns] with row pitch ldc, boxes of
   // 128 rows x 128 bytes, 128-byte swizzle (matching the staging buffer).
   CUtensorMap tmO;
@@ -875,75 +1003,56 @@ static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, c
   if (p.out_vec) {
     EncodeTiledFn enc = get_encode_fn();
     cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
-    cuuint64_t strides[1] = {(cuuint64_t)ldc * esize};
+    cuuint64_t strides[1] = {(cuuint64_t)a.ldc * esize};
     cuuint32_t box[2] = {(cuuint32_t)(128 / esize), 128};
     cuuint32_t estr[2] = {1, 1};
-    if (enc && enc(&tmO, out_dtype == QGEMM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                   2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    if (enc && enc(&tmO, a.out_dtype == QGEMM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                   2, a.out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
       p.tma_store = 1;
   }
 
   using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params);
-  const Kern kern = use_pair ? (bf16 ? w8a8_tcgen05_pair_kernel<true> : w8a8_tcgen05_pair_kernel<false>)
-                             : (bf16 ? w8a8_tcgen05_kernel<true> : w8a8_tcgen05_kernel<false>);
+  static const Kern kerns[2][3] = {
+      {w8a8_tcgen05_kernel<KIND_I8>, w8a8_tcgen05_kernel<KIND_BF16>, w8a8_tcgen05_kernel<KIND_TF32>},
+      {w8a8_tcgen05_pair_kernel<KIND_I8>, w8a8_tcgen05_pair_kernel<KIND_BF16>,
+       w8a8_tcgen05_pair_kernel<KIND_TF32>}};
+  const Kern kern = kerns[use_pair ? 1 : 0][a.kind];
   const int smem = use_pair ? pair::SMEM_BYTES : SMEM_BYTES;
-  static bool attr_set[64][2][2] = {};
+  static bool attr_set[64][2][3] = {};
   const int ord = s->dev->ordinal;
-  if (ord < 0 || ord >= 64 || !attr_set[ord][use_pair][bf16 ? 1 : 0]) {
+  if (ord < 0 || ord >= 64 || !attr_set[ord][use_pair][a.kind]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8a8_tcgen05)");
-    if (ord >= 0 && ord < 64) attr_set[ord][use_pair][bf16 ? 1 : 0] = true;
+    if (ord >= 0 && ord < 64) attr_set[ord][use_pair][a.kind] = true;
   }
-  int grid;
-  p.split_w = p.num_tiles;
+  p.split_w = t.num_tiles;
   p.split_s = 1;
   p.part = nullptr;
   p.cnt = nullptr;
-  if (use_pair) {
-    const int max_pairs = s->dev->sm_count / 2;
-    const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
-    grid = 2 * pairs;
-    // Last-wave split: when the final round would leave at least three quarters of the
-    // pairs idle, cut each leftover tile along K into 4 parts (at least two k-blocks
-    // each).  Measured: a K part runs at about 0.27 of a tile plus its share of the
-    // k-blocks and the partial sums add about a quarter of a tile, so two-way splits
-    // (4096^3: 34 leftover tiles on 74 pairs) lose and four-way ones win.
-    const int rounds = p.num_tiles / pairs, rest = p.num_tiles - rounds * pairs;
-    int parts = (rest > 0 && rest * 4 <= pairs) ? 4 : 1;
-    while (parts > 1 && p.num_k_blocks / parts < 2) --parts;
-    if (parts < 4) parts = 1;
-    if (rounds >= 1 && parts >= 2) {
-      // Scratch layout, fixed for every call on the handle: counters for up to
-      // 2 * max_pairs half-tiles (rest < max_pairs), then the partial sums.  The counters
-      // must sit at the same place in every call: they are zero between calls only
-      // because each call returns the ones it used to zero.
-      void* ws = nullptr;
-      const size_t part_bytes = (size_t)rest * 2 * parts * 128 * 256 * sizeof(int32_t);
-      const size_t cnt_bytes = ((size_t)max_pairs * 2 * sizeof(int) + 255) & ~(size_t)255;
-      if (scratch) {
-        if (scratch_bytes < cnt_bytes + part_bytes)
-          return fail(QGEMM_ERR_UNSUPPORTED,
-                      "this shape's last-wave split needs %zu bytes of scratch; the static "
-                      "scratch holds %zu", cnt_bytes + part_bytes, scratch_bytes);
-        ws = scratch;
-      } else if (stream_workspace(s, cnt_bytes + part_bytes, &ws) != QGEMM_OK) {
-        ws = nullptr;  // e.g. under graph capture: run the last round unsplit
-      }
-      if (ws) {
-        p.split_w = rounds * pairs;
-        p.split_s = parts;
-        p.cnt = static_cast<int*>(ws);
-        p.part = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + cnt_bytes);
-      }
+  if (t.split_s > 1) {
+    const size_t need = t.cnt_bytes + t.part_bytes;
+    void* ws = nullptr;
+    if (a.scratch) {
+      if (a.scratch_bytes < need)
+        return fail(QGEMM_ERR_UNSUPPORTED,
+                    "this shape's last-wave split needs %zu bytes of scratch; the given "
+                    "scratch holds %zu", need, a.scratch_bytes);
+      ws = a.scratch;
+    } else if (stream_workspace(s, need, &ws) != QGEMM_OK) {
+      ws = nullptr;  // e.g. under graph capture: run the last round unsplit
     }
-  } else {
-    grid = p.num_tiles < s->dev->sm_count ? p.num_tiles : s->dev->sm_count;
+    if (ws) {
+      p.split_w = t.split_w;
+      p.split_s = t.split_s;
+      p.cnt = static_cast<int*>(ws);
+      p.part = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + t.cnt_bytes);
+    }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.gridDim = dim3(t.grid, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s->stream;
@@ -957,16 +1066,40 @@ static qgemm_status launch_tc_gemm(qgemm_stream_s* s, int bf16, const void* A, c
   return QGEMM_OK;
 }
 
+static TcArgs w8a8_args(const void* A, const void* B, int b_kn, const float* sA, const float* sB,
+                        void* out, int out_dtype, int ldc, int M, int N, int K, int32_t* acc) {
+  TcArgs a;
+  a.kind = KIND_I8;
+  a.A = A; a.B = B; a.b_kn = b_kn;
+  a.M = M; a.N = N; a.K = K;
+  a.sA = sA; a.sB = sB; a.acc = acc;
+  a.out = out; a.out_dtype = out_dtype; a.ldc = ldc;
+  return a;
+}
+
 qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
                                  const float* sA, const float* sB, void* out, int out_dtype,
                                  int ldc, int M, int N, int K, int32_t* acc) {
-  return launch_tc_gemm(s, 0, A, B, b_kn, sA, sB, out, out_dtype, ldc, M, N, K, acc);
+  return launch_tc_gemm(s, w8a8_args(A, B, b_kn, sA, sB, out, out_dtype, ldc, M, N, K, acc));
 }
 
+// With a_repeat = 2, each row of B holds 2 blocks of ceil(2K / 128) * 128 bytes (zero past
+// 2K bytes) and A is read twice along K: out = A * B_0^T + A * B_1^T.
 qgemm_status launch_bf16_gemm_nk(qgemm_stream_s* s, const void* A, const void* B, void* out,
                                  int ldc, int M, int N, int K, int a_repeat) {
-  return launch_tc_gemm(s, 1, A, B, 0, nullptr, nullptr, out, QGEMM_BF16, ldc, M, N, 2 * K,
-                        nullptr, a_repeat);
+  if (a_repeat != 1 && a_repeat != 2) return fail(QGEMM_ERR_INVALID_ARG, "a_repeat %d", a_repeat);
+  TcArgs a;
+  a.kind = KIND_BF16;
+  a.A = A; a.B = B;
+  a.M = M; a.N = N; a.K = 2 * K;
+  if (a_repeat == 2) {
+    const uint64_t blk = (uint64_t)((a.K + w8a8::BK - 1) / w8a8::BK) * w8a8::BK;
+    a.nseg = 2;
+    a.b_seg = 0x2u;
+    a.b_pitch = 2 * blk;
+  }
+  a.out = out; a.out_dtype = QGEMM_BF16; a.ldc = ldc;
+  return launch_tc_gemm(s, a);
 }
 
 // ---- the W8A8 GEMM with a static scratch (qgemm_w8a8_gemm_static_scratch) ----------
@@ -1003,8 +1136,10 @@ qgemm_status launch_w8a8_tcgen05_static(qgemm_stream_s* s, const void* A, const 
   // the counters must be zero when the kernel starts
   const cudaError_t e = cudaMemsetAsync(ws, 0, STATIC_CNT_BYTES, s->stream);
   if (e != cudaSuccess) return cuda_fail(e, "clearing the static scratch counters");
-  return launch_tc_gemm(s, 0, A, B, b_kn, sA, sB, out, out_dtype, ldc, M, N, K, acc, 1, ws,
-                        STATIC_SCRATCH_BYTES);
+  TcArgs a = w8a8_args(A, B, b_kn, sA, sB, out, out_dtype, ldc, M, N, K, acc);
+  a.scratch = ws;
+  a.scratch_bytes = STATIC_SCRATCH_BYTES;
+  return launch_tc_gemm(s, a);
 }
 
 }  // namespace qg

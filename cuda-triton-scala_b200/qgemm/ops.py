@@ -135,6 +135,43 @@ class QuantizedGemmOps:
         L.call("qgemm_launch_by_name", self._h, name.encode(), bufs, len(buffers), iv, len(ints))
 
 
+class MatrixOps:
+    """The fp32 entry points of ``object MatrixOps``
+    (src/main/scala/cuda/dsl/operators/linalg/MatrixOps.scala): same names, parameter
+    order and meaning.  The GEMMs run as three tf32 tensor-core products per fp32
+    product with fp32 sums (|C - exact| <= 1e-5 * sum_k |A_ik * B_kj|)."""
+
+    def __init__(self, stream):
+        self.stream = stream
+        self._h = stream.handle
+
+    # -- MatrixOps.scala:16-28
+    def matmul(self, A, B, C, M: int, N: int, K: int):
+        L.call("qgemm_matmul_f32", self._h, L.addr(A), L.addr(B), L.addr(C), M, N, K)
+
+    # -- MatrixOps.scala:31-44
+    def matmulAddBias(self, A, B, bias, C, M: int, N: int, K: int):
+        L.call("qgemm_matmul_add_bias_f32", self._h, L.addr(A), L.addr(B), L.addr(bias),
+               L.addr(C), M, N, K)
+
+    # -- MatrixOps.scala:166-177
+    def gemv(self, A, x, y, M: int, N: int):
+        L.call("qgemm_gemv_f32", self._h, L.addr(A), L.addr(x), L.addr(y), M, N)
+
+
+class BLASOps:
+    """``object BLASOps`` (MatrixOps.scala:227+): sgemm on the same tensor-core path."""
+
+    def __init__(self, stream):
+        self.stream = stream
+        self._h = stream.handle
+
+    # -- MatrixOps.scala:230-243: C = alpha * (A x B) + beta * C (C always read)
+    def sgemm(self, A, B, C, M: int, N: int, K: int, alpha: float, beta: float):
+        L.call("qgemm_sgemm", self._h, L.addr(A), L.addr(B), L.addr(C), M, N, K,
+               float(alpha), float(beta))
+
+
 def shard_columns(N: int, world: int, rank: int, align: int = 256) -> tuple[int, int]:
     """Column range [n0, n1) of rank ``rank`` for an N-column weight split into
     ``world`` contiguous slices whose boundaries are multiples of ``align``."""

@@ -246,6 +246,30 @@ QGEMM_API qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t
 QGEMM_API qgemm_status qgemm_quantize_per_token(qgemm_stream_t s, uint64_t x, int in_dtype,
                                                 uint64_t q, uint64_t sA, int M, int K);
 
+/* fp32 entry points of the same facade, all operands fp32 row-major:
+ *   qgemm_matmul_f32           C[M,N] = A[M,K] x B[K,N]      MatrixOps.matmul
+ *                              (operators/linalg/MatrixOps.scala:16-28)
+ *   qgemm_matmul_add_bias_f32  C = A x B + bias[N]           MatrixOps.matmulAddBias (:31-44)
+ *   qgemm_sgemm                C = alpha * (A x B) + beta * C BLASOps.sgemm (:230-243);
+ *                              C is read whatever beta is, as in the reference
+ *   qgemm_gemv_f32             y[M] = A[M,N] x x[N]          MatrixOps.gemv (:166-177)
+ * The GEMMs run on the sm_100 tensor cores as three tf32 products per fp32 product
+ * (hi/lo splits of both operands) with fp32 sums: |C - exact| <= 1e-5 * sum_k |A*B|
+ * terms, the accuracy of the reference's sequential fp32 loop.  An infinite input
+ * sends the whole call through a CUDA-core kernel in the reference's own order
+ * (bit-identical to the loop).  The split operands (8 * (M + N) * roundup(K, 32)
+ * bytes) live in the stream handle's scratch, made or grown by the call (make one call
+ * before capturing the stream into a graph).  Deterministic.  Requires sm_100 for the
+ * GEMMs; 4-byte aligned pointers. */
+QGEMM_API qgemm_status qgemm_matmul_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t C,
+                                        int M, int N, int K);
+QGEMM_API qgemm_status qgemm_matmul_add_bias_f32(qgemm_stream_t s, uint64_t A, uint64_t B,
+                                                 uint64_t bias, uint64_t C, int M, int N, int K);
+QGEMM_API qgemm_status qgemm_sgemm(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t C, int M,
+                                   int N, int K, float alpha, float beta);
+QGEMM_API qgemm_status qgemm_gemv_f32(qgemm_stream_t s, uint64_t A, uint64_t x, uint64_t y, int M,
+                                      int N);
+
 /* One-time weight repack: int8 [K,N] (reference layout) -> [N,K] (K-major). */
 QGEMM_API qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src_kn, uint64_t dst_nk,
                                  int K, int N);
@@ -256,7 +280,8 @@ QGEMM_API qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src_kn, ui
  * bufs are device addresses in the reference method's parameter order, ints
  * the Int parameters in order (Bool as 0/1).  Names: "w8a32Gemm", "w4a16Gemm",
  * "w8a16Gemm", "w8a16GemmRowWise", "dynamicQuantize",
- * "weightOnlyQuantizePerChannel", "dequantize".  Unknown name -> INVALID_ARG. */
+ * "weightOnlyQuantizePerChannel", "dequantize", "matmul", "matmulAddBias", "gemv"
+ * (sgemm takes Float parameters: call qgemm_sgemm).  Unknown name -> INVALID_ARG. */
 QGEMM_API qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name,
                                   const uint64_t* bufs, int nbufs,
                                   const int* ints, int nints);

@@ -58,6 +58,9 @@ def lib():
         L.oracle_dynamic_quantize.argtypes = [_P, _P, _P, _I, _I, _I]
         L.oracle_weight_only_quantize_per_channel.argtypes = [_P, _P, _P, _P, _I, _I]
         L.oracle_dequantize.argtypes = [_P, _P, _P, _I, _I]
+        L.oracle_matmul_f32.argtypes = [_P, _P, _P, _P, _I, _I, _I, ctypes.c_float,
+                                        ctypes.c_float, _I, _I]
+        L.oracle_gemv_f32.argtypes = [_P, _P, _P, _I, _I]
         L.oracle_max_threads.restype = _I
         _lib = L
     return _lib
@@ -210,3 +213,29 @@ def dequantize(qWeight, scales):
     w = np.empty((K, N), np.float32)
     lib().oracle_dequantize(_ptr(q), _ptr(s), _ptr(w), K, N)
     return w
+
+
+# ---- fp32 operators (MatrixOps.scala) ----------------------------------------
+
+def matmul_f32(A, B, bias=None, C=None, alpha=1.0, beta=0.0, mode=0, threads=0):
+    """MatrixOps.matmul (:16-28) / matmulAddBias (:31-44) / BLASOps.sgemm (:230-243).
+    mode 0: A @ B; 1: A @ B + bias; 2: alpha * (A @ B) + beta * C (C is the input C)."""
+    a = _c(A, np.float32); b = _c(B, np.float32)
+    M, K = a.shape
+    K2, N = b.shape
+    assert K == K2
+    out = np.array(C, dtype=np.float32, copy=True) if mode == 2 else np.empty((M, N), np.float32)
+    assert out.shape == (M, N)
+    bb = _c(bias, np.float32) if bias is not None else None
+    lib().oracle_matmul_f32(_ptr(a), _ptr(b), _ptr(bb), _ptr(out), M, N, K, float(alpha),
+                            float(beta), int(mode), int(threads))
+    return out
+
+
+def gemv_f32(A, x):
+    """MatrixOps.gemv (:166-177): y = A x, A [M,N]."""
+    a = _c(A, np.float32); xx = _c(x, np.float32)
+    M, N = a.shape
+    y = np.empty(M, np.float32)
+    lib().oracle_gemv_f32(_ptr(a), _ptr(xx), _ptr(y), M, N)
+    return y

@@ -270,3 +270,52 @@ void oracle_dequantize(const int8_t* qWeight, const float* scales,
     weight[i] = (float)qWeight[i] * scales[col];
   }
 }
+
+/* ---- fp32 operators of the same facade (operators/linalg/MatrixOps.scala) ----
+ *
+ * MatrixOps.matmul :16-28, matmulAddBias :31-44, BLASOps.sgemm :230-243:
+ *   var sum = 0.0f
+ *   for (k <- 0 until K) sum += A(row*K + k) * B(k*N + col)
+ *   matmul:        C(row*N + col) = sum
+ *   matmulAddBias: C(row*N + col) = sum + bias(col)
+ *   sgemm:         C(row*N + col) = alpha*sum + beta*C(row*N + col)
+ * mode 0 / 1 / 2 selects the epilogue.  Each product and sum is rounded on its own
+ * (JVM float semantics), k ascending per element; the loops run k outside the
+ * columns so that B is read row by row, which keeps every element's order. */
+void oracle_matmul_f32(const float* A, const float* B, const float* bias, float* C,
+                       int M, int N, int K, float alpha, float beta, int mode,
+                       int threads) {
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+#endif
+  for (int row = 0; row < M; ++row) {
+    float* sum = (float*)malloc(sizeof(float) * (N > 0 ? N : 1));
+    for (int col = 0; col < N; ++col) sum[col] = 0.0f;
+    for (int k = 0; k < K; ++k) {
+      const float a = A[(int64_t)row * K + k];
+      const float* b = B + (int64_t)k * N;
+      for (int col = 0; col < N; ++col) sum[col] += a * b[col];
+    }
+    float* c = C + (int64_t)row * N;
+    for (int col = 0; col < N; ++col) {
+      if (mode == 1) c[col] = sum[col] + bias[col];
+      else if (mode == 2) c[col] = alpha * sum[col] + beta * c[col];
+      else c[col] = sum[col];
+    }
+    free(sum);
+  }
+  (void)threads;
+}
+
+/* MatrixOps.gemv :166-177:
+ *   var sum = 0.0f
+ *   for (j <- 0 until N) sum += A(i*N + j) * x(j)
+ *   y(i) = sum */
+void oracle_gemv_f32(const float* A, const float* x, float* y, int M, int N) {
+  for (int i = 0; i < M; ++i) {
+    float sum = 0.0f;
+    for (int j = 0; j < N; ++j) sum += A[(int64_t)i * N + j] * x[j];
+    y[i] = sum;
+  }
+}

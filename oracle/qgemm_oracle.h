@@ -1,5 +1,6 @@
 /*
- * qgemm_oracle.h -- CPU restatement of the reference's quantized-matmul operators.
+ * qgemm_oracle.h -- CPU restatement of the reference's quantized-matmul operators
+ * and of the fp32 matmul / sgemm / gemv of the same facade.
  *
  * TEST INFRASTRUCTURE ONLY.  This library is the checker for the CUDA path in
  * libqgemm: only tests/, __graft_entry__.smoke() and the cpu_baseline /
@@ -14,7 +15,9 @@
  * only element (0,0)).  Each function below restates one operator body
  * statement by statement, with the reference's arithmetic order, and is pinned
  * only by hand-computed known-answer cases and an independent pure-Python
- * restatement (tests/golden/make_golden.py).
+ * restatement (tests/golden/make_golden.py).  The fp32 operators
+ * (operators/linalg/MatrixOps.scala) are likewise untested in the reference; their
+ * restatement is pinned by known answers and by float64 error bounds.
  *
  * Floating point: the library is compiled with -ffp-contract=off on x86-64
  * (SSE scalar float), which gives the same IEEE-754 binary32
@@ -93,6 +96,16 @@ void oracle_weight_only_quantize_per_channel(const float* weight, float* scales,
 /* QuantizedGemmOps.dequantize (QuantizedGemmOps.scala:198-212). */
 void oracle_dequantize(const int8_t* qWeight, const float* scales,
                        float* weight, int K, int N);
+
+/* MatrixOps.matmul / matmulAddBias / BLASOps.sgemm (MatrixOps.scala:16-44,
+ * :230-243): mode 0 C = A x B, 1 C = A x B + bias, 2 C = alpha (A x B) + beta C.
+ * threads <= 0: all (OpenMP over rows; each element's order is unchanged). */
+void oracle_matmul_f32(const float* A, const float* B, const float* bias, float* C,
+                       int M, int N, int K, float alpha, float beta, int mode,
+                       int threads);
+
+/* MatrixOps.gemv (MatrixOps.scala:166-177): y = A x, A [M,N]. */
+void oracle_gemv_f32(const float* A, const float* x, float* y, int M, int N);
 
 /* Threads the OpenMP build can use (1 without OpenMP). */
 int oracle_max_threads(void);

@@ -39,3 +39,31 @@ def rel_err(y: np.ndarray, ref: np.ndarray) -> float:
     ref = ref.astype(np.float64)
     floor = 1e-2 * float(np.sqrt(np.mean(ref * ref))) + 1e-30
     return float(np.max(np.abs(y - ref) / np.maximum(np.abs(ref), floor)))
+
+
+def gemm_bound_ratio(y, A, B, *, bias=None, C=None, alpha=1.0, beta=0.0) -> float:
+    """max_ij |y_ij - exact_ij| / (|alpha| sum_k |A_ik B_kj| + |bias_j| + |beta C_ij|),
+    the exact value taken in float64: the forward-error measure of a floating-point
+    GEMM.  A sequential fp32 loop over K stays below K * 2^-24 of it; the fp32 gate is
+    1e-5.  Elements whose denominator is 0 must be exact."""
+    A64 = np.asarray(A, np.float64)
+    B64 = np.asarray(B, np.float64)
+    exact = alpha * (A64 @ B64)
+    scale = abs(alpha) * (np.abs(A64) @ np.abs(B64))
+    if bias is not None:
+        exact = exact + np.asarray(bias, np.float64)[None, :]
+        scale = scale + np.abs(np.asarray(bias, np.float64))[None, :]
+    if C is not None and beta != 0.0:
+        C64 = np.asarray(C, np.float64)
+        exact = exact + beta * C64
+        scale = scale + abs(beta) * np.abs(C64)
+    err = np.abs(np.asarray(y, np.float64) - exact)
+    if (err[scale == 0] != 0).any():
+        return float("inf")
+    nz = scale > 0
+    return float(np.max(err[nz] / scale[nz])) if nz.any() else 0.0
+
+
+def gemv_bound_ratio(y, A, x) -> float:
+    """gemm_bound_ratio for y = A x."""
+    return gemm_bound_ratio(np.asarray(y)[:, None], A, np.asarray(x)[:, None])

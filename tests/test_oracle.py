@@ -185,3 +185,58 @@ def test_grouped_threads_deterministic(oracle):
     b, bb = oracle.w4a16_grouped(wq, sc, 8, 128, x, threads=4)
     np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
     np.testing.assert_array_equal(ab, bb)
+
+
+# ---- fp32 operators of the same facade (MatrixOps.scala) ----------------------
+
+def test_matmul_known_answer(oracle):
+    A = np.array([[1, 2, 3, 4], [5, 6, 7, 8]], np.float32)
+    B = np.array([[1, 0, 2], [0, 1, 0], [1, 1, 1], [2, 0, 1]], np.float32)
+    np.testing.assert_array_equal(oracle.matmul_f32(A, B), [[12, 5, 9], [28, 13, 25]])
+    bias = np.array([0.5, -1, 2], np.float32)
+    np.testing.assert_array_equal(oracle.matmul_f32(A, B, bias=bias, mode=1),
+                                  [[12.5, 4, 11], [28.5, 12, 27]])
+    C = np.ones((2, 3), np.float32)
+    np.testing.assert_array_equal(oracle.matmul_f32(A, B, C=C, alpha=2.0, beta=-3.0, mode=2),
+                                  [[21, 7, 15], [53, 23, 47]])
+    np.testing.assert_array_equal(oracle.gemv_f32(A, np.array([1, 0, -1, 2], np.float32)),
+                                  [6, 14])
+
+
+def test_matmul_sequential_fp32_order(oracle):
+    # k ascending with each sum rounded to binary32: (1e8 + 1) rounds back to 1e8, so
+    # the loop gives 0 where the exact value is 1.
+    A = np.ones((1, 3), np.float32)
+    B = np.array([[1e8], [1.0], [-1e8]], np.float32)
+    assert oracle.matmul_f32(A, B)[0, 0] == 0.0
+    assert oracle.gemv_f32(B.T.copy(), np.ones(3, np.float32))[0] == 0.0
+
+
+def test_sgemm_reads_c_whatever_beta(oracle):
+    # BLASOps.sgemm computes alpha*sum + beta*C literally: beta = 0 keeps C's NaN.
+    A = np.ones((2, 2), np.float32)
+    C = np.array([[np.nan, 1], [np.inf, 2]], np.float32)
+    y = oracle.matmul_f32(A, A, C=C, alpha=1.0, beta=0.0, mode=2)
+    assert np.isnan(y[0, 0]) and np.isnan(y[1, 0])
+    assert y[0, 1] == 2 and y[1, 1] == 2
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (7, 13, 33), (64, 48, 1000)])
+def test_matmul_within_fp32_bound(oracle, M, N, K):
+    from helpers import gemm_bound_ratio, gemv_bound_ratio
+    rng = np.random.default_rng(M * 100 + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    y = oracle.matmul_f32(A, B)
+    assert gemm_bound_ratio(y, A, B) <= K * 2.0 ** -24
+    x = rng.standard_normal(K).astype(np.float32)
+    assert gemv_bound_ratio(oracle.gemv_f32(A, x), A, x) <= K * 2.0 ** -24
+
+
+def test_matmul_threads_identical(oracle):
+    rng = np.random.default_rng(3)
+    A = rng.standard_normal((33, 70)).astype(np.float32)
+    B = rng.standard_normal((70, 45)).astype(np.float32)
+    y1 = oracle.matmul_f32(A, B, threads=1)
+    y4 = oracle.matmul_f32(A, B, threads=4)
+    np.testing.assert_array_equal(y1.view(np.uint32), y4.view(np.uint32))
