@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--no-large", action="store_true", help="skip the sharded large GEMM")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-llama", action="store_true", help="skip the Llama-shaped W4A16 stack")
-    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large", "llama"], default="all",
+    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large", "llama", "f32"], default="all",
                    help="run one workload alone (for profiling); prints its own JSON line")
     p.add_argument("--profile", action="store_true",
                    help="with --only w8a8|w4a16: warmup + steps plain launches and nothing "
@@ -463,6 +463,70 @@ def w8a8_pipeline(ops, hb, steps, peaks):
             "quantize_plus_gemm_TOPS": 2.0 * M * N * K / res["quantize_plus_gemm"] / 1e12}
 
 
+def f32_facade(st, peaks, steps=10):
+    """The fp32 entry points (MatrixOps.matmul / gemv) on device-resident inputs:
+    matmul 4096^3 on the tensor cores (3 tf32 products per fp32 product), a skinny
+    16 x 4096 x 4096 matmul on the CUDA-core path, gemv 16384 x 16384.  Two rotating input
+    sets of 128 MB (matmul) and one 1 GB matrix (gemv) keep every launch above L2."""
+    import torch
+    import qgemm
+    m = qgemm.MatrixOps(st)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4242)
+
+    def run(fn, n):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / n
+
+    res = {}
+    M = N = K = 4096
+    A = [torch.randn((M, K), device="cuda", generator=gen) for _ in range(2)]
+    B = [torch.randn((K, N), device="cuda", generator=gen) for _ in range(2)]
+    C = torch.empty((M, N), device="cuda")
+    t = run(lambda i: m.matmul(A[i % 2], B[i % 2], C, M, N, K), steps)
+    fl = 2.0 * M * N * K
+    tf32_peak = 0.5 * peaks["bf16_tflops"]
+    res["matmul_4096"] = {"us": t * 1e6, "TFLOP_s": fl / t / 1e12,
+                          "tensor_TFLOP_s": 3 * fl / t / 1e12,
+                          "tensor_frac_of_tf32_peak": 3 * fl / t / 1e12 / tf32_peak,
+                          "tf32_peak_basis": "0.5 x measured bf16_tflops (dense tf32 runs at "
+                                             "half the bf16 rate on B200)",
+                          "includes": "two operand split passes (A, B -> hi/lo) + GEMM"}
+    rows = torch.randperm(M, device="cuda", generator=gen)[:32]
+    ref = A[1][rows].double() @ B[1].double()
+    res["matmul_4096"]["max_err_over_sum_abs"] = float(
+        ((C[rows].double() - ref).abs() / (A[1][rows].abs().double() @ B[1].abs().double())).max())
+    torch.backends.cuda.matmul.allow_tf32 = False
+    tt = run(lambda i: torch.matmul(A[i % 2], B[i % 2], out=C), 5)
+    res["matmul_4096"]["torch_fp32_TFLOP_s_context"] = fl / tt / 1e12
+    Ms = 16
+    As = torch.randn((Ms, K), device="cuda", generator=gen)
+    Cs = torch.empty((Ms, N), device="cuda")
+    t = run(lambda i: m.matmul(As, B[i % 2], Cs, Ms, N, K), steps)
+    res["matmul_16x4096x4096"] = {"us": t * 1e6, "TFLOP_s": 2.0 * Ms * N * K / t / 1e12,
+                                  "B_read_GB_s": 4.0 * K * N / t / 1e9}
+    del A, B, C, As, Cs
+    torch.cuda.empty_cache()
+    Mv = Nv = 16384
+    Av = torch.randn((Mv, Nv), device="cuda", generator=gen)
+    x = torch.randn((Nv,), device="cuda", generator=gen)
+    y = torch.empty((Mv,), device="cuda")
+    t = run(lambda i: m.gemv(Av, x, y, Mv, Nv), steps)
+    gbs = 4.0 * (Mv * Nv + Nv + Mv) / t / 1e9
+    res["gemv_16384"] = {"us": t * 1e6, "GB_s": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"]}
+    del Av
+    torch.cuda.empty_cache()
+    return res
+
+
 LLAMA_LINEARS = (("qkv", 4096, 12288), ("o", 4096, 4096), ("gate_up", 4096, 22016),
                  ("down", 11008, 4096))
 
@@ -726,6 +790,12 @@ def main():
         if rank == 0:
             print(json.dumps({"only": "w4a16", "w4a16_decode": r}), flush=True)
         return 0
+    if args.only == "f32":
+        log("fp32 facade (only)")
+        r = f32_facade(st, peaks, K)
+        if rank == 0:
+            print(json.dumps({"only": "f32", "fp32_facade": r}), flush=True)
+        return 0
     if args.only == "llama":
         log("llama stack (only)")
         r = llama_stack(ops, peaks)
@@ -777,6 +847,9 @@ def main():
     for k in ("A", "B", "sA", "sB"):
         hb.pop(k)
     torch.cuda.empty_cache()
+    if world == 1 and rank == 0:
+        log("fp32 facade")
+        extra["fp32_facade"] = f32_facade(st, peaks)
     if world == 1 and rank == 0 and not args.no_llama:
         log("llama stack")
         extra["llama2_7b_w4a16_stack"] = llama_stack(ops, peaks)

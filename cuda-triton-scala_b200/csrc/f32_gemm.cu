@@ -29,9 +29,19 @@
 // output.  Without the flag that kernel returns at once.  NaN inputs need no such
 // path: they propagate through the three products as they do through the loop.
 //
+// Shapes with few rows or few columns (M <= 64 or N <= 64) would give the tensor cores
+// too few tiles and pay the split passes for nothing.  They run on CUDA cores instead:
+// rows_gemm_kernel<MT> gives each thread one column of B and MT rows of A (A's k-tile
+// in shared memory, B read once, coalesced along N) over one K chunk, fp32 fma, and
+// writes a partial tile; rows_reduce_kernel adds the chunks in chunk order (so the
+// result is deterministic) and applies the epilogue.  The infinity flag and the
+// exact-order kernel work as on the tensor-core path.
+//
 // gemv (y = A x, A [M,N] row-major) is bound by the read of A: T threads per row
 // (T = 32..256 so that short matrices still fill the GPU), float4 streaming loads,
 // four independent partial sums per thread, a shuffle / shared-memory reduction.
+// Matrices with fewer rows than 4 blocks per SM cut each row into chunks (one block
+// each) whose partial sums a second kernel adds in chunk order.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -179,6 +189,93 @@ __global__ void __launch_bounds__(256) exact_gemm_kernel(const float* __restrict
   }
 }
 
+// Partial products of rows [m0, m0 + MT) (blockIdx.z) x columns [256 bx, +256) over the
+// K chunk [kc * by, +kc): part[by][m][n].  Block 256 threads, one column each.
+template <int MT>
+__global__ void __launch_bounds__(256) rows_gemm_kernel(const float* __restrict__ A,
+                                                        const float* __restrict__ B,
+                                                        float* __restrict__ part, int M, int N,
+                                                        int K, int kc, int* inf_flag) {
+  constexpr int LD = MT + 4;  // row pitch of the transposed A tile (16-byte aligned rows)
+  __shared__ __align__(16) float As[32][LD];
+  const int n = blockIdx.x * 256 + threadIdx.x;
+  const int k_begin = blockIdx.y * kc;
+  const int k_end = K - k_begin < kc ? K : k_begin + kc;
+  const int m0 = blockIdx.z * MT;
+  float acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+  bool inf = false;
+  for (int k0 = k_begin; k0 < k_end; k0 += 32) {
+    const int kn = k_end - k0 < 32 ? k_end - k0 : 32;
+    for (int i = threadIdx.x; i < 32 * MT; i += 256) {
+      const int m = i / 32, kk = i % 32;
+      const float v = (m0 + m < M && kk < kn) ? __ldg(A + (size_t)(m0 + m) * K + k0 + kk) : 0.f;
+      inf |= is_inf(v);
+      As[kk][m] = v;
+    }
+    __syncthreads();
+    if (n < N) {
+      if (kn == 32) {
+        float b[32];
+#pragma unroll
+        for (int kk = 0; kk < 32; ++kk) b[kk] = __ldg(B + (size_t)(k0 + kk) * N + n);
+#pragma unroll
+        for (int kk = 0; kk < 32; ++kk) {
+          inf |= is_inf(b[kk]);
+#pragma unroll
+          for (int m = 0; m < MT; m += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(&As[kk][m]);
+            acc[m] = fmaf(a.x, b[kk], acc[m]);
+            acc[m + 1] = fmaf(a.y, b[kk], acc[m + 1]);
+            acc[m + 2] = fmaf(a.z, b[kk], acc[m + 2]);
+            acc[m + 3] = fmaf(a.w, b[kk], acc[m + 3]);
+          }
+        }
+      } else {
+        for (int kk = 0; kk < kn; ++kk) {
+          const float b = __ldg(B + (size_t)(k0 + kk) * N + n);
+          inf |= is_inf(b);
+#pragma unroll
+          for (int m = 0; m < MT; m += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(&As[kk][m]);
+            acc[m] = fmaf(a.x, b, acc[m]);
+            acc[m + 1] = fmaf(a.y, b, acc[m + 1]);
+            acc[m + 2] = fmaf(a.z, b, acc[m + 2]);
+            acc[m + 3] = fmaf(a.w, b, acc[m + 3]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (inf) *inf_flag = 1;
+  if (n < N) {
+    float* dst = part + ((size_t)blockIdx.y * M + m0) * N + n;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      if (m0 + m < M) dst[(size_t)m * N] = acc[m];
+  }
+}
+
+// C = epilogue(sum over chunks of part[c]) unless *flag (the exact-order kernel writes C).
+__global__ void __launch_bounds__(256) rows_reduce_kernel(const float* __restrict__ part,
+                                                          const float* __restrict__ bias,
+                                                          float* __restrict__ C, int M, int N,
+                                                          int chunks, float alpha, float beta,
+                                                          int mode, const int* flag) {
+  if (*reinterpret_cast<const volatile int*>(flag) != 0) return;
+  const size_t total = (size_t)M * N;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float v = __ldcs(part + i);
+    for (int c = 1; c < chunks; ++c) v = __fadd_rn(v, __ldcs(part + (size_t)c * total + i));
+    if (mode == F32_MATMUL_BIAS) v = __fadd_rn(v, bias[i % N]);
+    else if (mode == F32_SGEMM) v = __fadd_rn(__fmul_rn(alpha, v), __fmul_rn(beta, C[i]));
+    C[i] = v;
+  }
+}
+
 // y[row] = sum_j A[row, j] * x[j]: groups of T threads per row, 256 / T rows per block.
 template <int T>
 __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ A,
@@ -239,18 +336,68 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ A,
   }
 }
 
+// Short matrices (too few rows to fill the GPU): row blockIdx.y is cut into chunks of L
+// values (a multiple of 1024), one block each; part[row * chunks + chunk].
+__global__ void __launch_bounds__(256) gemv_split_kernel(const float* __restrict__ A,
+                                                         const float* __restrict__ x,
+                                                         float* __restrict__ part, int N, int L,
+                                                         int vec) {
+  const int row = blockIdx.y;
+  const int j0 = blockIdx.x * L;
+  const int j1 = N - j0 < L ? N : j0 + L;
+  const float* a = A + (size_t)row * N;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (vec) {  // N % 4 == 0 and j0 % 4 == 0
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int j = j0 / 4 + threadIdx.x; j < j1 / 4; j += 256) {
+      const float4 av = __ldcs(a4 + j), xv = __ldg(x4 + j);
+      s0 = fmaf(av.x, xv.x, s0);
+      s1 = fmaf(av.y, xv.y, s1);
+      s2 = fmaf(av.z, xv.z, s2);
+      s3 = fmaf(av.w, xv.w, s3);
+    }
+  } else {
+    for (int j = j0 + threadIdx.x; j < j1; j += 256) s0 = fmaf(__ldcs(a + j), __ldg(x + j), s0);
+  }
+  float s = (s0 + s1) + (s2 + s3);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w];
+    part[(size_t)row * gridDim.x + blockIdx.x] = t;
+  }
+}
+
+// y[row] = sum of the row's chunks, in chunk order.
+__global__ void gemv_reduce_kernel(const float* __restrict__ part, float* __restrict__ y, int M,
+                                   int chunks) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= M) return;
+  float s = part[(size_t)row * chunks];
+  for (int c = 1; c < chunks; ++c) s += part[(size_t)row * chunks + c];
+  y[row] = s;
+}
+
 }  // namespace f32
 
 // Stream scratch layout of one fp32 GEMM: the tcgen05 GEMM's split scratch (its counter
-// block first), 1 KiB holding the infinity flag, A split, B split; 1 KiB aligned.
+// block first, kept in place for every other call on the stream), 1 KiB holding the
+// infinity flag, then A split and B split (tensor cores) or the partial tiles (CUDA
+// cores); 1 KiB aligned.
 struct F32Layout {
   size_t sc, flag, a, b, total;
 };
 
-static F32Layout f32_layout(const qgemm_device_s* d, int M, int N, int K) {
+static F32Layout f32_layout_tc(const qgemm_device_s* d, int M, int N, int K) {
   const size_t Kp = ((size_t)K + f32::KB - 1) / f32::KB * f32::KB;
   F32Layout l;
-  l.sc = (tc_gemm_scratch_bytes(d, M, N, 3 * (int)(Kp / f32::KB)) + 1023) & ~(size_t)1023;
+  l.sc = (tc_gemm_scratch_bytes(d, M, N, 3 * (int)(Kp / f32::KB), true) + 1023) & ~(size_t)1023;
   l.flag = l.sc;
   l.a = l.flag + 1024;
   l.b = l.a + (((size_t)M * 2 * Kp * 4 + 1023) & ~(size_t)1023);
@@ -258,23 +405,78 @@ static F32Layout f32_layout(const qgemm_device_s* d, int M, int N, int K) {
   return l;
 }
 
-size_t f32_gemm_workspace_bytes(const qgemm_device_s* d, int M, int N, int K) {
-  return f32_layout(d, M, N, K).total;
+// CUDA-core plan: rows per thread, K chunk, grid.
+struct RowsPlan {
+  int mt, kc, chunks;
+  dim3 grid;
+};
+
+static RowsPlan rows_plan(const qgemm_device_s* d, int M, int N, int K) {
+  RowsPlan r;
+  r.mt = M <= 4 ? 4 : M <= 8 ? 8 : M <= 16 ? 16 : M <= 32 ? 32 : 64;
+  const int gx = (N + 255) / 256, gz = (M + r.mt - 1) / r.mt;
+  // enough blocks for two waves of two blocks per SM, K chunks of at least 64
+  const long long want = (long long)d->sm_count * 4;
+  long long chunks = (want + (long long)gx * gz - 1) / ((long long)gx * gz);
+  const long long max_chunks = (K + 63) / 64;
+  if (chunks > max_chunks) chunks = max_chunks;
+  if (chunks < 1) chunks = 1;
+  r.kc = (int)(((K + chunks - 1) / chunks + 31) / 32 * 32);
+  r.chunks = (K + r.kc - 1) / r.kc;
+  r.grid = dim3(gx, r.chunks, gz);
+  return r;
 }
 
-qgemm_status launch_f32_gemm(qgemm_stream_s* s, const float* A, const float* B,
-                             const float* bias, float* C, int M, int N, int K, float alpha,
-                             float beta, int mode) {
+static qgemm_status launch_exact(qgemm_stream_s* s, const float* A, const float* B,
+                                 const float* bias, float* C, int M, int N, int K, float alpha,
+                                 float beta, int mode, const int* inf_flag) {
+  f32::exact_gemm_kernel<<<s->dev->sm_count * 8, 256, 0, s->stream>>>(A, B, bias, C, M, N, K,
+                                                                       alpha, beta, mode,
+                                                                       inf_flag);
+  return cuda_fail(cudaGetLastError(), "exact_gemm launch");
+}
+
+static qgemm_status launch_f32_rows(qgemm_stream_s* s, const float* A, const float* B,
+                                    const float* bias, float* C, int M, int N, int K,
+                                    float alpha, float beta, int mode) {
   using namespace f32;
-  if (K == 0) {
-    const size_t total = (size_t)M * N;
-    const size_t cap = (size_t)s->dev->sm_count * 16;
-    const int grid = (int)((total + 255) / 256 < cap ? (total + 255) / 256 : cap);
-    empty_k_kernel<<<grid, 256, 0, s->stream>>>(bias, C, M, N, alpha, beta, mode);
-    return cuda_fail(cudaGetLastError(), "empty_k launch");
+  const RowsPlan r = rows_plan(s->dev, M, N, K);
+  if (r.grid.z > 65535u || r.grid.y > 65535u)
+    return fail(QGEMM_ERR_UNSUPPORTED, "CUDA-core fp32 GEMM: M=%d needs more than 65535 row groups", M);
+  const size_t cnt = (tc_gemm_scratch_bytes(s->dev, 1, 1, 1) + 1023) & ~(size_t)1023;
+  const size_t total = cnt + 1024 + (size_t)r.chunks * M * N * 4;
+  void* ws = nullptr;
+  const qgemm_status st = stream_workspace(s, total, &ws);
+  if (st != QGEMM_OK) return st;
+  int* inf_flag = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + cnt);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt + 1024);
+  cudaError_t e = cudaMemsetAsync(inf_flag, 0, sizeof(int), s->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the infinity flag");
+  switch (r.mt) {
+    case 4: rows_gemm_kernel<4><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
+    case 8: rows_gemm_kernel<8><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
+    case 16: rows_gemm_kernel<16><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
+    case 32: rows_gemm_kernel<32><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
+    default: rows_gemm_kernel<64><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
   }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rows_gemm launch");
+  const size_t elems = (size_t)M * N;
+  const size_t cap = (size_t)s->dev->sm_count * 16;
+  const int grid = (int)((elems + 255) / 256 < cap ? (elems + 255) / 256 : cap);
+  rows_reduce_kernel<<<grid, 256, 0, s->stream>>>(part, bias, C, M, N, r.chunks, alpha, beta,
+                                                  mode, inf_flag);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rows_reduce launch");
+  return launch_exact(s, A, B, bias, C, M, N, K, alpha, beta, mode, inf_flag);
+}
+
+static qgemm_status launch_f32_tc(qgemm_stream_s* s, const float* A, const float* B,
+                                  const float* bias, float* C, int M, int N, int K, float alpha,
+                                  float beta, int mode) {
+  using namespace f32;
   const int Kp = (K + KB - 1) / KB * KB;
-  const F32Layout l = f32_layout(s->dev, M, N, K);
+  const F32Layout l = f32_layout_tc(s->dev, M, N, K);
   void* ws = nullptr;
   const qgemm_status st = stream_workspace(s, l.total, &ws);
   if (st != QGEMM_OK) return st;
@@ -318,13 +520,31 @@ qgemm_status launch_f32_gemm(qgemm_stream_s* s, const float* A, const float* B,
   a.ep_beta = mode == F32_SGEMM;
   a.bias = mode == F32_MATMUL_BIAS ? bias : nullptr;
   a.skip_flag = inf_flag;
+  a.full_split = 1;
   a.scratch = ws;
   a.scratch_bytes = l.sc;
   const qgemm_status gs = launch_tc_gemm(s, a);
   if (gs != QGEMM_OK) return gs;
-  exact_gemm_kernel<<<s->dev->sm_count * 8, 256, 0, s->stream>>>(A, B, bias, C, M, N, K, alpha,
-                                                                  beta, mode, inf_flag);
-  return cuda_fail(cudaGetLastError(), "exact_gemm launch");
+  return launch_exact(s, A, B, bias, C, M, N, K, alpha, beta, mode, inf_flag);
+}
+
+qgemm_status launch_f32_gemm(qgemm_stream_s* s, const float* A, const float* B,
+                             const float* bias, float* C, int M, int N, int K, float alpha,
+                             float beta, int mode, int algo) {
+  using namespace f32;
+  if (K == 0) {
+    const size_t total = (size_t)M * N;
+    const size_t cap = (size_t)s->dev->sm_count * 16;
+    const int grid = (int)((total + 255) / 256 < cap ? (total + 255) / 256 : cap);
+    empty_k_kernel<<<grid, 256, 0, s->stream>>>(bias, C, M, N, alpha, beta, mode);
+    return cuda_fail(cudaGetLastError(), "empty_k launch");
+  }
+  bool tc = algo == QGEMM_ALGO_TCGEN05;
+  if (algo == QGEMM_ALGO_AUTO)
+    tc = s->dev->tcgen05 && ((M > 64 && N > 64) || (M + 63) / 64 > 65535);
+  if (tc && !s->dev->tcgen05) return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
+  return tc ? launch_f32_tc(s, A, B, bias, C, M, N, K, alpha, beta, mode)
+            : launch_f32_rows(s, A, B, bias, C, M, N, K, alpha, beta, mode);
 }
 
 qgemm_status launch_f32_gemv(qgemm_stream_s* s, const float* A, const float* x, float* y, int M,
@@ -333,6 +553,27 @@ qgemm_status launch_f32_gemv(qgemm_stream_s* s, const float* A, const float* x, 
   // Threads per row: enough groups to fill the GPU (64 warps per SM), at least two
   // float4 per thread.
   const long long target_warps = (long long)s->dev->sm_count * 64;
+  // Fewer rows than 8 blocks per SM: cut the rows into chunks of at least 1024 values.
+  const long long target_blocks = (long long)s->dev->sm_count * 8;
+  if ((long long)M < target_blocks / 2 && N >= 2048) {
+    long long chunks = (target_blocks + M - 1) / M;
+    if (chunks > N / 1024) chunks = N / 1024;
+    const int L = (int)(((N + chunks - 1) / chunks + 1023) / 1024 * 1024);
+    const int nch = (N + L - 1) / L;
+    if (nch >= 2) {
+      const size_t cnt = (tc_gemm_scratch_bytes(s->dev, 1, 1, 1) + 1023) & ~(size_t)1023;
+      void* ws = nullptr;
+      const qgemm_status st = stream_workspace(s, cnt + (size_t)M * nch * 4, &ws);
+      if (st != QGEMM_OK) return st;
+      float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt);
+      const int vec = (N % 4 == 0) && aligned((uint64_t)A, 16) && aligned((uint64_t)x, 16);
+      gemv_split_kernel<<<dim3(nch, M), 256, 0, s->stream>>>(A, x, part, N, L, vec);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "gemv_split launch");
+      gemv_reduce_kernel<<<(M + 255) / 256, 256, 0, s->stream>>>(part, y, M, nch);
+      return cuda_fail(cudaGetLastError(), "gemv_reduce launch");
+    }
+  }
   int T = 32;
   while (T < 256 && (long long)M * (T / 32) < target_warps && (long long)T * 8 <= N) T *= 2;
   const int R = 256 / T;

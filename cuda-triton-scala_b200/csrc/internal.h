@@ -89,6 +89,8 @@ struct TcArgs {
   int ep_alpha = 0, ep_beta = 0;
   // Device word read by the epilogue: non-zero -> store nothing.
   const int* skip_flag = nullptr;
+  // Cut every tile along K when there are fewer pair tiles than CTA pairs.
+  int full_split = 0;
   // Last-wave split scratch: counters (zero) at offset 0, partial tiles after them;
   // null: the stream handle's scratch.
   void* scratch = nullptr;
@@ -97,7 +99,8 @@ struct TcArgs {
 qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a);
 // Scratch bytes a launch of this shape uses for its last-wave split: the counter block
 // (always counted) and the partial tiles.
-size_t tc_gemm_scratch_bytes(const qgemm_device_s* d, int M, int N, int num_k_blocks);
+size_t tc_gemm_scratch_bytes(const qgemm_device_s* d, int M, int N, int num_k_blocks,
+                             bool full_split = false);
 
 // ---- launchers (each returns a status and never throws) ----
 qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
@@ -119,11 +122,12 @@ qgemm_status launch_bf16_gemm_nk(qgemm_stream_s* s, const void* A, const void* B
 // fp32 entry points (f32_gemm.cu).  C [M,N] = A [M,K] x B [K,N], all fp32 row-major,
 // through three tf32 tensor-core products per fp32 product; the split operands live in
 // the stream's scratch after the GEMM's counter block.
-enum : int { F32_MATMUL = 0, F32_MATMUL_BIAS = 1, F32_SGEMM = 2 };
-size_t f32_gemm_workspace_bytes(const qgemm_device_s* d, int M, int N, int K);
+enum : int { F32_MATMUL = QGEMM_F32_MATMUL, F32_MATMUL_BIAS = QGEMM_F32_MATMUL_BIAS,
+              F32_SGEMM = QGEMM_F32_SGEMM };
+// algo: QGEMM_ALGO_AUTO / _TCGEN05 (3xTF32 tensor cores) / _SIMT (CUDA-core split-K).
 qgemm_status launch_f32_gemm(qgemm_stream_s* s, const float* A, const float* B,
                              const float* bias, float* C, int M, int N, int K, float alpha,
-                             float beta, int mode);
+                             float beta, int mode, int algo);
 qgemm_status launch_f32_gemv(qgemm_stream_s* s, const float* A, const float* x, float* y, int M,
                              int N);
 qgemm_status launch_w8a8_simt(qgemm_stream_s* s, const int8_t* A, const int8_t* B, int b_kn,

@@ -636,13 +636,17 @@ qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src, uint64_t dst, i
 
 // ---- fp32 entry points (MatrixOps / BLASOps) ----
 
-static qgemm_status f32_gemm_entry(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t bias,
-                                   uint64_t C, int M, int N, int K, float alpha, float beta,
-                                   int mode) {
+qgemm_status qgemm_gemm_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t bias, uint64_t C,
+                            int M, int N, int K, float alpha, float beta, int mode, int algo) {
   QG_TRY(enter(s));
   QG_TRY(check_dims(M, N, K));
+  if (mode < QGEMM_F32_MATMUL || mode > QGEMM_F32_SGEMM)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad mode %d", mode);
+  if (algo < QGEMM_ALGO_AUTO || algo > QGEMM_ALGO_SIMT)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad algo %d", algo);
   if (M == 0 || N == 0) return QGEMM_OK;
-  if (!s->dev->tcgen05) return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
+  if (algo == QGEMM_ALGO_TCGEN05 && !s->dev->tcgen05)
+    return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
   if (K > 0) { QG_TRY(need(A, "A")); QG_TRY(need(B, "B")); }
   QG_TRY(need(C, "C"));
   if (mode == F32_MATMUL_BIAS) QG_TRY(need(bias, "bias"));
@@ -652,22 +656,23 @@ static qgemm_status f32_gemm_entry(qgemm_stream_t s, uint64_t A, uint64_t B, uin
     return fail(QGEMM_ERR_UNSUPPORTED, "a split operand of M=%d N=%d K=%d would exceed 64 GiB", M, N, K);
   return launch_f32_gemm(s, reinterpret_cast<const float*>(A), reinterpret_cast<const float*>(B),
                          reinterpret_cast<const float*>(bias), reinterpret_cast<float*>(C), M, N,
-                         K, alpha, beta, mode);
+                         K, alpha, beta, mode, algo);
 }
 
 qgemm_status qgemm_matmul_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t C, int M, int N,
                               int K) {
-  return f32_gemm_entry(s, A, B, 0, C, M, N, K, 1.f, 0.f, F32_MATMUL);
+  return qgemm_gemm_f32(s, A, B, 0, C, M, N, K, 1.f, 0.f, QGEMM_F32_MATMUL, QGEMM_ALGO_AUTO);
 }
 
 qgemm_status qgemm_matmul_add_bias_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t bias,
                                        uint64_t C, int M, int N, int K) {
-  return f32_gemm_entry(s, A, B, bias, C, M, N, K, 1.f, 0.f, F32_MATMUL_BIAS);
+  return qgemm_gemm_f32(s, A, B, bias, C, M, N, K, 1.f, 0.f, QGEMM_F32_MATMUL_BIAS,
+                        QGEMM_ALGO_AUTO);
 }
 
 qgemm_status qgemm_sgemm(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t C, int M, int N, int K,
                          float alpha, float beta) {
-  return f32_gemm_entry(s, A, B, 0, C, M, N, K, alpha, beta, F32_SGEMM);
+  return qgemm_gemm_f32(s, A, B, 0, C, M, N, K, alpha, beta, QGEMM_F32_SGEMM, QGEMM_ALGO_AUTO);
 }
 
 qgemm_status qgemm_gemv_f32(qgemm_stream_t s, uint64_t A, uint64_t x, uint64_t y, int M, int N) {

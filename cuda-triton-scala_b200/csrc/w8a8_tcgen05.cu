@@ -909,7 +909,9 @@ struct TcPlan {
   size_t part_bytes;      // partial tiles after it (0: no split)
 };
 
-static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks) {
+// full_split: a shape with fewer pair tiles than pairs has every tile cut along K (up
+// to 16 parts of at least two k-blocks each) so that the pairs are busy.
+static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, bool full_split) {
   using namespace w8a8;
   TcPlan t;
   // CTA pairs (256 x 256 tiles) whenever the problem has at least one full pair tile.
@@ -930,6 +932,19 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks) {
     t.grid = t.num_tiles < d->sm_count ? t.num_tiles : d->sm_count;
     return t;
   }
+  if (full_split && t.num_tiles < max_pairs) {
+    int parts = max_pairs / t.num_tiles;
+    if (parts > 16) parts = 16;
+    if (parts > num_k_blocks / 2) parts = num_k_blocks / 2;
+    if (parts >= 2) {
+      // every tile is a tail tile: split_w = 0, one K part per pair
+      t.split_w = 0;
+      t.split_s = parts;
+      t.grid = 2 * t.num_tiles * parts;
+      t.part_bytes = (size_t)t.num_tiles * 2 * parts * 128 * 256 * sizeof(int32_t);
+      return t;
+    }
+  }
   const int pairs = t.num_tiles < max_pairs ? t.num_tiles : max_pairs;
   t.grid = 2 * pairs;
   // Last-wave split: when the final round would leave at least three quarters of the
@@ -949,8 +964,9 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks) {
   return t;
 }
 
-size_t tc_gemm_scratch_bytes(const qgemm_device_s* d, int M, int N, int num_k_blocks) {
-  const TcPlan t = tc_plan(d, M, N, num_k_blocks);
+size_t tc_gemm_scratch_bytes(const qgemm_device_s* d, int M, int N, int num_k_blocks,
+                             bool full_split) {
+  const TcPlan t = tc_plan(d, M, N, num_k_blocks, full_split);
   return t.cnt_bytes + t.part_bytes;
 }
 
@@ -961,7 +977,7 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   const int M = a.M, N = a.N, K = a.K;
   const uint64_t kblk = (uint64_t)((K + BK - 1) / BK);
   const int num_k_blocks = (int)kblk * a.nseg;
-  const TcPlan t = tc_plan(s->dev, M, N, num_k_blocks);
+  const TcPlan t = tc_plan(s->dev, M, N, num_k_blocks, a.full_split != 0);
   const bool use_pair = t.use_pair;
   const int bm = use_pair ? pair::BM : BM, bn = use_pair ? pair::BN : BN;
   const uint64_t a_pitch = a.a_pitch ? a.a_pitch : (uint64_t)K;

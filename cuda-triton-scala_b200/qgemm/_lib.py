@@ -93,6 +93,8 @@ SIGNATURES = {
                                                _U64, _SZ]),
     "qgemm_gemm_bf16_nk": (_S, [_P, _U64, _U64, _U64, _I, _I, _I, _I]),
     "qgemm_quantize_per_token": (_S, [_P, _U64, _I, _U64, _U64, _I, _I]),
+    "qgemm_gemm_f32": (_S, [_P, _U64, _U64, _U64, _U64, _I, _I, _I, ctypes.c_float,
+                            ctypes.c_float, _I, _I]),
     "qgemm_matmul_f32": (_S, [_P, _U64, _U64, _U64, _I, _I, _I]),
     "qgemm_matmul_add_bias_f32": (_S, [_P, _U64, _U64, _U64, _U64, _I, _I, _I]),
     "qgemm_sgemm": (_S, [_P, _U64, _U64, _U64, _I, _I, _I, ctypes.c_float, ctypes.c_float]),

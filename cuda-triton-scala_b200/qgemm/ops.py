@@ -154,6 +154,13 @@ class MatrixOps:
         L.call("qgemm_matmul_add_bias_f32", self._h, L.addr(A), L.addr(B), L.addr(bias),
                L.addr(C), M, N, K)
 
+    def gemmF32(self, A, B, C, M: int, N: int, K: int, *, bias=None, alpha: float = 1.0,
+                beta: float = 0.0, mode: int = 0, algo: int = L.ALGO_AUTO):
+        """The general form behind matmul / matmulAddBias / sgemm: mode 0, 1, 2 and a
+        path choice (ALGO_TCGEN05: tensor cores, ALGO_SIMT: CUDA cores)."""
+        L.call("qgemm_gemm_f32", self._h, L.addr(A), L.addr(B), L.addr(bias), L.addr(C), M, N,
+               K, float(alpha), float(beta), int(mode), int(algo))
+
     # -- MatrixOps.scala:166-177
     def gemv(self, A, x, y, M: int, N: int):
         L.call("qgemm_gemv_f32", self._h, L.addr(A), L.addr(x), L.addr(y), M, N)

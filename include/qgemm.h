@@ -246,6 +246,13 @@ QGEMM_API qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t
 QGEMM_API qgemm_status qgemm_quantize_per_token(qgemm_stream_t s, uint64_t x, int in_dtype,
                                                 uint64_t q, uint64_t sA, int M, int K);
 
+/* Epilogues of qgemm_gemm_f32. */
+typedef enum {
+  QGEMM_F32_MATMUL = 0,       /* C = A x B                          */
+  QGEMM_F32_MATMUL_BIAS = 1,  /* C = A x B + bias[N]                */
+  QGEMM_F32_SGEMM = 2         /* C = alpha * (A x B) + beta * C     */
+} qgemm_f32_mode;
+
 /* fp32 entry points of the same facade, all operands fp32 row-major:
  *   qgemm_matmul_f32           C[M,N] = A[M,K] x B[K,N]      MatrixOps.matmul
  *                              (operators/linalg/MatrixOps.scala:16-28)
@@ -253,14 +260,18 @@ QGEMM_API qgemm_status qgemm_quantize_per_token(qgemm_stream_t s, uint64_t x, in
  *   qgemm_sgemm                C = alpha * (A x B) + beta * C BLASOps.sgemm (:230-243);
  *                              C is read whatever beta is, as in the reference
  *   qgemm_gemv_f32             y[M] = A[M,N] x x[N]          MatrixOps.gemv (:166-177)
- * The GEMMs run on the sm_100 tensor cores as three tf32 products per fp32 product
- * (hi/lo splits of both operands) with fp32 sums: |C - exact| <= 1e-5 * sum_k |A*B|
- * terms, the accuracy of the reference's sequential fp32 loop.  An infinite input
- * sends the whole call through a CUDA-core kernel in the reference's own order
- * (bit-identical to the loop).  The split operands (8 * (M + N) * roundup(K, 32)
- * bytes) live in the stream handle's scratch, made or grown by the call (make one call
- * before capturing the stream into a graph).  Deterministic.  Requires sm_100 for the
- * GEMMs; 4-byte aligned pointers. */
+ * The GEMMs (qgemm_gemm_f32 with algo QGEMM_ALGO_AUTO) run on the sm_100 tensor cores
+ * as three tf32 products per fp32 product (hi/lo splits of both operands) with fp32
+ * sums, or, for M <= 64 or N <= 64 (and on other GPUs), on CUDA cores as a split-K fp32
+ * GEMM that reads B once.  Both meet |C - exact| <= 1e-5 * sum_k |A*B| terms, the
+ * accuracy of the reference's sequential fp32 loop.  An infinite input sends the whole
+ * call through a CUDA-core kernel in the reference's own order (bit-identical to the
+ * loop).  Split operands (8 * (M + N) * roundup(K, 32) bytes) or partial sums live in
+ * the stream handle's scratch, made or grown by the call (make one call before
+ * capturing the stream into a graph).  Deterministic.  4-byte aligned pointers. */
+QGEMM_API qgemm_status qgemm_gemm_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t bias,
+                                      uint64_t C, int M, int N, int K, float alpha, float beta,
+                                      int mode, int algo);
 QGEMM_API qgemm_status qgemm_matmul_f32(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t C,
                                         int M, int N, int K);
 QGEMM_API qgemm_status qgemm_matmul_add_bias_f32(qgemm_stream_t s, uint64_t A, uint64_t B,

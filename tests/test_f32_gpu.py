@@ -33,7 +33,12 @@ def rand(shape, rng, scale=1.0):
     return (rng.standard_normal(shape) * scale).astype(np.float32)
 
 
-def run_matmul(gpu, mops, A, B, *, bias=None, C=None, alpha=1.0, beta=0.0):
+ALGOS = {"auto": L.ALGO_AUTO, "tc": L.ALGO_TCGEN05, "simt": L.ALGO_SIMT}
+
+
+def run_matmul(gpu, mops, A, B, *, bias=None, C=None, alpha=1.0, beta=0.0, algo=None):
+    """Through the reference-named entry points, or through qgemm_gemm_f32 with a path
+    choice when `algo` is given."""
     dev, st, _ = gpu
     M, K = A.shape
     N = B.shape[1]
@@ -43,7 +48,11 @@ def run_matmul(gpu, mops, A, B, *, bias=None, C=None, alpha=1.0, beta=0.0):
     m, b = mops
     dA = dev_array(gpu, A if K else np.zeros(1, np.float32))
     dB = dev_array(gpu, B if K else np.zeros(1, np.float32))
-    if C is not None:
+    if algo is not None:
+        mode = 2 if C is not None else (1 if bias is not None else 0)
+        m.gemmF32(dA, dB, out, M, N, K, bias=None if bias is None else dev_array(gpu, bias),
+                  alpha=alpha, beta=beta, mode=mode, algo=ALGOS[algo])
+    elif C is not None:
         b.sgemm(dA, dB, out, M, N, K, alpha, beta)
     elif bias is not None:
         m.matmulAddBias(dA, dB, dev_array(gpu, bias), out, M, N, K)
@@ -81,6 +90,32 @@ def test_matmul(gpu, mops, oracle, M, N, K):
     assert np.isfinite(y).all()
     assert gemm_bound_ratio(y, A, B) <= TOL
     assert gemm_bound_ratio(oracle.matmul_f32(A, B), A, B) <= TOL
+
+
+@pytest.mark.parametrize("algo", ["tc", "simt"])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 5, 7), (64, 300, 129), (65, 66, 67),
+                                   (256, 256, 256), (512, 512, 512), (1024, 768, 640),
+                                   (16, 4096, 1024), (2000, 8, 300), (40, 1030, 4100)])
+def test_matmul_each_path(gpu, mops, M, N, K, algo):
+    # Both paths on every shape class: tiny, ragged, one tile cut into many K parts
+    # (256^3, 512^3), several tiles split, skinny in M or N, long K.
+    rng = np.random.default_rng(M * 5 + N * 11 + K + len(algo))
+    A, B = rand((M, K), rng), rand((K, N), rng)
+    y = run_matmul(gpu, mops, A, B, algo=algo)
+    assert gemm_bound_ratio(y, A, B) <= TOL
+    y2 = run_matmul(gpu, mops, A, B, algo=algo)
+    np.testing.assert_array_equal(y.view(np.uint32), y2.view(np.uint32))  # deterministic
+
+
+@pytest.mark.parametrize("algo", ["tc", "simt"])
+def test_sgemm_each_path(gpu, mops, algo):
+    rng = np.random.default_rng(606)
+    M, N, K = 48, 520, 333
+    A, B, C, bias = rand((M, K), rng), rand((K, N), rng), rand((M, N), rng), rand(N, rng)
+    y = run_matmul(gpu, mops, A, B, C=C, alpha=-0.75, beta=1.5, algo=algo)
+    assert gemm_bound_ratio(y, A, B, C=C, alpha=-0.75, beta=1.5) <= TOL
+    y = run_matmul(gpu, mops, A, B, bias=bias, algo=algo)
+    assert gemm_bound_ratio(y, A, B, bias=bias) <= TOL
 
 
 def test_matmul_small_integers_exact(gpu, mops, oracle):
@@ -167,8 +202,9 @@ def test_nan_propagates(gpu, mops, oracle):
     assert finite_ratio(y, ref, A, B) <= TOL
 
 
+@pytest.mark.parametrize("algo", [None, "simt"])
 @pytest.mark.parametrize("mode", ["matmul", "bias", "sgemm"])
-def test_infinite_inputs_take_the_exact_order_path(gpu, mops, oracle, mode):
+def test_infinite_inputs_take_the_exact_order_path(gpu, mops, oracle, mode, algo):
     # An infinite input routes the whole product to the CUDA-core kernel that runs the
     # reference's loop (k ascending, separate roundings): bit-identical to the oracle,
     # including +-inf where three tf32 products would give inf - inf or inf * 0.
@@ -181,18 +217,18 @@ def test_infinite_inputs_take_the_exact_order_path(gpu, mops, oracle, mode):
     B[11, 7] = np.inf
     bias, C = rand(N, rng), rand((M, N), rng)
     if mode == "matmul":
-        y, ref = run_matmul(gpu, mops, A, B), oracle.matmul_f32(A, B)
+        y, ref = run_matmul(gpu, mops, A, B, algo=algo), oracle.matmul_f32(A, B)
     elif mode == "bias":
-        y = run_matmul(gpu, mops, A, B, bias=bias)
+        y = run_matmul(gpu, mops, A, B, bias=bias, algo=algo)
         ref = oracle.matmul_f32(A, B, bias=bias, mode=1)
     else:
-        y = run_matmul(gpu, mops, A, B, C=C, alpha=0.5, beta=-2.0)
+        y = run_matmul(gpu, mops, A, B, C=C, alpha=0.5, beta=-2.0, algo=algo)
         ref = oracle.matmul_f32(A, B, C=C, alpha=0.5, beta=-2.0, mode=2)
     same_bits(y, ref)
     assert np.isinf(y[2]).sum() > N // 2
     # the next call without infinities is back on the tensor cores and within the bound
     A2, B2 = rand((M, K), rng), rand((K, N), rng)
-    assert gemm_bound_ratio(run_matmul(gpu, mops, A2, B2), A2, B2) <= TOL
+    assert gemm_bound_ratio(run_matmul(gpu, mops, A2, B2, algo=algo), A2, B2) <= TOL
 
 
 def test_matmul_large_sampled(gpu, mops):
@@ -206,7 +242,8 @@ def test_matmul_large_sampled(gpu, mops):
 
 
 @pytest.mark.parametrize("M,N", [(1, 1), (1, 4096), (7, 1001), (4096, 4096), (100000, 64),
-                                 (3, 100003), (513, 36)])
+                                 (3, 100003), (513, 36), (1, 65536), (2, 200000), (100, 5000),
+                                 (600, 3000)])
 def test_gemv(gpu, mops, oracle, M, N):
     dev, st, _ = gpu
     rng = np.random.default_rng(M + N)
@@ -263,6 +300,12 @@ def test_bad_arguments(gpu, mops):
     assert e.value.status == L.ERR_BAD_ALIGN
     with pytest.raises(qgemm.QGemmError) as e:
         m.gemv(16, 0, 16, 4, 4)
+    assert e.value.status == L.ERR_INVALID_ARG
+    with pytest.raises(qgemm.QGemmError) as e:
+        m.gemmF32(16, 16, 16, 4, 4, 4, mode=3)
+    assert e.value.status == L.ERR_INVALID_ARG
+    with pytest.raises(qgemm.QGemmError) as e:
+        m.gemmF32(16, 16, 16, 4, 4, 4, algo=7)
     assert e.value.status == L.ERR_INVALID_ARG
     m.matmul(0, 0, 0, 0, 4, 4)  # M = 0: nothing to do
     m.gemv(0, 0, 0, 0, 4)
