@@ -29,13 +29,14 @@
 // output.  Without the flag that kernel returns at once.  NaN inputs need no such
 // path: they propagate through the three products as they do through the loop.
 //
-// Shapes with few rows or few columns (M <= 64 or N <= 64) would give the tensor cores
-// too few tiles and pay the split passes for nothing.  They run on CUDA cores instead:
-// rows_gemm_kernel<MT> gives each thread one column of B and MT rows of A (A's k-tile
-// in shared memory, B read once, coalesced along N) over one K chunk, fp32 fma, and
-// writes a partial tile; rows_reduce_kernel adds the chunks in chunk order (so the
-// result is deterministic) and applies the epilogue.  The infinity flag and the
-// exact-order kernel work as on the tensor-core path.
+// Shapes that give the tensor cores few tiles (few rows, or small products) would pay
+// the split passes for little; f32_prefer_tc estimates both paths' times and sends
+// those to CUDA cores instead:
+// rows_gemm_kernel<MT> gives each thread 4 columns of B and MT <= 16 rows of A (A's
+// k-tile in shared memory, B read once per 16 rows, coalesced along N) over one K
+// chunk, fp32 fma, and writes a partial tile; rows_reduce_kernel adds the chunks in chunk order (so the
+// result is deterministic) and applies the epilogue; when the kernels saw an infinite
+// input it computes every element in the reference's order instead.
 //
 // gemv (y = A x, A [M,N] row-major) is bound by the read of A: T threads per row
 // (T = 32..256 so that short matrices still fill the GPU), float4 streaming loads,
@@ -189,23 +190,39 @@ __global__ void __launch_bounds__(256) exact_gemm_kernel(const float* __restrict
   }
 }
 
-// Partial products of rows [m0, m0 + MT) (blockIdx.z) x columns [256 bx, +256) over the
-// K chunk [kc * by, +kc): part[by][m][n].  Block 256 threads, one column each.
+// Partial products of rows [m0, m0 + MT) (blockIdx.z) x columns [1024 bx, +1024) over the
+// K chunk [kc * by, +kc): part[by][m][n].  256 threads, each 4 adjacent columns x MT
+// rows (4 * MT accumulators): per k one float4 of B from global memory (coalesced, B
+// read once per row group) and MT / 4 broadcast float4 of A from shared memory for
+// 4 * MT fma.  The B loads of the next 8 k are in flight while 8 k are computed.
+// vec: N % 4 == 0 and B 16-byte aligned (float4 loads and stores).
 template <int MT>
-__global__ void __launch_bounds__(256) rows_gemm_kernel(const float* __restrict__ A,
-                                                        const float* __restrict__ B,
-                                                        float* __restrict__ part, int M, int N,
-                                                        int K, int kc, int* inf_flag) {
-  constexpr int LD = MT + 4;  // row pitch of the transposed A tile (16-byte aligned rows)
-  __shared__ __align__(16) float As[32][LD];
-  const int n = blockIdx.x * 256 + threadIdx.x;
+__global__ void __launch_bounds__(256, 2) rows_gemm_kernel(const float* __restrict__ A,
+                                                           const float* __restrict__ B,
+                                                           float* __restrict__ part, int M,
+                                                           int N, int K, int kc, int vec,
+                                                           int* inf_flag) {
+  __shared__ __align__(16) float As[32][MT];
+  const int n = blockIdx.x * 1024 + 4 * threadIdx.x;
   const int k_begin = blockIdx.y * kc;
   const int k_end = K - k_begin < kc ? K : k_begin + kc;
   const int m0 = blockIdx.z * MT;
-  float acc[MT];
+  float acc[MT][4];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[m][j] = 0.f;
   bool inf = false;
+  auto load_b = [&](int k) -> float4 {
+    const float* src = B + (size_t)k * N + n;
+    if (vec && n + 3 < N) return __ldg(reinterpret_cast<const float4*>(src));
+    float4 v;
+    v.x = n < N ? __ldg(src) : 0.f;
+    v.y = n + 1 < N ? __ldg(src + 1) : 0.f;
+    v.z = n + 2 < N ? __ldg(src + 2) : 0.f;
+    v.w = n + 3 < N ? __ldg(src + 3) : 0.f;
+    return v;
+  };
   for (int k0 = k_begin; k0 < k_end; k0 += 32) {
     const int kn = k_end - k0 < 32 ? k_end - k0 : 32;
     for (int i = threadIdx.x; i < 32 * MT; i += 256) {
@@ -216,33 +233,24 @@ __global__ void __launch_bounds__(256) rows_gemm_kernel(const float* __restrict_
     }
     __syncthreads();
     if (n < N) {
-      if (kn == 32) {
-        float b[32];
+      for (int kb = 0; kb < kn; kb += 8) {
+        float4 b[8];
 #pragma unroll
-        for (int kk = 0; kk < 32; ++kk) b[kk] = __ldg(B + (size_t)(k0 + kk) * N + n);
+        for (int u = 0; u < 8; ++u) b[u] = (kb + u < kn) ? load_b(k0 + kb + u) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int kk = 0; kk < 32; ++kk) {
-          inf |= is_inf(b[kk]);
-#pragma unroll
-          for (int m = 0; m < MT; m += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(&As[kk][m]);
-            acc[m] = fmaf(a.x, b[kk], acc[m]);
-            acc[m + 1] = fmaf(a.y, b[kk], acc[m + 1]);
-            acc[m + 2] = fmaf(a.z, b[kk], acc[m + 2]);
-            acc[m + 3] = fmaf(a.w, b[kk], acc[m + 3]);
-          }
-        }
-      } else {
-        for (int kk = 0; kk < kn; ++kk) {
-          const float b = __ldg(B + (size_t)(k0 + kk) * N + n);
-          inf |= is_inf(b);
+        for (int u = 0; u < 8; ++u) {
+          inf |= is_inf(b[u].x) | is_inf(b[u].y) | is_inf(b[u].z) | is_inf(b[u].w);
 #pragma unroll
           for (int m = 0; m < MT; m += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(&As[kk][m]);
-            acc[m] = fmaf(a.x, b, acc[m]);
-            acc[m + 1] = fmaf(a.y, b, acc[m + 1]);
-            acc[m + 2] = fmaf(a.z, b, acc[m + 2]);
-            acc[m + 3] = fmaf(a.w, b, acc[m + 3]);
+            const float4 a = *reinterpret_cast<const float4*>(&As[kb + u][m]);
+            const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              acc[m + i][0] = fmaf(av[i], b[u].x, acc[m + i][0]);
+              acc[m + i][1] = fmaf(av[i], b[u].y, acc[m + i][1]);
+              acc[m + i][2] = fmaf(av[i], b[u].z, acc[m + i][2]);
+              acc[m + i][3] = fmaf(av[i], b[u].w, acc[m + i][3]);
+            }
           }
         }
       }
@@ -253,23 +261,43 @@ __global__ void __launch_bounds__(256) rows_gemm_kernel(const float* __restrict_
   if (n < N) {
     float* dst = part + ((size_t)blockIdx.y * M + m0) * N + n;
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-      if (m0 + m < M) dst[(size_t)m * N] = acc[m];
+    for (int m = 0; m < MT; ++m) {
+      if (m0 + m >= M) break;
+      float* row = dst + (size_t)m * N;
+      if (vec && n + 3 < N) {
+        *reinterpret_cast<float4*>(row) = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n + j < N) row[j] = acc[m][j];
+      }
+    }
   }
 }
 
-// C = epilogue(sum over chunks of part[c]) unless *flag (the exact-order kernel writes C).
+// C = epilogue(sum over chunks of part[c]).  With *flag set (an infinite input) each
+// element is instead the reference's loop: k ascending, each product and sum rounded on
+// its own (bit-identical to it).
 __global__ void __launch_bounds__(256) rows_reduce_kernel(const float* __restrict__ part,
+                                                          const float* __restrict__ A,
+                                                          const float* __restrict__ B,
                                                           const float* __restrict__ bias,
                                                           float* __restrict__ C, int M, int N,
-                                                          int chunks, float alpha, float beta,
-                                                          int mode, const int* flag) {
-  if (*reinterpret_cast<const volatile int*>(flag) != 0) return;
+                                                          int K, int chunks, float alpha,
+                                                          float beta, int mode, const int* flag) {
+  const bool exact = *reinterpret_cast<const volatile int*>(flag) != 0;
   const size_t total = (size_t)M * N;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
-    float v = __ldcs(part + i);
-    for (int c = 1; c < chunks; ++c) v = __fadd_rn(v, __ldcs(part + (size_t)c * total + i));
+    float v;
+    if (exact) {
+      const size_t m = i / N, n = i % N;
+      v = 0.f;
+      for (int k = 0; k < K; ++k) v = __fadd_rn(v, __fmul_rn(A[m * K + k], B[(size_t)k * N + n]));
+    } else {
+      v = __ldcs(part + i);
+      for (int c = 1; c < chunks; ++c) v = __fadd_rn(v, __ldcs(part + (size_t)c * total + i));
+    }
     if (mode == F32_MATMUL_BIAS) v = __fadd_rn(v, bias[i % N]);
     else if (mode == F32_SGEMM) v = __fadd_rn(__fmul_rn(alpha, v), __fmul_rn(beta, C[i]));
     C[i] = v;
@@ -413,11 +441,13 @@ struct RowsPlan {
 
 static RowsPlan rows_plan(const qgemm_device_s* d, int M, int N, int K) {
   RowsPlan r;
-  r.mt = M <= 4 ? 4 : M <= 8 ? 8 : M <= 16 ? 16 : M <= 32 ? 32 : 64;
-  const int gx = (N + 255) / 256, gz = (M + r.mt - 1) / r.mt;
-  // enough blocks for two waves of two blocks per SM, K chunks of at least 64
-  const long long want = (long long)d->sm_count * 4;
-  long long chunks = (want + (long long)gx * gz - 1) / ((long long)gx * gz);
+  r.mt = M <= 4 ? 4 : M <= 8 ? 8 : 16;
+  const int gx = (N + 1023) / 1024, gz = (M + r.mt - 1) / r.mt;
+  // Two resident blocks per SM (launch bounds); K chunks of at least 64 so that the
+  // partial sums stay small next to the reads of B.
+  const long long slots = (long long)d->sm_count * 2;
+  const long long tiles = (long long)gx * gz;
+  long long chunks = (slots + tiles - 1) / tiles;
   const long long max_chunks = (K + 63) / 64;
   if (chunks > max_chunks) chunks = max_chunks;
   if (chunks < 1) chunks = 1;
@@ -425,6 +455,39 @@ static RowsPlan rows_plan(const qgemm_device_s* d, int M, int N, int K) {
   r.chunks = (K + r.kc - 1) / r.kc;
   r.grid = dim3(gx, r.chunks, gz);
   return r;
+}
+
+// Path choice for QGEMM_ALGO_AUTO from a time estimate of each path, with rates
+// measured on B200 (CUDA events, fp32 inputs in HBM):
+//   tensor cores: ~1.55 TFLOP/s of fp32 work per busy SM for the GEMM (4096^3: 598 of
+//     663 us), SMs busy = min(2 x pair tiles x K parts, SMs) or the 1-CTA tiles; plus
+//     the split passes' 20 bytes per element of A and B at ~6 TB/s; plus ~25 us of
+//     fixed cost (five launches, three tensor maps);
+//   CUDA cores: ~45 TFLOP/s when N fills 1024-column blocks (scaled down by N / 1024
+//     below that) plus ~12 us of fixed cost.
+static bool f32_prefer_tc(const qgemm_device_s* d, int M, int N, int K) {
+  const double flops = 2.0 * M * (double)N * K;
+  const int max_pairs = d->sm_count / 2;
+  double busy;
+  if (M >= 256 && N >= 256) {
+    const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    long long parts = 1;
+    if (tiles < max_pairs) {  // tc_plan's full split
+      const long long kb = 3LL * ((K + 31) / 32);
+      parts = max_pairs / tiles;
+      if (parts > 8) parts = 8;
+      if (parts > kb / 8) parts = kb / 8;
+      if (parts < 2) parts = 1;
+    }
+    busy = 2.0 * (double)tiles * (double)parts;
+  } else {
+    busy = (double)((M + 127) / 128) * (double)((N + 255) / 256);
+  }
+  if (busy > d->sm_count) busy = d->sm_count;
+  const double t_tc = flops / (busy * 1.55e12) + 20.0 * (M + (double)N) * K / 6.0e12 + 25e-6;
+  const double fill = N >= 1024 ? 1.0 : N / 1024.0;
+  const double t_simt = flops / (45e12 * fill) + 12e-6;
+  return t_tc < t_simt;
 }
 
 static qgemm_status launch_exact(qgemm_stream_s* s, const float* A, const float* B,
@@ -452,23 +515,20 @@ static qgemm_status launch_f32_rows(qgemm_stream_s* s, const float* A, const flo
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt + 1024);
   cudaError_t e = cudaMemsetAsync(inf_flag, 0, sizeof(int), s->stream);
   if (e != cudaSuccess) return cuda_fail(e, "clearing the infinity flag");
+  const int vec = (N % 4 == 0) && aligned((uint64_t)B, 16);
   switch (r.mt) {
-    case 4: rows_gemm_kernel<4><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
-    case 8: rows_gemm_kernel<8><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
-    case 16: rows_gemm_kernel<16><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
-    case 32: rows_gemm_kernel<32><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
-    default: rows_gemm_kernel<64><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, inf_flag); break;
+    case 4: rows_gemm_kernel<4><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, vec, inf_flag); break;
+    case 8: rows_gemm_kernel<8><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, vec, inf_flag); break;
+    default: rows_gemm_kernel<16><<<r.grid, 256, 0, s->stream>>>(A, B, part, M, N, K, r.kc, vec, inf_flag); break;
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "rows_gemm launch");
   const size_t elems = (size_t)M * N;
   const size_t cap = (size_t)s->dev->sm_count * 16;
   const int grid = (int)((elems + 255) / 256 < cap ? (elems + 255) / 256 : cap);
-  rows_reduce_kernel<<<grid, 256, 0, s->stream>>>(part, bias, C, M, N, r.chunks, alpha, beta,
-                                                  mode, inf_flag);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "rows_reduce launch");
-  return launch_exact(s, A, B, bias, C, M, N, K, alpha, beta, mode, inf_flag);
+  rows_reduce_kernel<<<grid, 256, 0, s->stream>>>(part, A, B, bias, C, M, N, K, r.chunks, alpha,
+                                                  beta, mode, inf_flag);
+  return cuda_fail(cudaGetLastError(), "rows_reduce launch");
 }
 
 static qgemm_status launch_f32_tc(qgemm_stream_s* s, const float* A, const float* B,
@@ -541,7 +601,7 @@ qgemm_status launch_f32_gemm(qgemm_stream_s* s, const float* A, const float* B,
   }
   bool tc = algo == QGEMM_ALGO_TCGEN05;
   if (algo == QGEMM_ALGO_AUTO)
-    tc = s->dev->tcgen05 && ((M > 64 && N > 64) || (M + 63) / 64 > 65535);
+    tc = s->dev->tcgen05 && (f32_prefer_tc(s->dev, M, N, K) || (M + 15) / 16 > 65535);
   if (tc && !s->dev->tcgen05) return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
   return tc ? launch_f32_tc(s, A, B, bias, C, M, N, K, alpha, beta, mode)
             : launch_f32_rows(s, A, B, bias, C, M, N, K, alpha, beta, mode);

@@ -910,7 +910,7 @@ struct TcPlan {
 };
 
 // full_split: a shape with fewer pair tiles than pairs has every tile cut along K (up
-// to 16 parts of at least two k-blocks each) so that the pairs are busy.
+// to 8 parts of at least 8 k-blocks each) so that more pairs are busy.
 static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, bool full_split) {
   using namespace w8a8;
   TcPlan t;
@@ -933,9 +933,12 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, b
     return t;
   }
   if (full_split && t.num_tiles < max_pairs) {
+    // at most 8 parts of at least 8 k-blocks: the part that finishes last adds all the
+    // partial tiles alone, so many short parts cost more than they save (512^3 with
+    // 16 parts of 3 k-blocks: 89 us against 54 unsplit)
     int parts = max_pairs / t.num_tiles;
-    if (parts > 16) parts = 16;
-    if (parts > num_k_blocks / 2) parts = num_k_blocks / 2;
+    if (parts > 8) parts = 8;
+    if (parts > num_k_blocks / 8) parts = num_k_blocks / 8;
     if (parts >= 2) {
       // every tile is a tail tile: split_w = 0, one K part per pair
       t.split_w = 0;
