@@ -39,8 +39,11 @@ METRIC = "W8A8 GEMM TOPS & W4A16 GEMV HBM GB/s at 1/2/4/8 B200, % of roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch from one `ncu --set full` capture of the same
 # kernel on the same workload (profiles/w8a8_tcgen05_pair_4096.md, profiles/w4a16_tile_m1.md).
-NCU_TRAFFIC_W8A8_4096 = 33626112 + 2321920
+NCU_TRAFFIC_W8A8_4096 = 33694208 + 3904000
 NCU_TRAFFIC_W4A16_M1 = 30312704 + 256
+# dram__bytes_read.sum + dram__bytes_write.sum of one tf32 GEMM launch of the fp32
+# matmul at 4096^3 (ncu --set full, profiles/f32_tf32_pair_4096.md)
+NCU_TRAFFIC_F32_GEMM_4096 = 985069568 + 61620736
 
 
 def parse_args():
@@ -495,6 +498,7 @@ def f32_facade(st, peaks, steps=10):
     fl = 2.0 * M * N * K
     tf32_peak = 0.5 * peaks["bf16_tflops"]
     res["matmul_4096"] = {"us": t * 1e6, "TFLOP_s": fl / t / 1e12,
+                          "gemm_kernel_traffic_bytes": NCU_TRAFFIC_F32_GEMM_4096,
                           "tensor_TFLOP_s": 3 * fl / t / 1e12,
                           "tensor_frac_of_tf32_peak": 3 * fl / t / 1e12 / tf32_peak,
                           "tf32_peak_basis": "0.5 x measured bf16_tflops (dense tf32 runs at "
