@@ -460,16 +460,18 @@ static RowsPlan rows_plan(const qgemm_device_s* d, int M, int N, int K) {
 // Path choice for QGEMM_ALGO_AUTO from a time estimate of each path, with rates
 // measured on B200 (CUDA events, fp32 inputs in HBM):
 //   tensor cores: ~1.55 TFLOP/s of fp32 work per busy SM for the GEMM (4096^3: 598 of
-//     663 us), SMs busy = min(2 x pair tiles x K parts, SMs) or the 1-CTA tiles; plus
-//     the split passes' 20 bytes per element of A and B at ~6 TB/s; plus ~25 us of
-//     fixed cost (five launches, three tensor maps);
-//   CUDA cores: ~45 TFLOP/s when N fills 1024-column blocks (scaled down by N / 1024
-//     below that) plus ~12 us of fixed cost.
+//     663 us), SMs busy = min(2 x pair tiles x K parts, SMs) (pairs also for shapes
+//     whose 1-CTA tiles cannot fill the GPU) or the 1-CTA tiles; plus
+//     the split passes' 20 bytes per element of A and B at ~6 TB/s; plus ~40 us of
+//     fixed cost (launches, tensor maps, pipeline fill; 256^3 takes 45 us);
+//   CUDA cores: ~24 TFLOP/s when N fills 1024-column blocks (scaled down by N / 1024
+//     below that) plus ~15 us of fixed cost.
 static bool f32_prefer_tc(const qgemm_device_s* d, int M, int N, int K) {
   const double flops = 2.0 * M * (double)N * K;
   const int max_pairs = d->sm_count / 2;
-  double busy;
-  if (M >= 256 && N >= 256) {
+  double busy, work;  // busy SMs; fp32 work of the whole tiles (edges included)
+  const double tiles1 = (double)((M + 127) / 128) * (double)((N + 255) / 256);
+  if ((M >= 256 && N >= 256) || tiles1 < d->sm_count) {  // tc_plan's pair choice
     const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
     long long parts = 1;
     if (tiles < max_pairs) {  // tc_plan's full split
@@ -480,13 +482,15 @@ static bool f32_prefer_tc(const qgemm_device_s* d, int M, int N, int K) {
       if (parts < 2) parts = 1;
     }
     busy = 2.0 * (double)tiles * (double)parts;
+    work = 2.0 * (double)tiles * 256.0 * 256.0 * K;
   } else {
-    busy = (double)((M + 127) / 128) * (double)((N + 255) / 256);
+    busy = tiles1;
+    work = 2.0 * tiles1 * 128.0 * 256.0 * K;
   }
   if (busy > d->sm_count) busy = d->sm_count;
-  const double t_tc = flops / (busy * 1.55e12) + 20.0 * (M + (double)N) * K / 6.0e12 + 25e-6;
+  const double t_tc = work / (busy * 1.55e12) + 20.0 * (M + (double)N) * K / 6.0e12 + 40e-6;
   const double fill = N >= 1024 ? 1.0 : N / 1024.0;
-  const double t_simt = flops / (45e12 * fill) + 12e-6;
+  const double t_simt = flops / (24e12 * fill) + 15e-6;
   return t_tc < t_simt;
 }
 

@@ -391,7 +391,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
     }
     ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
     ptx::named_bar_sync(1, 128);
-    if (elected && !skip) {
+    if (elected && !skip && row0 < p.M && n0 + ch * cwe < p.N) {  // blocks past the edge: nothing to store
       ptx::tma_store_2d(tmO, buf, n0 + ch * cwe, row0);
       ptx::bulk_commit_group();
     }
@@ -914,8 +914,12 @@ struct TcPlan {
 static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, bool full_split) {
   using namespace w8a8;
   TcPlan t;
-  // CTA pairs (256 x 256 tiles) whenever the problem has at least one full pair tile.
-  t.use_pair = M >= 256 && N >= 256 && d->sm_count >= 2;
+  // CTA pairs (256 x 256 tiles) whenever the problem has at least one full pair tile;
+  // with full_split also for smaller shapes whose 1-CTA tiles cannot fill the GPU
+  // (rows and columns past the edges are zero-filled by TMA and never stored).
+  const long long tiles1 = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  t.use_pair = d->sm_count >= 2 &&
+               ((M >= 256 && N >= 256) || (full_split && tiles1 < d->sm_count));
   const int bm = t.use_pair ? pair::BM : BM, bn = t.use_pair ? pair::BN : BN;
   t.num_tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
   t.split_w = t.num_tiles;
