@@ -48,10 +48,16 @@ constexpr int W_BYTES = SR * TWB;       // 16 KB
 constexpr int S_BYTES = 32 * TW * 2;    // up to 32 scale rows (group >= 16) x 64 columns
 constexpr int MAX_KS = 8;
 
+// MT = 1, 2: two CTAs per SM.  MT = 4 (32 activation rows): one CTA per SM, whose
+// register file holds the 4x accumulators; the weights are streamed once for 32 rows
+// instead of twice for two 16-row passes.  Measured on B200 (M = 32): 1.86x faster when
+// the 16-row grid would leave SMs idle (N=4096, K=11008: 27.5 against 51.2 us), ~2 %
+// slower when it already covers every SM (N=14336, K=4096: 38.7 against 37.8 us).
 template <int MT>
 struct Cfg {
   static constexpr int MR = 8 * MT;
-  static constexpr int STAGES = MT == 1 ? 3 : 2;  // two CTAs per SM either way
+  static constexpr int STAGES = MT == 2 ? 2 : 3;
+  static constexpr int CTAS_PER_SM = MT == 4 ? 1 : 2;
   static constexpr int X_BYTES = SR * MR * 2;
   static constexpr int STAGE_BYTES = W_BYTES + S_BYTES + X_BYTES;
   static constexpr int RED_BYTES = NCW * MR * TW * 4;
@@ -113,7 +119,8 @@ __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 template <int MT>
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(THREADS, Cfg<MT>::CTAS_PER_SM)
+    __maxnreg__(MT == 4 ? 224 : 96)
     w4a16_tile_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmX,
                       const Params p) {
   using C = Cfg<MT>;
@@ -381,7 +388,8 @@ bool w4a16_tile_supported(const qgemm_device_s* d, uint64_t x, uint64_t wt, uint
                           int N, int K, int G, const char** why) {
   auto no = [&](const char* w) { if (why) *why = w; return false; };
   if (!d->tcgen05) return no("device is not sm_100");
-  const int smem = M > 8 ? w4x::Cfg<2>::SMEM_BYTES : w4x::Cfg<1>::SMEM_BYTES;
+  const int smem = M > 16 ? w4x::Cfg<4>::SMEM_BYTES  // the larger of the M > 16 configs
+                 : M > 8 ? w4x::Cfg<2>::SMEM_BYTES : w4x::Cfg<1>::SMEM_BYTES;
   if (d->smem_optin < (size_t)smem) return no("not enough shared memory per block");
   if (K % 16 != 0) return no("K must be a multiple of 16");
   // every 512-row stage starts on a group boundary and every 16-row chunk lies in
@@ -402,9 +410,13 @@ qgemm_status launch_w4a16_tile(qgemm_stream_s* s, const void* x, const uint8_t* 
                                const void* sc, int zp, int G, void* y, int M, int N, int K) {
   using namespace w4x;
   qgemm_device_s* d = s->dev;
-  const bool mt2 = M > 8;
-  const int MR = mt2 ? 16 : 8;
-  const int smem = mt2 ? Cfg<2>::SMEM_BYTES : Cfg<1>::SMEM_BYTES;
+  const int ntiles0 = (N + TW - 1) / TW;
+  const int Kr0 = (K + SR - 1) / SR * SR;
+  // MT = 4 for M > 16 when the 16-row grid has no more CTAs than SMs
+  const bool wide = M > 16 && ntiles0 * choose_ks(ntiles0, Kr0, d->sm_count) <= d->sm_count;
+  const int mti = wide ? 2 : M > 8 ? 1 : 0;  // MT = 4, 2, 1
+  const int MR = 8 << mti;
+  const int smem = mti == 2 ? Cfg<4>::SMEM_BYTES : mti == 1 ? Cfg<2>::SMEM_BYTES : Cfg<1>::SMEM_BYTES;
   const int ntiles = (N + TW - 1) / TW;
   Params p;
   p.M = M; p.N = N; p.K = K; p.G = G; p.zp = zp;
@@ -423,14 +435,14 @@ qgemm_status launch_w4a16_tile(qgemm_stream_s* s, const void* x, const uint8_t* 
     return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for the W4A16 operands");
 
   void (*kern)(const CUtensorMap, const CUtensorMap, const Params) =
-      mt2 ? w4a16_tile_kernel<2> : w4a16_tile_kernel<1>;
-  static bool attr_done[64][2] = {};
+      mti == 2 ? w4a16_tile_kernel<4> : mti == 1 ? w4a16_tile_kernel<2> : w4a16_tile_kernel<1>;
+  static bool attr_done[64][3] = {};
   const int ord = d->ordinal;
-  if (ord >= 0 && ord < 64 && !attr_done[ord][mt2]) {
+  if (ord >= 0 && ord < 64 && !attr_done[ord][mti]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_tile)");
-    attr_done[ord][mt2] = true;
+    attr_done[ord][mti] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.KS, ntiles, 1);
