@@ -11,8 +11,12 @@
 // with IEEE fp32 division and multiplication (no fused or approximate forms), so the
 // result is bit-identical to the reference arithmetic.  x is fp32 or bf16 (widened).
 //
-// One CTA per row: a first pass over the row finds maxAbs (block reduction), a second
-// pass (served from L2) writes the int8 row.  HBM-bound: one read of x, one write of q.
+// One CTA per row.  Rows of up to 256 x 4 vectors of 16 bytes (bf16: K <= 8192,
+// fp32: K <= 4096) with 16-byte aligned rows are read once into registers with vector
+// loads, reduced to maxAbs, quantised from the registers and written with vector
+// stores (quantize_rows_vec_kernel).  Other rows take two passes: maxAbs, then the
+// int8 row, the second pass served from L2 (quantize_rows_kernel).  HBM-bound: one
+// read of x, one write of q.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -88,11 +92,129 @@ __global__ void __launch_bounds__(THREADS) quantize_rows_kernel(const T* __restr
   }
 }
 
+// Block-wide maxAbs of per-thread maxima, in the "if (v > m) m = v" form (NaN never
+// replaces a number); thread 0 also writes sA[m].  Returns 127 / maxAbs (or 1).
+__device__ __forceinline__ float block_mul(float mx, float* sA, int m) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, mx, off);
+    if (o > mx) mx = o;
+  }
+  __shared__ float wmax[THREADS / 32];
+  __shared__ float bcast;
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = wmax[0];
+    for (int w = 1; w < THREADS / 32; ++w)
+      if (wmax[w] > v) v = wmax[w];
+    bcast = (v > 1e-6f) ? __fdiv_rn(127.0f, v) : 1.0f;
+    sA[m] = __fdiv_rn(v, 127.0f);
+  }
+  __syncthreads();
+  return bcast;
+}
+
+// 16-byte vectors of T: 8 bf16 or 4 fp32.
+template <typename T> struct Vec;
+template <> struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+  __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = __ldcs(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+};
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const float* p, float (&v)[4]) {
+    const float4 u = __ldcs(reinterpret_cast<const float4*>(p));
+    v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+  }
+};
+
+// One row per CTA, NV vectors per thread held in registers; K % VEC == 0 and 16-byte
+// aligned rows of x, (VEC)-byte aligned rows of q.
+template <typename T, int NV>
+__global__ void __launch_bounds__(THREADS) quantize_rows_vec_kernel(const T* __restrict__ x,
+                                                                    int8_t* __restrict__ q,
+                                                                    float* __restrict__ sA,
+                                                                    int M, int K) {
+  constexpr int VEC = Vec<T>::N;
+  const int m = blockIdx.x;
+  if (m >= M) return;
+  const T* row = x + (size_t)m * K;
+  const int nvec = K / VEC;
+  float v[NV][VEC];
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int vi = threadIdx.x + j * THREADS;
+    if (vi < nvec) {
+      Vec<T>::load(row + (size_t)vi * VEC, v[j]);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const float a = fabsf(v[j][i]);
+        if (a > mx) mx = a;
+      }
+    }
+  }
+  const float mul = block_mul(mx, sA, m);
+  int8_t* qrow = q + (size_t)m * K;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int vi = threadIdx.x + j * THREADS;
+    if (vi < nvec) {
+      uint32_t packed[VEC / 4];
+#pragma unroll
+      for (int w = 0; w < VEC / 4; ++w) {
+        uint32_t b = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          b |= (uint32_t)(uint8_t)quant(v[j][4 * w + i], mul) << (8 * i);
+        packed[w] = b;
+      }
+      if constexpr (VEC == 8)
+        *reinterpret_cast<uint2*>(qrow + (size_t)vi * VEC) = make_uint2(packed[0], packed[1]);
+      else
+        *reinterpret_cast<uint32_t*>(qrow + (size_t)vi * VEC) = packed[0];
+    }
+  }
+}
+
 }  // namespace qtok
 
 qgemm_status launch_quantize_tokens(qgemm_stream_s* s, const void* x, int in_dtype, int8_t* q,
                                     float* sA, int M, int K) {
   using namespace qtok;
+  const bool bf = in_dtype == QGEMM_BF16;
+  const int VEC = bf ? 8 : 4;
+  const int nv = (K / VEC + THREADS - 1) / THREADS;  // vectors per thread
+  const bool vec = K > 0 && K % VEC == 0 && nv <= 4 && aligned((uint64_t)x, 16) &&
+                   ((uint64_t)K * (bf ? 2 : 4)) % 16 == 0 && aligned((uint64_t)q, VEC) &&
+                   K % VEC == 0;
+  if (vec) {
+    if (bf) {
+      const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+      switch (nv) {
+        case 1: quantize_rows_vec_kernel<__nv_bfloat16, 1><<<M, THREADS, 0, s->stream>>>(xb, q, sA, M, K); break;
+        case 2: quantize_rows_vec_kernel<__nv_bfloat16, 2><<<M, THREADS, 0, s->stream>>>(xb, q, sA, M, K); break;
+        default: quantize_rows_vec_kernel<__nv_bfloat16, 4><<<M, THREADS, 0, s->stream>>>(xb, q, sA, M, K); break;
+      }
+    } else {
+      const float* xf = static_cast<const float*>(x);
+      switch (nv) {
+        case 1: quantize_rows_vec_kernel<float, 1><<<M, THREADS, 0, s->stream>>>(xf, q, sA, M, K); break;
+        case 2: quantize_rows_vec_kernel<float, 2><<<M, THREADS, 0, s->stream>>>(xf, q, sA, M, K); break;
+        default: quantize_rows_vec_kernel<float, 4><<<M, THREADS, 0, s->stream>>>(xf, q, sA, M, K); break;
+      }
+    }
+    return cuda_fail(cudaGetLastError(), "quantize_rows_vec launch");
+  }
   if (in_dtype == QGEMM_BF16)
     quantize_rows_kernel<__nv_bfloat16><<<M, THREADS, 0, s->stream>>>(
         static_cast<const __nv_bfloat16*>(x), q, sA, M, K);

@@ -127,7 +127,11 @@ def test_unshard_columns(gpu, world, M, ncols):
 
 
 @pytest.mark.parametrize("M,K,dt", [(7, 300, "f32"), (64, 4096, "bf16"), (3, 13, "f32"),
-                                    (129, 1024, "bf16")])
+                                    (129, 1024, "bf16"),
+                                    # rows held in registers: 3 and 4 vectors per thread
+                                    (5, 6000, "bf16"), (4, 4096, "f32"), (3, 8192, "bf16"),
+                                    # rows too long for registers, or K not a multiple of 8
+                                    (2, 8200, "bf16"), (3, 4100, "f32"), (6, 1028, "bf16")])
 def test_quantize_per_token_matches_reference_rows(gpu, oracle, M, K, dt):
     """Per-token quantisation == the reference dynamicQuantize applied to x^T, bit for bit
     (scales and int8 values), for fp32 and bf16 activations."""
