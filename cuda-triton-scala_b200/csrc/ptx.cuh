@@ -157,6 +157,13 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// Load with acquire semantics at GPU scope (pairs with a writer's fence + atomic).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Programmatic dependent launch: wait for the previous kernel in the stream to
 // complete (and its writes to be visible); let the next kernel start launching.
 __device__ __forceinline__ void grid_dependency_wait() {

@@ -271,17 +271,21 @@ __device__ __forceinline__ size_t part_index(int c, int v, int rl) {
   return ((size_t)(c * 8 + v) * 128 + rl);
 }
 
-// With `parts` set, the accumulators are not read from TMEM but summed from `nparts`
-// partial tiles, `part_stride` words apart, in part order: int32 sums, or fp32 sums
-// when `fp` (the words are then fp32 accumulators).
+// With `parts` set, the accumulators are summed from `nparts` partial tiles,
+// `part_stride` words apart, in part order: int32 sums, or fp32 sums when `fp` (the
+// words are then fp32 accumulators).  from_r: the sum starts from r's values (the
+// final part's own accumulator) instead of zero.
 __device__ __forceinline__ uint32_t add_word(uint32_t a, int b, bool fp) {
   return fp ? __float_as_uint(__fadd_rn(__uint_as_float(a), __int_as_float(b))) : a + (uint32_t)b;
 }
 
 __device__ __forceinline__ void sum_parts(const int32_t* parts, int nparts, size_t part_stride,
-                                          int rl, int col, bool fp, uint32_t (&r)[32]) {
+                                          int rl, int col, bool fp, uint32_t (&r)[32],
+                                          bool from_r = false) {
+  if (!from_r) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) r[j] = 0u;  // also fp32 +0
+    for (int j = 0; j < 32; ++j) r[j] = 0u;  // also fp32 +0
+  }
   for (int pp = 0; pp < nparts; ++pp) {
     const int4* src = reinterpret_cast<const int4*>(parts + pp * part_stride);
 #pragma unroll
@@ -300,7 +304,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
                                               int lane, int row0, int n0, uint32_t stg,
                                               bool elected, int& chunk_seq, bool ok,
                                               const int32_t* parts = nullptr, int nparts = 0,
-                                              size_t part_stride = 0) {
+                                              size_t part_stride = 0, bool add_tmem = false) {
   const int row = row0 + q * 32 + lane;
   const int rl = q * 32 + lane;  // row within the staging block
   const float sa = (!p.fp_acc && row < p.M) ? __ldg(p.sA + row) : 0.f;
@@ -311,12 +315,11 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       uint32_t r[32];
       __syncwarp();
       if (!ok) return;
-      if (parts) {
-        sum_parts(parts, nparts, part_stride, rl, c * 32, p.fp_acc != 0, r);
-      } else {
+      if (!parts || add_tmem) {
         ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + c * 32, r);
         ptx::tmem_wait_ld();
       }
+      if (parts) sum_parts(parts, nparts, part_stride, rl, c * 32, p.fp_acc != 0, r, add_tmem);
       if (!skip) store_chunk(p, row, n0 + c * 32, sa, r);
     }
     return;
@@ -334,13 +337,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       uint32_t r[32];
       const int nc = n0 + ch * cwe + sub * 32;
       __syncwarp();
-      if (ok && parts) {
-        sum_parts(parts, nparts, part_stride, rl, ch * cwe + sub * 32, p.fp_acc != 0, r);
-      } else if (ok) {
+      if (ok && (!parts || add_tmem)) {
         ptx::tmem_ld_32x32b_x32(
             tmem_base + ((uint32_t)(q * 32) << 16) + acc_col + (uint32_t)(ch * cwe + sub * 32), r);
         ptx::tmem_wait_ld();
-      } else {
+      }
+      if (ok && parts) {
+        sum_parts(parts, nparts, part_stride, rl, ch * cwe + sub * 32, p.fp_acc != 0, r, add_tmem);
+      } else if (!ok) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = 0u;  // a wait ran out: keep the barrier sequence
       }
@@ -798,40 +802,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
         continue;
       }
-      // A K part of a tail tile: park the int32 partial sums of this CTA's 128 rows,
-      // then count in; the last part of the tile adds all parts and stores the tile.
+      // A K part of a tail tile.  Parts 0 .. split_s-2 park their partial sums (this
+      // CTA's 128 rows) and count in.  The final part (the last K range) waits until the
+      // others have counted in, adds their partials to its own accumulator in TMEM and
+      // stores the tile; it neither writes nor re-reads a partial of its own.
       const size_t slot_ints = (size_t)128 * 256;
       const int tt = (tile - p.split_w) * 2 + (int)rank;
-      int4* mine = reinterpret_cast<int4*>(p.part + ((size_t)tt * p.split_s + part) * slot_ints);
+      if (part < p.split_s - 1) {
+        int4* mine = reinterpret_cast<int4*>(p.part + ((size_t)tt * p.split_s + part) * slot_ints);
 #pragma unroll 1
-      for (int c = 0; c < 256 / 32; ++c) {
-        uint32_t r[32];
-        __syncwarp();
-        if (ok) {
-          ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN + c * 32), r);
-          ptx::tmem_wait_ld();
-        } else {
+        for (int c = 0; c < 256 / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          if (ok) {
+            ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN + c * 32), r);
+            ptx::tmem_wait_ld();
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = 0u;
+            for (int j = 0; j < 32; ++j) r[j] = 0u;
+          }
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            mine[part_index(c, v, rl)] =
+                make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
         }
-#pragma unroll
-        for (int v = 0; v < 8; ++v)
-          mine[part_index(c, v, rl)] =
-              make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
-      }
-      ptx::tc_fence_before();
-      ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);  // TMEM is free again
-      __threadfence();
-      ptx::named_bar_sync(1, 128);
-      if (elected) *last_flag = atomicAdd(p.cnt + tt, 1) == p.split_s - 1;
-      ptx::named_bar_sync(1, 128);
-      if (*last_flag) {
+        ptx::tc_fence_before();
+        ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);  // TMEM is free again
         __threadfence();
-        epilogue_tile(p, &tmO, tmem_base, 0u, q, lane, mb * BM + (int)rank * 128, nb * BN,
-                      stg_base, elected, chunk_seq, ok,
-                      p.part + (size_t)tt * p.split_s * slot_ints, p.split_s, slot_ints);
-        if (elected) p.cnt[tt] = 0;
+        ptx::named_bar_sync(1, 128);
+        if (elected) atomicAdd(p.cnt + tt, 1);
+        continue;
       }
+      if (elected) {
+        // bounded wait for the other parts' count-ins (all CTAs of the grid are resident,
+        // and the other parts wait on nothing of this one)
+        bool got = false;
+        const unsigned long long t0 = ptx::globaltimer();
+        for (;;) {
+          if (ptx::ld_acquire_gpu(p.cnt + tt) >= p.split_s - 1) { got = true; break; }
+          if (*abort_flag || ptx::globaltimer() - t0 > ptx::kWaitLimitNs) break;
+          __nanosleep(64);
+        }
+        if (!got && !*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag, rank);
+        *last_flag = got ? 1 : 0;
+      }
+      ptx::named_bar_sync(1, 128);
+      const bool ready = ok && *last_flag != 0;
+      epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM + (int)rank * 128,
+                    nb * BN, stg_base, elected, chunk_seq, ready,
+                    p.part + (size_t)tt * p.split_s * slot_ints, p.split_s - 1, slot_ints, true);
+      ptx::tc_fence_before();
+      ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
+      if (elected) p.cnt[tt] = 0;
       ptx::named_bar_sync(1, 128);  // the flag is rewritten only after everyone read it
     }
     if (elected) ptx::bulk_wait_group_all();
@@ -956,9 +978,10 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, b
   t.grid = 2 * pairs;
   // Last-wave split: when the final round would leave at least three quarters of the
   // pairs idle, cut each leftover tile along K into 4 parts (at least two k-blocks
-  // each).  Measured: a K part runs at about 0.27 of a tile plus its share of the
-  // k-blocks and the partial sums add about a quarter of a tile, so two-way splits
-  // (4096^3: 34 leftover tiles on 74 pairs) lose and four-way ones win.
+  // each).  Measured (bf16 out, [K,N] B): four-way splits win (3840x4096x4096:
+  // 1931 against 1874 TOPS unsplit); two-way splits lose even with the final part
+  // adding the others' partials in TMEM (4096^3: 2295 against 2511; 4096x4096x2048:
+  // 1494 against 1825).
   const int rounds = t.num_tiles / pairs, rest = t.num_tiles - rounds * pairs;
   int parts = (rest > 0 && rest * 4 <= pairs) ? 4 : 1;
   while (parts > 1 && num_k_blocks / parts < 2) --parts;
