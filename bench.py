@@ -826,15 +826,20 @@ def main():
     int8_peak = 2.0 * peaks["bf16_tflops"]
     int8_sustained = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     achieved = hb["ops_per_launch"] / hb["per_launch_s"] / 1e12
+    # The timed steps follow one second of back-to-back launches (so that the clock
+    # sampler sees the timed region under load): the kernel runs at sustained clocks
+    # and is set against the sustained peak; the burst fraction is reported beside it.
     roofline = {"bound": "tensor", "kernel": "w8a8_tcgen05_pair_kernel", "achieved": achieved,
-                "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
+                "peak": int8_sustained, "unit": "TOPS", "frac": achieved / int8_sustained,
                 "traffic": NCU_TRAFFIC_W8A8_4096,
                 "algorithmic_ops_per_launch": hb["ops_per_launch"],
                 "algorithmic_bytes_per_launch": hb["M"] * hb["K"] + hb["K"] * hb["N"]
                 + 2 * hb["M"] * hb["N"] + 4 * (hb["M"] + hb["N"]),
-                "peak_basis": f"2 x bf16_tflops ({peak_src}, burst cuBLAS bf16): dense int8 "
-                              f"runs at twice the bf16 rate on B200",
-                "frac_of_sustained_peak": achieved / int8_sustained}
+                "peak_basis": f"2 x bf16_tflops_sustained ({peak_src}: cuBLAS bf16 back to back "
+                              f"for seconds under the power cap): dense int8 runs at twice the "
+                              f"bf16 rate on B200; the timed steps follow 1 s of sustained load",
+                "burst_peak": int8_peak,
+                "frac_of_burst_peak": achieved / int8_peak}
     libctx = library_int8_context(hb, K) if rank == 0 else None
     pipe = w8a8_pipeline(ops, hb, max(10, min(K, 50)), peaks) if rank == 0 else None
     log("e2e")
