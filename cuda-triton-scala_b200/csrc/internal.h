@@ -115,8 +115,8 @@ bool w8a8_tcgen05_supported(const qgemm_device_s* d, uint64_t A, uint64_t B, int
                             const char** why);
 // bf16 GEMM on the same tcgen05 kernels: out[M, ldc] (bf16, RNE) = A[M,K] * B[N,K]^T,
 // fp32 accumulation.  A and B bf16, K-major; K % 8 == 0; 16-byte aligned A and B.
-// a_repeat = r > 1: B rows hold r blocks of K values, each padded with zeros to a
-// multiple of 64, and out = sum_i A * B_i^T.
+// a_repeat = 2: B rows hold 2 blocks of K values, each padded with zeros to a
+// multiple of 64, and out = A * B_0^T + A * B_1^T (two K segments of one launch).
 qgemm_status launch_bf16_gemm_nk(qgemm_stream_s* s, const void* A, const void* B, void* out,
                                  int ldc, int M, int N, int K, int a_repeat = 1);
 // fp32 entry points (f32_gemm.cu).  C [M,N] = A [M,K] x B [K,N], all fp32 row-major,
