@@ -378,6 +378,7 @@ __global__ void __launch_bounds__(256) gemv_split_kernel(const float* __restrict
   if (vec) {  // N % 4 == 0 and j0 % 4 == 0
     const float4* a4 = reinterpret_cast<const float4*>(a);
     const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 4
     for (int j = j0 / 4 + threadIdx.x; j < j1 / 4; j += 256) {
       const float4 av = __ldcs(a4 + j), xv = __ldg(x4 + j);
       s0 = fmaf(av.x, xv.x, s0);
@@ -402,14 +403,24 @@ __global__ void __launch_bounds__(256) gemv_split_kernel(const float* __restrict
   }
 }
 
-// y[row] = sum of the row's chunks, in chunk order.
-__global__ void gemv_reduce_kernel(const float* __restrict__ part, float* __restrict__ y, int M,
-                                   int chunks) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= M) return;
-  float s = part[(size_t)row * chunks];
-  for (int c = 1; c < chunks; ++c) s += part[(size_t)row * chunks + c];
-  y[row] = s;
+// y[row] = sum of the row's chunks: one block per row; thread t adds chunks t, t + 256,
+// ... in order, then a fixed shuffle / shared-memory tree (deterministic).
+__global__ void __launch_bounds__(256) gemv_reduce_kernel(const float* __restrict__ part,
+                                                          float* __restrict__ y, int chunks) {
+  const float* pr = part + (size_t)blockIdx.x * chunks;
+  float s = 0.f;
+  for (int c = threadIdx.x; c < chunks; c += 256) s += pr[c];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w];
+    y[blockIdx.x] = t;
+  }
 }
 
 }  // namespace f32
@@ -634,7 +645,7 @@ qgemm_status launch_f32_gemv(qgemm_stream_s* s, const float* A, const float* x, 
       gemv_split_kernel<<<dim3(nch, M), 256, 0, s->stream>>>(A, x, part, N, L, vec);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(e, "gemv_split launch");
-      gemv_reduce_kernel<<<(M + 255) / 256, 256, 0, s->stream>>>(part, y, M, nch);
+      gemv_reduce_kernel<<<M, 256, 0, s->stream>>>(part, y, nch);
       return cuda_fail(cudaGetLastError(), "gemv_reduce launch");
     }
   }
