@@ -55,7 +55,8 @@ def parse_args():
     p.add_argument("--no-large", action="store_true", help="skip the sharded large GEMM")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-llama", action="store_true", help="skip the Llama-shaped W4A16 stack")
-    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large", "llama", "f32"], default="all",
+    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large", "llama", "f32", "side"],
+                   default="all",
                    help="run one workload alone (for profiling); prints its own JSON line")
     p.add_argument("--profile", action="store_true",
                    help="with --only w8a8|w4a16: warmup + steps plain launches and nothing "
@@ -531,6 +532,47 @@ def f32_facade(st, peaks, steps=10):
     return res
 
 
+def side_kernels(st, ops, steps, warmup):
+    """The facade's smaller kernels on their own, each `warmup` + `steps` launches:
+    fp32 gemv A [16384, 16384], per-token quantisation of x [4096, 4096] bf16, and the
+    CUDA-core fp32 GEMM at 64 x 4096 x 4096 (the case profiles/ cite)."""
+    import torch
+    import qgemm
+    m = qgemm.MatrixOps(st)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2)
+
+    def run(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / steps
+
+    res = {}
+    A = torch.randn((16384, 16384), device="cuda", generator=gen)
+    x = torch.randn((16384,), device="cuda", generator=gen)
+    y = torch.empty((16384,), device="cuda")
+    res["gemv_16384_us"] = run(lambda: m.gemv(A, x, y, 16384, 16384))
+    del A
+    xb = torch.randn((4096, 4096), device="cuda", generator=gen).to(torch.bfloat16)
+    q = torch.empty((4096, 4096), dtype=torch.int8, device="cuda")
+    sA = torch.empty((4096,), device="cuda")
+    res["quantize_4096_bf16_us"] = run(
+        lambda: ops.quantizePerToken(xb, q, sA, 4096, 4096, in_dtype=qgemm.BF16))
+    Af = torch.randn((64, 4096), device="cuda", generator=gen)
+    Bf = torch.randn((4096, 4096), device="cuda", generator=gen)
+    Cf = torch.empty((64, 4096), device="cuda")
+    res["rows_gemm_64x4096x4096_us"] = run(
+        lambda: m.gemmF32(Af, Bf, Cf, 64, 4096, 4096, algo=qgemm.ALGO_SIMT))
+    return res
+
+
 LLAMA_LINEARS = (("qkv", 4096, 12288), ("o", 4096, 4096), ("gate_up", 4096, 22016),
                  ("down", 11008, 4096))
 
@@ -793,6 +835,12 @@ def main():
         r = w4a16_profile(ops, K, W) if args.profile else w4a16_decode(ops, peaks)
         if rank == 0:
             print(json.dumps({"only": "w4a16", "w4a16_decode": r}), flush=True)
+        return 0
+    if args.only == "side":
+        log("side kernels (only)")
+        r = side_kernels(st, ops, K, W)
+        if rank == 0:
+            print(json.dumps({"only": "side", "side_kernels": r}), flush=True)
         return 0
     if args.only == "f32":
         log("fp32 facade (only)")
