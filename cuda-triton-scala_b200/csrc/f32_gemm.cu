@@ -48,6 +48,7 @@
 #include <cstdint>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace qg {
 namespace f32 {
@@ -110,6 +111,9 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 __global__ void __launch_bounds__(256) split_cols_kernel(const float* __restrict__ B,
                                                          float* __restrict__ out, int K, int N,
                                                          int Kp, int* inf_flag) {
+  // The tf32 GEMM that follows may begin its set-up; it reads the split operands only
+  // after griddepcontrol.wait, i.e. after this grid has finished.
+  ptx::grid_launch_dependents();
   __shared__ float t[32][33];
   const int n0 = blockIdx.x * 32;
   for (int kb = blockIdx.y; kb < Kp / 32; kb += gridDim.y) {

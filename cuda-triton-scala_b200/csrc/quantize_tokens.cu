@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace qg {
 namespace qtok {
@@ -145,6 +146,9 @@ __global__ void __launch_bounds__(THREADS) quantize_rows_vec_kernel(const T* __r
                                                                     float* __restrict__ sA,
                                                                     int M, int K) {
   constexpr int VEC = Vec<T>::N;
+  // The GEMM that consumes q and sA may begin its set-up; it reads them only after
+  // griddepcontrol.wait, i.e. after this grid has finished.
+  ptx::grid_launch_dependents();
   const int m = blockIdx.x;
   if (m >= M) return;
   const T* row = x + (size_t)m * K;
