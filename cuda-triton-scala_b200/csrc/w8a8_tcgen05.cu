@@ -834,8 +834,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         continue;
       }
       if (elected) {
-        // bounded wait for the other parts' count-ins (all CTAs of the grid are resident,
-        // and the other parts wait on nothing of this one)
+        // bounded wait for the other parts' count-ins.  They run on lower-numbered pairs
+        // (pair = tail tile * split_s + part), which are dispatched before this one, and
+        // wait on nothing: a resident final part never waits on a part that cannot run.
         bool got = false;
         const unsigned long long t0 = ptx::globaltimer();
         for (;;) {
