@@ -120,7 +120,6 @@ __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v 
 
 template <int MT>
 __global__ void __launch_bounds__(THREADS, Cfg<MT>::CTAS_PER_SM)
-    __maxnreg__(MT == 4 ? 224 : 96)
     w4a16_tile_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmX,
                       const Params p) {
   using C = Cfg<MT>;
