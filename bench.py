@@ -534,8 +534,9 @@ def f32_facade(st, peaks, steps=10):
 
 def side_kernels(st, ops, steps, warmup):
     """The facade's smaller kernels on their own, each `warmup` + `steps` launches:
-    fp32 gemv A [16384, 16384], per-token quantisation of x [4096, 4096] bf16, and the
-    CUDA-core fp32 GEMM at 64 x 4096 x 4096 (the case profiles/ cite)."""
+    fp32 gemv A [16384, 16384], per-token quantisation of x [4096, 4096] bf16, the
+    CUDA-core fp32 GEMM at 64 x 4096 x 4096 (the cases profiles/ cite), and w8a16Gemm
+    at 1 x 14336 x 4096."""
     import torch
     import qgemm
     m = qgemm.MatrixOps(st)
@@ -570,6 +571,15 @@ def side_kernels(st, ops, steps, warmup):
     Cf = torch.empty((64, 4096), device="cuda")
     res["rows_gemm_64x4096x4096_us"] = run(
         lambda: m.gemmF32(Af, Bf, Cf, 64, 4096, 4096, algo=qgemm.ALGO_SIMT))
+    # QuantizedGemmOps.w8a16Gemm (exact reference order) at the decode shape, M = 1
+    w8 = torch.randint(-127, 128, (4096, 14336), dtype=torch.int8, device="cuda", generator=gen)
+    s8 = torch.rand((14336,), device="cuda", generator=gen) * 0.01
+    b8 = torch.randn((14336,), device="cuda", generator=gen)
+    x8 = torch.randn((1, 4096), device="cuda", generator=gen)
+    y8 = torch.empty((1, 14336), device="cuda")
+    t = run(lambda: ops.w8a16Gemm(w8, s8, x8, b8, y8, 1, 14336, 4096, True))
+    res["w8a16_1x14336x4096_us"] = t
+    res["w8a16_1x14336x4096_GB_s"] = (4096 * 14336 + 4096 * 4 + 14336 * 12) / t / 1e3
     return res
 
 

@@ -135,6 +135,12 @@ qgemm_status launch_w8a8_simt(qgemm_stream_s* s, const int8_t* A, const int8_t* 
                               int ldc, int M, int N, int K, int32_t* acc);
 qgemm_status launch_w4a16_ref(qgemm_stream_s* s, const uint8_t* w, const float* sw,
                               const float* x, float* y, int M, int N, int K);
+// Exact-order w8a16 on a TMA weight stream (w8a16_stream.cu); needs sm_100, N % 16 == 0,
+// K % 4 == 0, 16-byte aligned wInt8 and x.
+bool w8a16_stream_supported(const qgemm_device_s* d, uint64_t w, uint64_t x, int N, int K);
+qgemm_status launch_w8a16_stream(qgemm_stream_s* s, const int8_t* w, const float* sw,
+                                 const float* x, const float* bias, float* y, int M, int N,
+                                 int K, int hasBias, int rowwise);
 qgemm_status launch_w8a16_ref(qgemm_stream_s* s, const int8_t* w, const float* sw,
                               const float* x, const float* bias, float* y, int M, int N,
                               int K, int hasBias, int rowwise);

@@ -562,6 +562,12 @@ qgemm_status qgemm_w8a16_gemm(qgemm_stream_t s, uint64_t wInt8, uint64_t scalesW
   if (hasBias) QG_TRY(need(bias, "bias"));
   QG_TRY(need_align(scalesW, 4, "scalesW")); QG_TRY(need_align(x, 4, "x"));
   QG_TRY(need_align(y, 4, "y")); QG_TRY(need_align(bias, 4, "bias"));
+  if (w8a16_stream_supported(s->dev, wInt8, x, N, K))
+    return launch_w8a16_stream(s, reinterpret_cast<const int8_t*>(wInt8),
+                               reinterpret_cast<const float*>(scalesW),
+                               reinterpret_cast<const float*>(x),
+                               reinterpret_cast<const float*>(bias), reinterpret_cast<float*>(y),
+                               M, N, K, hasBias ? 1 : 0, 0);
   return launch_w8a16_ref(s, reinterpret_cast<const int8_t*>(wInt8),
                           reinterpret_cast<const float*>(scalesW),
                           reinterpret_cast<const float*>(x), reinterpret_cast<const float*>(bias),
@@ -577,6 +583,11 @@ qgemm_status qgemm_w8a16_gemm_rowwise(qgemm_stream_t s, uint64_t wInt8, uint64_t
   QG_TRY(need(y, "y"));
   QG_TRY(need_align(scalesW, 4, "scalesW")); QG_TRY(need_align(x, 4, "x"));
   QG_TRY(need_align(y, 4, "y"));
+  if (w8a16_stream_supported(s->dev, wInt8, x, N, K))
+    return launch_w8a16_stream(s, reinterpret_cast<const int8_t*>(wInt8),
+                               reinterpret_cast<const float*>(scalesW),
+                               reinterpret_cast<const float*>(x), nullptr,
+                               reinterpret_cast<float*>(y), M, N, K, 0, 1);
   return launch_w8a16_ref(s, reinterpret_cast<const int8_t*>(wInt8),
                           reinterpret_cast<const float*>(scalesW),
                           reinterpret_cast<const float*>(x), nullptr, reinterpret_cast<float*>(y),

@@ -37,6 +37,34 @@ def test_w8a16(gpu, oracle, has_bias):
     np.testing.assert_array_equal(y.read(np.uint32, (M, N)), f32_bits(ref))
 
 
+@pytest.mark.parametrize("M,N,K,has_bias,rowwise", [
+    (1, 14336, 4096, True, False),   # the decode-GEMV shape, int8 weights
+    (9, 512, 1000, False, False),    # three 4-row passes, a 232-row last stage
+    (4, 4112, 256, True, False),     # a partial last 128-column block
+    (3, 1024, 520, False, True),     # row-wise scales
+    (2, 48, 4, True, False),         # a single short stage
+])
+def test_w8a16_weight_stream_path(gpu, oracle, M, N, K, has_bias, rowwise):
+    """N % 16 == 0 and K % 4 == 0 take the TMA weight-stream kernel: still the
+    reference's sequential fp32 order, bit for bit."""
+    dev, st, ops = gpu
+    rng = np.random.default_rng(M * N + K)
+    w = rng.integers(-127, 128, (K, N), dtype=np.int8)
+    sw = rng.uniform(0.001, 0.01, K if rowwise else N).astype(np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    y = Out(dev, st, M * N * 4)
+    if rowwise:
+        ops.w8a16GemmRowWise(dev_array(gpu, w), dev_array(gpu, sw), dev_array(gpu, x), y, M, N, K)
+        ref = oracle.w8a16_gemm_rowwise(w, sw, x)
+    else:
+        ops.w8a16Gemm(dev_array(gpu, w), dev_array(gpu, sw), dev_array(gpu, x), dev_array(gpu, b),
+                      y, M, N, K, has_bias)
+        ref = oracle.w8a16_gemm(w, sw, x, b if has_bias else None)
+    st.sync()
+    np.testing.assert_array_equal(y.read(np.uint32, (M, N)), f32_bits(ref))
+
+
 def test_w8a16_rowwise_golden(gpu):
     dev, st, ops = gpu
     w, x = GOLD["w8a16_w"], GOLD["w8a16_x"]
