@@ -339,7 +339,8 @@ def library_int8_context(hb, steps):
 
 
 def w4a16_profile(ops, steps, warmup):
-    """The M = 1 decode GEMV as warmup + steps plain launches (no graph), for ncu."""
+    """The M = 1 decode GEMV as warmup + steps plain launches (no graph), for ncu: the
+    64-column-tile kernel, then the fragment-order kernel, each on its own layout."""
     import torch
     N, K, G, R = 14336, 4096, 128, 8
     gen = torch.Generator(device="cuda")
@@ -357,11 +358,22 @@ def w4a16_profile(ops, steps, warmup):
     for i in range(warmup + steps):
         ops.w4a16GemmGroupedTiled(x, wq[i % R], sc[i % R], y, 1, N, K, zero_point=8, group_size=G)
     torch.cuda.synchronize()
+    wf = []
+    for i in range(R):
+        w0 = torch.randint(-2**31, 2**31 - 1, (K, N // 8), dtype=torch.int32, device="cuda",
+                           generator=gen)
+        wf.append(torch.empty(ops.w4FragBytes(K, N), dtype=torch.uint8, device="cuda"))
+        ops.prepackW4Frag(w0, wf[-1], K, N)
+    for i in range(warmup + steps):
+        ops.w4a16GemmGroupedFrag(x, wf[i % R], sc[i % R], y, 1, N, K, zero_point=8, group_size=G)
+    torch.cuda.synchronize()
     return {"launches": warmup + steps, "M": 1, "N": N, "K": K}
 
 
 def w4a16_decode(ops, peaks):
-    """Config: x bf16 [M,4096] ~N(0,1), int4 [4096,14336] group 128, zp 8, bf16 out."""
+    """Config: x bf16 [M,4096] ~N(0,1), int4 [4096,14336] group 128, zp 8, bf16 out.
+    Each M is timed on both prepacked layouts (64-column tiles; fragment order for
+    M <= 4) and reported as the faster one, with both times."""
     import torch
     import qgemm.synthetic as syn
     N, K, G = 14336, 4096, 128
@@ -373,15 +385,15 @@ def w4a16_decode(ops, peaks):
                          generator=gen) for _ in range(R)]
     # one-time prepack of the static weights into 64-column tiles (not timed)
     wq = [torch.empty(ops.w4TiledBytes(K, N), dtype=torch.uint8, device="cuda") for _ in range(R)]
-    for a, b in zip(wq0, wq):
+    wf = [torch.empty(ops.w4FragBytes(K, N), dtype=torch.uint8, device="cuda") for _ in range(R)]
+    for a, b, c in zip(wq0, wq, wf):
         ops.prepackW4Tiled(a, b, K, N)
+        ops.prepackW4Frag(a, c, K, N)
     torch.cuda.synchronize()
     del wq0
     sc = [(torch.rand((K // G, N), device="cuda", generator=gen) * 0.015 + 0.005).to(torch.bfloat16)
           for _ in range(R)]
-    for M in (1, 4, 16):
-        x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
-        y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    def per_launch(M, x, y, path):
         launches = 64
         # one stream handle for warm-up and capture: its scratch is made by the
         # first (uncaptured) call
@@ -391,8 +403,12 @@ def w4a16_decode(ops, peaks):
 
         def body():
             for i in range(launches):
-                o.w4a16GemmGroupedTiled(x, wq[i % R], sc[i % R], y, M, N, K, zero_point=8,
-                                        group_size=G)
+                if path == "frag":
+                    o.w4a16GemmGroupedFrag(x, wf[i % R], sc[i % R], y, M, N, K, zero_point=8,
+                                           group_size=G)
+                else:
+                    o.w4a16GemmGroupedTiled(x, wq[i % R], sc[i % R], y, M, N, K, zero_point=8,
+                                            group_size=G)
 
         cap.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(cap):
@@ -413,13 +429,24 @@ def w4a16_decode(ops, peaks):
         e1.record()
         torch.cuda.synchronize()
         per = e0.elapsed_time(e1) / 1e3 / (reps * launches)
+        del g
+        q.destroy()
+        return per
+
+    for M in (1, 4, 16):
+        x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+        y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        times = {"tiled": per_launch(M, x, y, "tiled")}
+        if M <= 4:
+            times["frag"] = per_launch(M, x, y, "frag")
+        path = min(times, key=times.get)
+        per = times[path]
         bytes_alg = K * N // 2 + (K // G) * N * 2 + M * K * 2 + M * N * 2
         gbs = bytes_alg / per / 1e9
         res[f"M{M}"] = {"us_per_launch": per * 1e6, "GB_s": gbs, "bytes_per_launch": bytes_alg,
                         "frac_of_hbm": gbs / peaks["hbm_gbs"],
-                        "tflops": 2.0 * M * N * K / per / 1e12}
-        del g
-        q.destroy()
+                        "tflops": 2.0 * M * N * K / per / 1e12, "path": path,
+                        "us_by_layout": {k: v * 1e6 for k, v in times.items()}}
     _ = syn
     return res
 

@@ -161,6 +161,13 @@ qgemm_status launch_w4a16_tile(qgemm_stream_s* s, const void* x, const uint8_t* 
 size_t w4_tiled_bytes(int K, int N);
 qgemm_status launch_prepack_w4_tiled(qgemm_stream_s* s, const uint32_t* src, uint8_t* dst, int K,
                                      int N);
+bool w4a16_frag_supported(const qgemm_device_s* d, uint64_t x, uint64_t wf, uint64_t sc, int M,
+                          int N, int K, int G, const char** why);
+qgemm_status launch_w4a16_frag(qgemm_stream_s* s, const void* x, const void* wf, const void* sc,
+                               int zp, int G, void* y, int M, int N, int K);
+size_t w4_frag_bytes(int K, int N);
+qgemm_status launch_prepack_w4_frag(qgemm_stream_s* s, const uint32_t* src, uint32_t* dst, int K,
+                                    int N);
 size_t w4a16_prefill_workspace_bytes(int K, int N);
 qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
                                   const void* scales, int zp, int G, void* y, int M, int N,

@@ -483,6 +483,48 @@ qgemm_status qgemm_w4a16_grouped_gemm_tiled(qgemm_stream_t s, uint64_t x, uint64
                           reinterpret_cast<void*>(y), M, N, K);
 }
 
+qgemm_status qgemm_w4_frag_bytes(int K, int N, size_t* bytes) {
+  if (!bytes) return fail(QGEMM_ERR_INVALID_ARG, "bytes is null");
+  if (K < 0 || N < 0 || N % 8 != 0) return fail(QGEMM_ERR_INVALID_ARG, "bad K=%d N=%d", K, N);
+  *bytes = w4_frag_bytes(K, N);
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_prepack_w4_frag(qgemm_stream_t s, uint64_t wq, uint64_t dst, int K, int N) {
+  QG_TRY(enter(s));
+  if (K < 0 || N < 0 || N % 8 != 0) return fail(QGEMM_ERR_INVALID_ARG, "bad K=%d N=%d", K, N);
+  if (K == 0 || N == 0) return QGEMM_OK;
+  QG_TRY(need(wq, "wq")); QG_TRY(need(dst, "dst"));
+  QG_TRY(need_align(wq, 4, "wq")); QG_TRY(need_align(dst, 16, "dst"));
+  if (wq == dst) return fail(QGEMM_ERR_INVALID_ARG, "prepack cannot run in place");
+  return launch_prepack_w4_frag(s, reinterpret_cast<const uint32_t*>(wq),
+                                reinterpret_cast<uint32_t*>(dst), K, N);
+}
+
+qgemm_status qgemm_w4a16_grouped_gemm_frag(qgemm_stream_t s, uint64_t x, uint64_t wf,
+                                           uint64_t scales, int zero_point, int group_size,
+                                           uint64_t y, int M, int N, int K) {
+  QG_TRY(enter(s));
+  QG_TRY(check_dims(M, N, K));
+  if (group_size <= 0) return fail(QGEMM_ERR_INVALID_ARG, "group_size %d <= 0", group_size);
+  if (zero_point < 0 || zero_point > 15)
+    return fail(QGEMM_ERR_INVALID_ARG, "zero_point %d outside [0,15]", zero_point);
+  if (N % 8 != 0) return fail(QGEMM_ERR_INVALID_ARG, "N %d is not a multiple of 8", N);
+  if (K % group_size != 0)
+    return fail(QGEMM_ERR_INVALID_ARG, "K %d is not a multiple of group_size %d", K, group_size);
+  if (M == 0 || N == 0) return QGEMM_OK;
+  QG_TRY(need(y, "y"));
+  if (K == 0) return fail(QGEMM_ERR_UNSUPPORTED, "K == 0 on the frag path");
+  QG_TRY(need(x, "x")); QG_TRY(need(wf, "wf")); QG_TRY(need(scales, "scales"));
+  QG_TRY(need_align(y, 2, "y"));
+  const char* why = nullptr;
+  if (!w4a16_frag_supported(s->dev, x, wf, scales, M, N, K, group_size, &why))
+    return fail(QGEMM_ERR_UNSUPPORTED, "frag W4A16 path unavailable: %s", why);
+  return launch_w4a16_frag(s, reinterpret_cast<const void*>(x), reinterpret_cast<const void*>(wf),
+                           reinterpret_cast<const void*>(scales), zero_point, group_size,
+                           reinterpret_cast<void*>(y), M, N, K);
+}
+
 qgemm_status qgemm_w4a16_prefill_workspace_bytes(int K, int N, size_t* bytes) {
   if (!bytes) return fail(QGEMM_ERR_INVALID_ARG, "bytes is null");
   if (K < 0 || N < 0) return fail(QGEMM_ERR_INVALID_ARG, "negative size K=%d N=%d", K, N);

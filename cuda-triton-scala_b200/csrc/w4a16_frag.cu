@@ -1,0 +1,426 @@
+// w4a16_frag.cu -- W4A16 decode GEMV / skinny GEMM on fragment-ordered weights.
+//
+// Arithmetic (QuantizedGemmOps.scala:229-245 generalised to groups and a zero point):
+//     y[m,n] = sum_g s[g,n] * sum_{k in g} (q[k,n] - zp) * x[m,k]
+//
+// Weight layout ("frag", made once by qgemm_prepack_w4_frag).  The unit is one
+// 8-column group c times one 128-row block kb: 512 bytes, 16 per lane of a warp.
+//     frag[c][kb][lane][step] (uint32), lane = 4g + t, step s = 0..3 (32 rows each)
+// Word (c, kb, lane, s) holds the eight nibbles of column 8c+g at rows sb + {2t,
+// 16+2t, 2t+8, 24+2t, 2t+1, 17+2t, 2t+9, 25+2t} (sb = 128kb + 32s), nibble i at bits
+// 4i..4i+3, zero past K.  `(word >> 4i) & 0x000F000F | 0x43004300` is then, exactly,
+// the bf16 pair 128+q of A-fragment register i of mma.m16n8k16 whose 16 rows are
+// (column g, k half h): rows g take the first 16 rows of the step, rows g+8 the
+// second 16.  The B operand carries the matching halves of x: column n = 4h + m is
+// activation row m over k half h, so one MMA covers 8 columns x 32 k for up to 4
+// activation rows and the useful outputs are D[g][n] (h=0, t<2) and D[g+8][n]
+// (h=1, t>=2).  An all-ones MMA gives sum_k x per (h, m), which seeds the weight
+// MMAs' accumulator with -(128+zp) * sum x, so D = sum_k (q - zp) x directly.
+//
+// Grid: one CTA per SM; CTA i owns a contiguous run of 8-column groups (the counts
+// differ by at most one), so every SM streams the same bytes.  A column group's
+// units are one contiguous block (all of K), which is one stage of a shared-memory
+// ring of about 64 KB: warp 16 copies it with a single 1-D bulk copy, starting
+// before the programmatic-launch wait (weights never depend on the previous kernel).
+// Warps 0-15 take the 128-row blocks w, w+16, .. of every stage and keep those
+// blocks' activation fragments in registers; the CTA's scales (as fp32) sit in
+// shared memory.  Per column group a warp's partial sums go to shared memory and the
+// sixteen warps' partials are added in a fixed order (deterministic).  Every wait is
+// bounded.
+//
+// Measured on B200 (legacy tensor path, integer pipe): mma.m16n8k16 issues once per
+// 8 cycles per sub-partition; lop3 and shifts take 2 cycles a warp instruction and
+// overlap with the MMAs (28 of them and 4 MMAs: ~67 cycles), while mul.hi is slower
+// than a shift.  The dequantisation (4 lop3 + 3 shifts per word) and the per-stage
+// bookkeeping set the pace, so the loop keeps integer division out of the stage
+// counters, and 16 consumer warps (4 per sub-partition) hide the latencies better
+// than 8.  M = 1, N = 14336, K = 4096: 8.6 us against 11.5 us for the 64-column-tile
+// kernel (w4a16_tile.cu), which leaves 76 SMs with twice the work of the others.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace qg {
+namespace w4f {
+
+constexpr int KB = 128;          // rows per block
+constexpr int UNIT_U4 = 32;      // uint4 per unit (512 bytes)
+constexpr int NCW = 16;          // consumer warps
+constexpr int THREADS = 32 * (NCW + 1);
+constexpr int MAX_STAGES = 8;
+constexpr size_t RING_BYTES = 64 * 1024;  // ring target per CTA
+constexpr int MP = 4;            // activation rows per pass
+constexpr int MAX_NKB = 64;      // K <= 8192: a stage is at most 32 KB, KBW at most 4
+
+struct Params {
+  int M, N, K, G, zp;
+  int NKB;            // 128-row blocks (K rounded up)
+  int stages;         // ring stages (one column group each)
+  int cbase, crem;    // CTA i owns cbase + (i < crem) column groups
+  const uint4* w;     // frag layout
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* s;
+  __nv_bfloat16* y;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t mask, uint32_t bias) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(bias));
+  return r;
+}
+
+// d += A * B (no side effects: the compiler may schedule it freely)
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// d = A * B + (c0, c1, c0, c1)
+__device__ __forceinline__ void mma_bf16_init(float (&d)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1, float c0, float c1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1));
+}
+
+// Shared memory: the ring [stages][NKB * 512 B], the CTA's scales as fp32
+// [K/G][Cg*8], the warps' partial sums [NCW][MP][Cg*8] (fp32), the barriers.
+struct Smem {
+  size_t ring, sc, red, bar, total;
+};
+__host__ __device__ inline Smem smem_layout(int nkb, int stages, int srows, int cg) {
+  Smem m;
+  m.ring = 0;
+  m.sc = m.ring + (size_t)stages * nkb * 512;
+  m.red = m.sc + ((size_t)srows * cg * 8 * 4 + 15) / 16 * 16;
+  m.bar = m.red + (size_t)NCW * MP * cg * 8 * 4;
+  m.total = m.bar + 8 * 2 * MAX_STAGES + 16;
+  return m;
+}
+__host__ __device__ inline int ring_stages(int nkb, int cg) {
+  int st = (int)(RING_BYTES / ((size_t)nkb * 512));
+  st = st < 2 ? 2 : st > MAX_STAGES ? MAX_STAGES : st;
+  return st < cg ? st : (cg > 2 ? cg : 2);
+}
+
+// KBW: 128-row blocks per consumer warp (ceil(NKB / NCW)); GS: 32-row steps per scale
+// group (1, 2 or 4: group 32, 64 or a multiple of 128).
+template <int KBW, int GS>
+__global__ void __launch_bounds__(THREADS, 1) w4a16_frag_kernel(const Params p) {
+  constexpr int NQ = 4 / GS;  // scale groups per unit
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int cta = blockIdx.x;
+  const int c0 = cta * p.cbase + (cta < p.crem ? cta : p.crem);
+  const int Cg = p.cbase + (cta < p.crem ? 1 : 0);
+  const int ncol = Cg * 8;
+  const int srows = p.K / p.G;
+  const int STAGES = p.stages;
+  const Smem L = smem_layout(p.NKB, STAGES, srows, Cg);
+  const uint4* ring = reinterpret_cast<const uint4*>(smem + L.ring);
+  float* scf = reinterpret_cast<float*>(smem + L.sc);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  const uint32_t bar = ptx::smem_u32(smem + L.bar);
+  auto full_bar = [&](int s) { return bar + 8u * s; };
+  auto empty_bar = [&](int s) { return bar + 8u * (MAX_STAGES + s); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.bar + 8 * 2 * MAX_STAGES);
+  const uint32_t stage_bytes = (uint32_t)p.NKB * 512u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      ptx::mbar_init(empty_bar(s), NCW);
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::grid_launch_dependents();
+  }
+  __syncthreads();
+
+  if (warp == NCW) {
+    // ---------------- producer: one bulk copy per column group ----------------
+    if (lane == 0) {
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(p.w) + (size_t)c0 * stage_bytes;
+      const uint32_t ring0 = ptx::smem_u32(smem + L.ring);
+      int issued = 0, st = 0;
+      uint32_t ph = 0;  // parity of the ring lap
+      for (int c = 0; c < Cg; ++c) {
+        if (c >= STAGES && !ptx::mbar_wait_sleep(empty_bar(st), ph ^ 1u, abort_flag)) {
+          if (!*abort_flag) { *abort_flag = 1; if (p.err) atomicCAS(p.err, 0, DEVERR_TIMEOUT_PRODUCER); }
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(full_bar(st), stage_bytes);
+        ptx::bulk_load(ring0 + st * stage_bytes, src + (size_t)c * stage_bytes, stage_bytes,
+                       full_bar(st));
+        ++issued;
+        if (++st == STAGES) { st = 0; ph ^= 1u; }
+      }
+      // the copies in flight land before the CTA may exit
+      for (int c = (issued > STAGES ? issued - STAGES : 0); c < issued; ++c) {
+        if (!ptx::mbar_wait(full_bar(c % STAGES), (uint32_t)((c / STAGES) & 1), nullptr)) {
+          if (p.err) atomicCAS(p.err, 0, DEVERR_TIMEOUT_DRAIN);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int ctid = threadIdx.x;  // 0 .. 32*NCW-1
+  // the CTA's scales, widened to fp32 (no dependence on the previous kernel)
+  for (int i = ctid; i < srows * Cg; i += 32 * NCW) {
+    const int r = i / Cg, c = i - r * Cg;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.s) + ((size_t)r * p.N + (size_t)(c0 + c) * 8) / 8);
+    float4* d = reinterpret_cast<float4*>(scf + (size_t)r * ncol + c * 8);
+    d[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+    d[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                       __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
+  }
+  ptx::named_bar_sync(1, 32 * NCW);
+
+  const float zc = 128.0f + (float)p.zp;
+  const uint32_t MASK = 0x000F000Fu, BIAS = 0x43004300u, ONES = 0x3F803F80u;
+  int kbj[KBW];
+  bool vj[KBW];
+  uint32_t bx[KBW][8];   // B fragments: register (e & 1) of 32-row step e/2
+  float zs[KBW][NQ][2];  // -(128+zp) * sum_k x per scale group of this warp's blocks
+  int srow[KBW][NQ];
+#pragma unroll
+  for (int j = 0; j < KBW; ++j) {
+    kbj[j] = warp + j * NCW;
+    vj[j] = kbj[j] < p.NKB;
+  }
+  // activations may be written by the previous kernel in the stream
+  ptx::grid_dependency_wait();
+  {
+    const int m = g & 3, h = g >> 2;  // B column n = 4h + m: activation row m, k half h
+#pragma unroll
+    for (int j = 0; j < KBW; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int k = kbj[j] * KB + (e >> 1) * 32 + 16 * h + 2 * t + 8 * (e & 1);
+        // K % 16 == 0: a 16-row half lies wholly inside or wholly past K
+        bx[j][e] = (vj[j] && m < p.M && k < p.K)
+                       ? __ldg(reinterpret_cast<const uint32_t*>(p.x + (size_t)m * p.K + k))
+                       : 0u;
+      }
+  }
+#pragma unroll
+  for (int j = 0; j < KBW; ++j) {
+    const int kb = vj[j] ? kbj[j] : 0;
+    const uint32_t* b = bx[j];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = q * GS; s < q * GS + GS; ++s)
+        mma_bf16(d, ONES, ONES, ONES, ONES, b[2 * s], b[2 * s + 1]);
+      zs[j][q][0] = -zc * d[0];
+      zs[j][q][1] = -zc * d[1];
+      const int r = (kb * KB + q * GS * 32) / p.G;
+      srow[j][q] = (r < srows ? r : 0) * ncol + g;
+    }
+  }
+
+  float* redw = red + (size_t)warp * MP * ncol;
+  int st = 0;
+  uint32_t ph = 0;  // parity of the ring lap
+  for (int c = 0; c < Cg; ++c) {
+    const bool ok = ptx::mbar_wait_sleep(full_bar(st), ph, abort_flag);
+    if (!ok) {
+      if (!*abort_flag) { *abort_flag = 1; if (p.err) atomicCAS(p.err, 0, DEVERR_TIMEOUT_EPILOGUE); }
+      break;
+    }
+    const uint4* rs = ring + st * (p.NKB * UNIT_U4) + lane;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < KBW; ++j) {
+      if (vj[j]) {
+        const uint4 wv = rs[kbj[j] * UNIT_U4];
+        const uint32_t* b = bx[j];
+        const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          float d[4];
+#pragma unroll
+          for (int s = q * GS; s < q * GS + GS; ++s) {
+            const uint32_t w = wd[s];
+            const uint32_t a0 = and_or(w, MASK, BIAS), a1 = and_or(w >> 4, MASK, BIAS);
+            const uint32_t a2 = and_or(w >> 8, MASK, BIAS), a3 = and_or(w >> 12, MASK, BIAS);
+            if (s == q * GS)
+              mma_bf16_init(d, a0, a1, a2, a3, b[2 * s], b[2 * s + 1], zs[j][q][0], zs[j][q][1]);
+            else
+              mma_bf16(d, a0, a1, a2, a3, b[2 * s], b[2 * s + 1]);
+          }
+          const float sc = scf[srow[j][q] + c * 8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] = fmaf(sc, d[e], acc[e]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(empty_bar(st));
+    if (++st == STAGES) { st = 0; ph ^= 1u; }
+    // this lane's useful outputs: rows g (first k half, t < 2) or rows g+8 (second k
+    // half, t >= 2); then first half + second half (lanes t, t+2)
+    const float u0 = t >= 2 ? acc[2] : acc[0], u1 = t >= 2 ? acc[3] : acc[1];
+    const float v0 = u0 + __shfl_down_sync(0xffffffffu, u0, 2);
+    const float v1 = u1 + __shfl_down_sync(0xffffffffu, u1, 2);
+    if (t < 2) {
+      redw[(2 * t) * ncol + c * 8 + g] = v0;
+      redw[(2 * t + 1) * ncol + c * 8 + g] = v1;
+    }
+  }
+  ptx::named_bar_sync(1, 32 * NCW);
+  if (*abort_flag) return;
+  for (int idx = ctid; idx < p.M * ncol; idx += 32 * NCW) {
+    const int m = idx / ncol, r = idx - m * ncol;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) s += red[((size_t)w * MP + m) * ncol + r];
+    p.y[(size_t)m * p.N + (size_t)c0 * 8 + r] = __float2bfloat16_rn(s);
+  }
+}
+
+template <int KBW, int GS>
+static qgemm_status launch_one(qgemm_stream_s* s, const Params& p, int grid, size_t smem) {
+  auto kern = w4a16_frag_kernel<KBW, GS>;
+  static bool attr_done[64] = {};
+  const int ord = s->dev->ordinal;
+  if (ord < 0 || ord >= 64 || !attr_done[ord]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)s->dev->smem_optin);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_frag)");
+    if (ord >= 0 && ord < 64) attr_done[ord] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_fail(cudaLaunchKernelEx(&cfg, kern, p), "w4a16_frag_kernel launch");
+}
+
+template <int KBW>
+static qgemm_status launch_kbw(qgemm_stream_s* s, const Params& p, int gs, int grid,
+                               size_t smem) {
+  return gs == 1 ? launch_one<KBW, 1>(s, p, grid, smem)
+       : gs == 2 ? launch_one<KBW, 2>(s, p, grid, smem)
+                 : launch_one<KBW, 4>(s, p, grid, smem);
+}
+
+// 128-row blocks per consumer warp: 1, 2 or 4 (0: K too large)
+static int kbw_for(int K) {
+  const int nkb = (K + KB - 1) / KB;
+  if (nkb > MAX_NKB) return 0;
+  const int kbw = (nkb + NCW - 1) / NCW;
+  return kbw <= 1 ? 1 : kbw <= 2 ? 2 : 4;
+}
+
+static size_t smem_for(int K, int G, int NG, int grid) {
+  const int cmax = NG / grid + (NG % grid ? 1 : 0);
+  const int nkb = (K + KB - 1) / KB;
+  return smem_layout(nkb, ring_stages(nkb, cmax), K / G, cmax).total;
+}
+
+}  // namespace w4f
+
+size_t w4_frag_bytes(int K, int N) {
+  return (size_t)(N / 8) * (size_t)((K + w4f::KB - 1) / w4f::KB) * 512;
+}
+
+bool w4a16_frag_supported(const qgemm_device_s* d, uint64_t x, uint64_t wf, uint64_t sc, int M,
+                          int N, int K, int G, const char** why) {
+  auto no = [&](const char* w) { if (why) *why = w; return false; };
+  if (!d->tcgen05) return no("device is not sm_100");
+  if (K % 16 != 0) return no("K must be a multiple of 16");
+  if (!(G == 32 || G == 64 || G % 128 == 0)) return no("group_size must be 32, 64 or a multiple of 128");
+  if (N % 8 != 0) return no("N must be a multiple of 8");
+  if (w4f::kbw_for(K) == 0) return no("K must be at most 8192");
+  const int NG = N / 8, grid = NG < d->sm_count ? NG : d->sm_count;
+  if (w4f::smem_for(K, G, NG, grid) > d->smem_optin)
+    return no("shape needs more shared memory than a block has");
+  if (!aligned(x, 16) || !aligned(wf, 16) || !aligned(sc, 16))
+    return no("x, weights and scales must be 16-byte aligned");
+  (void)M;
+  return true;
+}
+
+qgemm_status launch_w4a16_frag(qgemm_stream_s* s, const void* x, const void* wf, const void* sc,
+                               int zp, int G, void* y, int M, int N, int K) {
+  using namespace w4f;
+  qgemm_device_s* d = s->dev;
+  const int NG = N / 8;
+  const int grid = NG < d->sm_count ? NG : d->sm_count;
+  Params p;
+  p.N = N; p.K = K; p.G = G; p.zp = zp;
+  p.NKB = (K + KB - 1) / KB;
+  p.cbase = NG / grid;
+  p.crem = NG % grid;
+  p.stages = ring_stages(p.NKB, p.cbase + (p.crem > 0 ? 1 : 0));
+  p.w = static_cast<const uint4*>(wf);
+  p.s = static_cast<const __nv_bfloat16*>(sc);
+  p.err = d->d_err;
+  const size_t smem = smem_for(K, G, NG, grid);
+  const int kbw = kbw_for(K);
+  const int gs = G == 32 ? 1 : G == 64 ? 2 : 4;
+  for (int m0 = 0; m0 < M; m0 += MP) {
+    p.M = (M - m0) < MP ? (M - m0) : MP;
+    p.x = static_cast<const __nv_bfloat16*>(x) + (size_t)m0 * K;
+    p.y = static_cast<__nv_bfloat16*>(y) + (size_t)m0 * N;
+    qgemm_status st = kbw == 1 ? launch_kbw<1>(s, p, gs, grid, smem)
+                    : kbw == 2 ? launch_kbw<2>(s, p, gs, grid, smem)
+                               : launch_kbw<4>(s, p, gs, grid, smem);
+    if (st != QGEMM_OK) return st;
+  }
+  return QGEMM_OK;
+}
+
+// ---- one-time weight repack: reference words -> fragment-ordered units ----------
+// dst word ((c * NKB + kb) * 32 + lane) * 4 + s; see the layout comment at the top.
+__global__ void prepack_w4_frag_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst,
+                                       int K, int N, int NKB) {
+  const int NG = N / 8;
+  const size_t total = (size_t)NG * NKB * 128;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int s = (int)(i & 3), lane = (int)((i >> 2) & 31);
+    const size_t unit = i >> 7;
+    const int kb = (int)(unit % NKB), c = (int)(unit / NKB);
+    const int g = lane >> 2, t = lane & 3;
+    const int sb = kb * w4f::KB + s * 32;
+    const int ks[8] = {sb + 2 * t,     sb + 16 + 2 * t, sb + 2 * t + 8, sb + 24 + 2 * t,
+                       sb + 2 * t + 1, sb + 17 + 2 * t, sb + 2 * t + 9, sb + 25 + 2 * t};
+    uint32_t v = 0;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+      if (ks[n] < K) v |= ((src[(size_t)ks[n] * NG + c] >> (4 * g)) & 0xFu) << (4 * n);
+    dst[i] = v;
+  }
+}
+
+qgemm_status launch_prepack_w4_frag(qgemm_stream_s* s, const uint32_t* src, uint32_t* dst, int K,
+                                    int N) {
+  const int NKB = (K + w4f::KB - 1) / w4f::KB;
+  const int grid = s->dev->sm_count * 8;
+  prepack_w4_frag_kernel<<<grid, 256, 0, s->stream>>>(src, dst, K, N, NKB);
+  return cuda_fail(cudaGetLastError(), "prepack_w4_frag launch");
+}
+
+}  // namespace qg

@@ -89,6 +89,13 @@ class QuantizedGemmOps:
         L.call("qgemm_w4a16_grouped_gemm_tiled", self._h, L.addr(x), L.addr(wt), L.addr(scales),
                zero_point, group_size, L.addr(y), M, N, K)
 
+    def w4a16GemmGroupedFrag(self, x, wf, scales, y, M: int, N: int, K: int, *,
+                             zero_point: int = 8, group_size: int = 128):
+        """Group-wise W4A16 on weights prepacked by prepackW4Frag (the decode path for
+        M <= 4; larger M runs in passes of 4 rows)."""
+        L.call("qgemm_w4a16_grouped_gemm_frag", self._h, L.addr(x), L.addr(wf), L.addr(scales),
+               zero_point, group_size, L.addr(y), M, N, K)
+
     @staticmethod
     def w4PrefillWorkspaceBytes(K: int, N: int) -> int:
         n = ctypes.c_size_t(0)
@@ -118,6 +125,16 @@ class QuantizedGemmOps:
     def prepackW4Tiled(self, wq, dst, K: int, N: int):
         """uint32 [K, N/8] reference-order int4 weights -> 64-column tiles (one time)."""
         L.call("qgemm_prepack_w4_tiled", self._h, L.addr(wq), L.addr(dst), K, N)
+
+    @staticmethod
+    def w4FragBytes(K: int, N: int) -> int:
+        n = ctypes.c_size_t(0)
+        L.call("qgemm_w4_frag_bytes", K, N, ctypes.byref(n))
+        return n.value
+
+    def prepackW4Frag(self, wq, dst, K: int, N: int):
+        """uint32 [K, N/8] reference-order int4 weights -> fragment order (one time)."""
+        L.call("qgemm_prepack_w4_frag", self._h, L.addr(wq), L.addr(dst), K, N)
 
     def quantizePerToken(self, x, q, sA, M: int, K: int, *, in_dtype: int = L.BF16):
         """dynamicQuantize along rows: x [M,K] (bf16 or fp32) -> int8 q [M,K], sA [M]."""

@@ -214,6 +214,27 @@ QGEMM_API qgemm_status qgemm_w4_tiled_bytes(int K, int N, size_t* bytes);
 QGEMM_API qgemm_status qgemm_prepack_w4_tiled(qgemm_stream_t s, uint64_t wq, uint64_t dst, int K,
                                               int N);
 
+/* The same group-wise W4A16 on weights repacked once by qgemm_prepack_w4_frag
+ * (fragment order: each SM streams an equal, contiguous share of 8-column groups;
+ * the fast decode path for M <= 4, and M <= 16 in passes of 4 rows).  Requires
+ * sm_100, K % 16 == 0, K <= 16384, group_size 32, 64 or a multiple of 128,
+ * N % 8 == 0 and 16-byte aligned x, wf and scales; otherwise
+ * QGEMM_ERR_UNSUPPORTED.  Deterministic. */
+QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_frag(qgemm_stream_t s, uint64_t x, uint64_t wf,
+                                                     uint64_t scales, int zero_point,
+                                                     int group_size, uint64_t y, int M, int N,
+                                                     int K);
+
+/* One-time int4 weight repack: uint32 [K, N/8] (reference nibble order) -> the
+ * fragment order: unit (c, kb) = columns 8c..8c+7 x rows 128kb..128kb+127, 512 bytes,
+ * units ordered c-major; inside a unit, lane 4g+t's four words (one per 32 rows)
+ * hold column 8c+g at rows sb + {2t, 2t+16, 2t+8, 2t+24, 2t+1, 2t+17, 2t+9, 2t+25}
+ * (sb = 128kb + 32*word), nibble i at bits 4i..4i+3, zero past K.
+ * qgemm_w4_frag_bytes gives the buffer size (N/8 * ceil(K/128) * 512). */
+QGEMM_API qgemm_status qgemm_w4_frag_bytes(int K, int N, size_t* bytes);
+QGEMM_API qgemm_status qgemm_prepack_w4_frag(qgemm_stream_t s, uint64_t wq, uint64_t dst, int K,
+                                             int N);
+
 /* Group-wise W4A16 GEMM for prefill-sized M (the same arithmetic as
  * qgemm_w4a16_grouped_gemm on the same prepacked weights `wt`): the weights are
  * expanded slab by slab into the caller's workspace as bf16 (q - zero_point) *

@@ -61,6 +61,96 @@ def test_prepack_w4_tiled_layout(gpu, K, N):
     np.testing.assert_array_equal(got, tiled_layout_numpy(wq, K, N))
 
 
+def frag(gpu, x, wq, sc, M, N, K, G, zp=8):
+    """Prepack once into fragment order, then the frag decode path."""
+    dev, st, ops = gpu
+    wf = Out(dev, st, ops.w4FragBytes(K, N))
+    ops.prepackW4Frag(dev_array(gpu, wq), wf, K, N)
+    y = Out(dev, st, M * N * 2)
+    ops.w4a16GemmGroupedFrag(dev_array(gpu, x), wf, dev_array(gpu, sc), y, M, N, K,
+                             zero_point=zp, group_size=G)
+    st.sync()
+    return y.read(np.uint16, (M, N))
+
+
+def frag_layout_numpy(wq, K, N):
+    """The documented fragment order: unit (c, kb) = columns 8c..8c+7 x rows
+    128kb..128kb+127; lane 4g+t, word s holds column 8c+g at rows 128kb + 32s +
+    {2t, 2t+16, 2t+8, 2t+24, 2t+1, 2t+17, 2t+9, 2t+25}, nibble i at bits 4i.."""
+    nkb = (K + 127) // 128
+    q = (wq[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 0xF   # [K, N/8, 8]
+    q = q.reshape(K, N).astype(np.uint32)
+    qp = np.zeros((nkb * 128, N), np.uint32)
+    qp[:K] = q
+    g, t = np.arange(32) // 4, np.arange(32) % 4
+    offs = np.array([0, 16, 8, 24, 1, 17, 9, 25])
+    out = np.zeros((N // 8, nkb, 32, 4), np.uint32)
+    for kb in range(nkb):
+        for s in range(4):
+            rows = kb * 128 + 32 * s + 2 * t[:, None] + offs[None, :]    # [32 lanes, 8 nibbles]
+            for c in range(N // 8):
+                vals = qp[rows, 8 * c + g[:, None]]                        # [32, 8]
+                out[c, kb, :, s] = (vals << (4 * np.arange(8, dtype=np.uint32))).sum(axis=1)
+    return out
+
+
+@pytest.mark.parametrize("K,N", [(128, 64), (160, 24), (4096, 16)])
+def test_prepack_w4_frag_layout(gpu, K, N):
+    dev, st, ops = gpu
+    _, wq, _ = syn.w4a16_inputs(1, N, K, group=32, seed=K + N)
+    nbytes = ops.w4FragBytes(K, N)
+    assert nbytes == (N // 8) * ((K + 127) // 128) * 512
+    wf = Out(dev, st, nbytes)
+    ops.prepackW4Frag(dev_array(gpu, wq), wf, K, N)
+    st.sync()
+    got = wf.read(np.uint32, (N // 8, (K + 127) // 128, 32, 4))
+    np.testing.assert_array_equal(got, frag_layout_numpy(wq, K, N))
+
+
+@pytest.mark.parametrize("M,N,K,G,zp", [
+    (1, 14336, 4096, 128, 8),    # decode shape
+    (4, 14336, 4096, 128, 0),
+    (16, 14336, 4096, 128, 8),   # four 4-row passes
+    (3, 1000, 512, 64, 8),       # fewer column groups than SMs on some CTAs, G = 64
+    (1, 4104, 4128, 32, 8),      # K not a multiple of 128, G = 32
+    (2, 4096, 8192, 256, 15),    # eight blocks per warp, G = 256
+    (1, 22016, 4096, 128, 8),    # 19 column groups on some CTAs
+    (5, 8, 32, 32, 8),           # one column group, one partial block, two passes
+])
+def test_grouped_frag_path(gpu, oracle, M, N, K, G, zp):
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M * 5 + N + K + G)
+    y = frag(gpu, x, wq, sc, M, N, K, G, zp)
+    ref, _ = oracle.w4a16_grouped(wq, sc, zp, G, x)
+    err = rel_err(syn.bf16_to_float(y), ref)
+    assert err <= TOL_BF16, err
+
+
+def test_frag_deterministic_and_matches_tiled(gpu):
+    M, N, K, G = 4, 14336, 4096, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=64)
+    a = frag(gpu, x, wq, sc, M, N, K, G)
+    b = frag(gpu, x, wq, sc, M, N, K, G)
+    np.testing.assert_array_equal(a, b)
+    c = syn.bf16_to_float(tiled(gpu, x, wq, sc, M, N, K, G)).astype(np.float64)
+    assert rel_err(syn.bf16_to_float(a).astype(np.float64), c) <= TOL_BF16
+
+
+@pytest.mark.parametrize("K,G", [(480, 48), (8320, 128)])
+def test_frag_rejects_unsupported_shapes(gpu, K, G):
+    """Group 48 (not 32, 64 or a multiple of 128) and K > 8192 are refused."""
+    import qgemm
+    dev, st, ops = gpu
+    x, wq, sc = syn.w4a16_inputs(1, 64, K, group=G, seed=65)
+    wf = Out(dev, st, ops.w4FragBytes(K, 64))
+    ops.prepackW4Frag(dev_array(gpu, wq), wf, K, 64)
+    y = Out(dev, st, 64 * 2)
+    with pytest.raises(qgemm.QGemmError) as e:
+        ops.w4a16GemmGroupedFrag(dev_array(gpu, x), wf, dev_array(gpu, sc), y, 1, 64, K,
+                                 group_size=G)
+    assert e.value.status == qgemm._lib.ERR_UNSUPPORTED
+    st.sync()
+
+
 def test_reference_entry_point(gpu, oracle):
     dev, st, ops = gpu
     M, N, K = 64, 512, 512
