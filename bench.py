@@ -372,8 +372,8 @@ def w4a16_profile(ops, steps, warmup):
 
 def w4a16_decode(ops, peaks):
     """Config: x bf16 [M,4096] ~N(0,1), int4 [4096,14336] group 128, zp 8, bf16 out.
-    Each M is timed on both prepacked layouts (64-column tiles; fragment order for
-    M <= 4) and reported as the faster one, with both times."""
+    Each M is timed on both prepacked layouts (64-column tiles; fragment order) and
+    reported as the faster one, with both times."""
     import torch
     import qgemm.synthetic as syn
     N, K, G = 14336, 4096, 128
@@ -436,9 +436,7 @@ def w4a16_decode(ops, peaks):
     for M in (1, 4, 16):
         x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
         y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
-        times = {"tiled": per_launch(M, x, y, "tiled")}
-        if M <= 4:
-            times["frag"] = per_launch(M, x, y, "frag")
+        times = {"tiled": per_launch(M, x, y, "tiled"), "frag": per_launch(M, x, y, "frag")}
         path = min(times, key=times.get)
         per = times[path]
         bytes_alg = K * N // 2 + (K // G) * N * 2 + M * K * 2 + M * N * 2

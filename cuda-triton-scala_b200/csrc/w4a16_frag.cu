@@ -293,9 +293,233 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_frag_kernel(const Params p) 
   }
 }
 
-template <int KBW, int GS>
+// ---- 5 to 16 activation rows: 16-column pairs --------------------------------------
+// The same layout read as column pairs (groups 2p, 2p+1 are adjacent, so a pair's
+// whole K is one contiguous block): the MMA rows are 16 columns, A of the first k
+// half of a step is (lop3 w0, lop3 w1, lop3 w0>>8, lop3 w1>>8) and of the second
+// (lop3 w0>>4, lop3 w1>>4, lop3 w0>>12, lop3 w1>>12), B is up to 8 activation rows
+// per n tile, NB tiles.  Each dequantised word feeds 2 NB MMAs, so the weights are
+// read once for 16 rows.  CTA i owns a contiguous run of pairs; warps take 128-row
+// blocks as in the kernel above; the activation fragments (16 NB registers per block)
+// stay in registers.  There is no producer warp (16 warps keep 128 registers a
+// thread; a 17th would cap them at 96): thread 0 issues the first stages, and the
+// warp that releases a stage last (an atomic count per stage) issues its refill.
+__host__ __device__ inline Smem smem_layout16(int nkb, int stages, int srows, int ncol, int mr) {
+  Smem m;
+  m.ring = 0;
+  m.sc = m.ring + (size_t)stages * nkb * 1024;
+  m.red = m.sc + ((size_t)srows * ncol * 4 + 15) / 16 * 16;
+  m.bar = m.red + (size_t)NCW * mr * ncol * 4;
+  m.total = m.bar + 8 * MAX_STAGES + 4 * 2 * MAX_STAGES + 16;
+  return m;
+}
+
+template <int NB, int KBW, int GS>
+__global__ void __launch_bounds__(32 * NCW, 1) w4a16_frag16_kernel(const Params p) {
+  constexpr int NQ = 4 / GS;
+  constexpr int MR = 8 * NB;  // activation rows of this pass (at most)
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int cta = blockIdx.x;
+  const int c0p = cta * p.cbase + (cta < p.crem ? cta : p.crem);  // first pair
+  const int Pg = p.cbase + (cta < p.crem ? 1 : 0);                  // pairs of this CTA
+  const int ncol = Pg * 16;
+  const int srows = p.K / p.G;
+  const int STAGES = p.stages;
+  const Smem L = smem_layout16(p.NKB, STAGES, srows, ncol, MR);
+  const uint4* ring = reinterpret_cast<const uint4*>(smem + L.ring);
+  float* scf = reinterpret_cast<float*>(smem + L.sc);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  const uint32_t bar = ptx::smem_u32(smem + L.bar);
+  auto full_bar = [&](int s) { return bar + 8u * s; };
+  int* released = reinterpret_cast<int*>(smem + L.bar + 8 * MAX_STAGES);  // per stage, never reset
+  int* laps = released + MAX_STAGES;                                      // copies issued per stage
+  volatile int* abort_flag = laps + MAX_STAGES;
+  const uint32_t stage_bytes = (uint32_t)p.NKB * 1024u;
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(p.w) + (size_t)c0p * stage_bytes;
+  const uint32_t ring0 = ptx::smem_u32(smem + L.ring);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      released[s] = 0;
+      laps[s] = 0;
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::grid_launch_dependents();
+    // the first stages, before the programmatic-launch wait
+    for (int c = 0; c < STAGES && c < Pg; ++c) {
+      ptx::mbar_arrive_expect_tx(full_bar(c), stage_bytes);
+      ptx::bulk_load(ring0 + c * stage_bytes, src + (size_t)c * stage_bytes, stage_bytes,
+                     full_bar(c));
+      laps[c] = 1;
+    }
+  }
+  __syncthreads();
+
+  const int ctid = threadIdx.x;
+  const int Cg = 2 * Pg, c0 = 2 * c0p;  // column groups of this CTA
+  for (int i = ctid; i < srows * Cg; i += 32 * NCW) {
+    const int r = i / Cg, c = i - r * Cg;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.s) + ((size_t)r * p.N + (size_t)(c0 + c) * 8) / 8);
+    float4* d = reinterpret_cast<float4*>(scf + (size_t)r * ncol + c * 8);
+    d[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+    d[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                       __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
+  }
+  ptx::named_bar_sync(1, 32 * NCW);
+
+  const float zc = 128.0f + (float)p.zp;
+  const uint32_t MASK = 0x000F000Fu, BIAS = 0x43004300u, ONES = 0x3F803F80u;
+  int kbj[KBW];
+  bool vj[KBW];
+  uint32_t bx[KBW][4][2][NB][2];  // [block][step][k half][n tile][register]
+  float zs[KBW][NQ][NB][2];
+  int srow[KBW][NQ];
+#pragma unroll
+  for (int j = 0; j < KBW; ++j) {
+    kbj[j] = warp + j * NCW;
+    vj[j] = kbj[j] < p.NKB;
+  }
+  ptx::grid_dependency_wait();
+#pragma unroll
+  for (int j = 0; j < KBW; ++j)
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+          const int m = 8 * nb + g;
+          const int k = kbj[j] * KB + s * 32 + 16 * h + 2 * t;
+          // K % 16 == 0: a 16-row half lies wholly inside or wholly past K
+          const bool ok = vj[j] && m < p.M && k < p.K;
+          const uint32_t* xp = reinterpret_cast<const uint32_t*>(p.x + (size_t)m * p.K + k);
+          bx[j][s][h][nb][0] = ok ? __ldg(xp) : 0u;
+          bx[j][s][h][nb][1] = ok ? __ldg(xp + 4) : 0u;
+        }
+#pragma unroll
+  for (int j = 0; j < KBW; ++j) {
+    const int kb = vj[j] ? kbj[j] : 0;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = q * GS; s < q * GS + GS; ++s)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            mma_bf16(d, ONES, ONES, ONES, ONES, bx[j][s][h][nb][0], bx[j][s][h][nb][1]);
+        zs[j][q][nb][0] = -zc * d[0];
+        zs[j][q][nb][1] = -zc * d[1];
+      }
+      const int r = (kb * KB + q * GS * 32) / p.G;
+      srow[j][q] = (r < srows ? r : 0) * ncol + g;
+    }
+  }
+
+  float* redw = red + (size_t)warp * MR * ncol;
+  int st = 0;
+  uint32_t ph = 0;
+  for (int c = 0; c < Pg; ++c) {
+    const bool ok = ptx::mbar_wait_sleep(full_bar(st), ph, abort_flag);
+    if (!ok) {
+      if (!*abort_flag) { *abort_flag = 1; if (p.err) atomicCAS(p.err, 0, DEVERR_TIMEOUT_EPILOGUE); }
+      break;
+    }
+    const uint4* rs = ring + st * (p.NKB * 2 * UNIT_U4) + lane;
+    float acc[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[nb][e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < KBW; ++j) {
+      if (vj[j]) {
+        const uint4 v0 = rs[kbj[j] * UNIT_U4], v1 = rs[(p.NKB + kbj[j]) * UNIT_U4];
+        const uint32_t w0s[4] = {v0.x, v0.y, v0.z, v0.w}, w1s[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          float d[NB][4];
+#pragma unroll
+          for (int s = q * GS; s < q * GS + GS; ++s) {
+            const uint32_t w0 = w0s[s], w1 = w1s[s];
+            const uint32_t l0 = and_or(w0, MASK, BIAS), l1 = and_or(w1, MASK, BIAS);
+            const uint32_t l2 = and_or(w0 >> 8, MASK, BIAS), l3 = and_or(w1 >> 8, MASK, BIAS);
+            const uint32_t h0 = and_or(w0 >> 4, MASK, BIAS), h1 = and_or(w1 >> 4, MASK, BIAS);
+            const uint32_t h2 = and_or(w0 >> 12, MASK, BIAS), h3 = and_or(w1 >> 12, MASK, BIAS);
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+              if (s == q * GS)
+                mma_bf16_init(d[nb], l0, l1, l2, l3, bx[j][s][0][nb][0], bx[j][s][0][nb][1],
+                              zs[j][q][nb][0], zs[j][q][nb][1]);
+              else
+                mma_bf16(d[nb], l0, l1, l2, l3, bx[j][s][0][nb][0], bx[j][s][0][nb][1]);
+              mma_bf16(d[nb], h0, h1, h2, h3, bx[j][s][1][nb][0], bx[j][s][1][nb][1]);
+            }
+          }
+          const float s0 = scf[srow[j][q] + c * 16], s1 = scf[srow[j][q] + c * 16 + 8];
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) {
+            acc[nb][0] = fmaf(s0, d[nb][0], acc[nb][0]);
+            acc[nb][1] = fmaf(s0, d[nb][1], acc[nb][1]);
+            acc[nb][2] = fmaf(s1, d[nb][2], acc[nb][2]);
+            acc[nb][3] = fmaf(s1, d[nb][3], acc[nb][3]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      // this warp's reads of the stage are done; the last of the NCW releases refills it
+      __threadfence_block();
+      if (atomicAdd(&released[st], 1) % NCW == NCW - 1 && c + STAGES < Pg) {
+        __threadfence_block();
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive_expect_tx(full_bar(st), stage_bytes);
+        ptx::bulk_load(ring0 + st * stage_bytes, src + (size_t)(c + STAGES) * stage_bytes,
+                       stage_bytes, full_bar(st));
+        laps[st] += 1;
+      }
+    }
+    if (++st == STAGES) { st = 0; ph ^= 1u; }
+    // D rows g / g+8 are columns 16c+g / 16c+8+g; D columns 2t, 2t+1 are rows 8nb+2t(+1)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      float* r0 = redw + (size_t)(8 * nb + 2 * t) * ncol + c * 16 + g;
+      r0[0] = acc[nb][0];
+      r0[ncol] = acc[nb][1];
+      r0[8] = acc[nb][2];
+      r0[ncol + 8] = acc[nb][3];
+    }
+  }
+  ptx::named_bar_sync(1, 32 * NCW);
+  if (*abort_flag) {
+    // copies still in flight land before the CTA exits
+    if (ctid == 0)
+      for (int s = 0; s < STAGES; ++s)
+        if (laps[s] > 0 &&
+            !ptx::mbar_wait(full_bar(s), (uint32_t)((laps[s] - 1) & 1), nullptr) && p.err)
+          atomicCAS(p.err, 0, DEVERR_TIMEOUT_DRAIN);
+    return;
+  }
+  for (int idx = ctid; idx < p.M * ncol; idx += 32 * NCW) {
+    const int m = idx / ncol, r = idx - m * ncol;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) s += red[((size_t)w * MR + m) * ncol + r];
+    p.y[(size_t)m * p.N + (size_t)c0 * 8 + r] = __float2bfloat16_rn(s);
+  }
+}
+
+template <int NB, int KBW, int GS>
 static qgemm_status launch_one(qgemm_stream_s* s, const Params& p, int grid, size_t smem) {
-  auto kern = w4a16_frag_kernel<KBW, GS>;
+  void (*kern)(const Params) =
+      NB == 0 ? w4a16_frag_kernel<KBW, GS> : w4a16_frag16_kernel<NB == 0 ? 1 : NB, KBW, GS>;
   static bool attr_done[64] = {};
   const int ord = s->dev->ordinal;
   if (ord < 0 || ord >= 64 || !attr_done[ord]) {
@@ -306,7 +530,7 @@ static qgemm_status launch_one(qgemm_stream_s* s, const Params& p, int grid, siz
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.blockDim = dim3(NB == 0 ? THREADS : 32 * NCW, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s->stream;
   cudaLaunchAttribute attr[1];
@@ -317,12 +541,21 @@ static qgemm_status launch_one(qgemm_stream_s* s, const Params& p, int grid, siz
   return cuda_fail(cudaLaunchKernelEx(&cfg, kern, p), "w4a16_frag_kernel launch");
 }
 
-template <int KBW>
+// NB = 0: the 8-column kernel (at most 4 rows); NB = 1, 2: column pairs, 8 NB rows
+template <int NB, int KBW>
 static qgemm_status launch_kbw(qgemm_stream_s* s, const Params& p, int gs, int grid,
                                size_t smem) {
-  return gs == 1 ? launch_one<KBW, 1>(s, p, grid, smem)
-       : gs == 2 ? launch_one<KBW, 2>(s, p, grid, smem)
-                 : launch_one<KBW, 4>(s, p, grid, smem);
+  return gs == 1 ? launch_one<NB, KBW, 1>(s, p, grid, smem)
+       : gs == 2 ? launch_one<NB, KBW, 2>(s, p, grid, smem)
+                 : launch_one<NB, KBW, 4>(s, p, grid, smem);
+}
+
+template <int NB>
+static qgemm_status launch_nb(qgemm_stream_s* s, const Params& p, int kbw, int gs, int grid,
+                              size_t smem) {
+  return kbw == 1 ? launch_kbw<NB, 1>(s, p, gs, grid, smem)
+       : kbw == 2 ? launch_kbw<NB, 2>(s, p, gs, grid, smem)
+                  : launch_kbw<NB, 4>(s, p, gs, grid, smem);
 }
 
 // 128-row blocks per consumer warp: 1, 2 or 4 (0: K too large)
@@ -333,11 +566,8 @@ static int kbw_for(int K) {
   return kbw <= 1 ? 1 : kbw <= 2 ? 2 : 4;
 }
 
-static size_t smem_for(int K, int G, int NG, int grid) {
-  const int cmax = NG / grid + (NG % grid ? 1 : 0);
-  const int nkb = (K + KB - 1) / KB;
-  return smem_layout(nkb, ring_stages(nkb, cmax), K / G, cmax).total;
-}
+// the pair kernel's ring: as many stages of two column groups as the target allows
+static int ring_stages16(int nkb, int pmax) { return ring_stages(2 * nkb, pmax); }
 
 }  // namespace w4f
 
@@ -353,9 +583,6 @@ bool w4a16_frag_supported(const qgemm_device_s* d, uint64_t x, uint64_t wf, uint
   if (!(G == 32 || G == 64 || G % 128 == 0)) return no("group_size must be 32, 64 or a multiple of 128");
   if (N % 8 != 0) return no("N must be a multiple of 8");
   if (w4f::kbw_for(K) == 0) return no("K must be at most 8192");
-  const int NG = N / 8, grid = NG < d->sm_count ? NG : d->sm_count;
-  if (w4f::smem_for(K, G, NG, grid) > d->smem_optin)
-    return no("shape needs more shared memory than a block has");
   if (!aligned(x, 16) || !aligned(wf, 16) || !aligned(sc, 16))
     return no("x, weights and scales must be 16-byte aligned");
   (void)M;
@@ -366,28 +593,76 @@ qgemm_status launch_w4a16_frag(qgemm_stream_s* s, const void* x, const void* wf,
                                int zp, int G, void* y, int M, int N, int K) {
   using namespace w4f;
   qgemm_device_s* d = s->dev;
-  const int NG = N / 8;
-  const int grid = NG < d->sm_count ? NG : d->sm_count;
-  Params p;
-  p.N = N; p.K = K; p.G = G; p.zp = zp;
-  p.NKB = (K + KB - 1) / KB;
-  p.cbase = NG / grid;
-  p.crem = NG % grid;
-  p.stages = ring_stages(p.NKB, p.cbase + (p.crem > 0 ? 1 : 0));
-  p.w = static_cast<const uint4*>(wf);
-  p.s = static_cast<const __nv_bfloat16*>(sc);
-  p.err = d->d_err;
-  const size_t smem = smem_for(K, G, NG, grid);
+  const int sms = d->sm_count;
+  const int nkb = (K + KB - 1) / KB, srows = K / G;
   const int kbw = kbw_for(K);
   const int gs = G == 32 ? 1 : G == 64 ? 2 : 4;
-  for (int m0 = 0; m0 < M; m0 += MP) {
-    p.M = (M - m0) < MP ? (M - m0) : MP;
-    p.x = static_cast<const __nv_bfloat16*>(x) + (size_t)m0 * K;
-    p.y = static_cast<__nv_bfloat16*>(y) + (size_t)m0 * N;
-    qgemm_status st = kbw == 1 ? launch_kbw<1>(s, p, gs, grid, smem)
-                    : kbw == 2 ? launch_kbw<2>(s, p, gs, grid, smem)
-                               : launch_kbw<4>(s, p, gs, grid, smem);
-    if (st != QGEMM_OK) return st;
+  const __nv_bfloat16* x16 = static_cast<const __nv_bfloat16*>(x);
+  __nv_bfloat16* y16 = static_cast<__nv_bfloat16*>(y);
+  const __nv_bfloat16* s16 = static_cast<const __nv_bfloat16*>(sc);
+  const uint4* w4 = static_cast<const uint4*>(wf);
+  Params p;
+  p.N = N; p.K = K; p.G = G; p.zp = zp;
+  p.NKB = nkb;
+  p.err = d->d_err;
+  // The columns go out in chunks of at most (SMs x a width whose shared memory fits);
+  // one chunk unless N is very wide.
+  auto widest = [&](int want, auto smem_of) {
+    while (want > 1 && smem_of(want) > d->smem_optin) --want;
+    return want;
+  };
+  if (M > MP && N % 16 == 0 && kbw <= 2) {
+    // more than 4 rows: 16-row passes on column pairs (weights read once per 16 rows)
+    const int NP = N / 16;
+    const int g0 = NP < sms ? NP : sms;
+    const int wmax = widest((NP + g0 - 1) / g0, [&](int w) {
+      return smem_layout16(nkb, ring_stages16(nkb, w), srows, 16 * w, 16).total;
+    });
+    for (int p0 = 0; p0 < NP; p0 += sms * wmax) {
+      const int np = (NP - p0) < sms * wmax ? (NP - p0) : sms * wmax;
+      const int grid = np < sms ? np : sms;
+      Params q = p;
+      q.cbase = np / grid;
+      q.crem = np % grid;
+      const int pmax = q.cbase + (q.crem > 0 ? 1 : 0);
+      q.stages = ring_stages16(nkb, pmax);
+      q.w = w4 + (size_t)p0 * 2 * nkb * UNIT_U4;
+      q.s = s16 + (size_t)p0 * 16;
+      for (int m0 = 0; m0 < M; m0 += 16) {
+        q.M = (M - m0) < 16 ? (M - m0) : 16;
+        q.x = x16 + (size_t)m0 * K;
+        q.y = y16 + (size_t)m0 * N + (size_t)p0 * 16;
+        const int nb = q.M > 8 ? 2 : 1;
+        const size_t sm = smem_layout16(nkb, q.stages, srows, 16 * pmax, 8 * nb).total;
+        qgemm_status st = nb == 2 ? launch_nb<2>(s, q, kbw, gs, grid, sm)
+                                  : launch_nb<1>(s, q, kbw, gs, grid, sm);
+        if (st != QGEMM_OK) return st;
+      }
+    }
+    return QGEMM_OK;
+  }
+  const int NG = N / 8;
+  const int g0 = NG < sms ? NG : sms;
+  const int wmax = widest((NG + g0 - 1) / g0, [&](int w) {
+    return smem_layout(nkb, ring_stages(nkb, w), srows, w).total;
+  });
+  for (int c0 = 0; c0 < NG; c0 += sms * wmax) {
+    const int ng = (NG - c0) < sms * wmax ? (NG - c0) : sms * wmax;
+    const int grid = ng < sms ? ng : sms;
+    p.cbase = ng / grid;
+    p.crem = ng % grid;
+    const int cmax = p.cbase + (p.crem > 0 ? 1 : 0);
+    p.stages = ring_stages(nkb, cmax);
+    p.w = w4 + (size_t)c0 * nkb * UNIT_U4;
+    p.s = s16 + (size_t)c0 * 8;
+    const size_t sm = smem_layout(nkb, p.stages, srows, cmax).total;
+    for (int m0 = 0; m0 < M; m0 += MP) {
+      p.M = (M - m0) < MP ? (M - m0) : MP;
+      p.x = x16 + (size_t)m0 * K;
+      p.y = y16 + (size_t)m0 * N + (size_t)c0 * 8;
+      qgemm_status st = launch_nb<0>(s, p, kbw, gs, grid, sm);
+      if (st != QGEMM_OK) return st;
+    }
   }
   return QGEMM_OK;
 }

@@ -91,8 +91,8 @@ class QuantizedGemmOps:
 
     def w4a16GemmGroupedFrag(self, x, wf, scales, y, M: int, N: int, K: int, *,
                              zero_point: int = 8, group_size: int = 128):
-        """Group-wise W4A16 on weights prepacked by prepackW4Frag (the decode path for
-        M <= 4; larger M runs in passes of 4 rows)."""
+        """Group-wise W4A16 on weights prepacked by prepackW4Frag (the fast decode path:
+        8-column groups for M <= 4, 16-column pairs in 16-row passes above)."""
         L.call("qgemm_w4a16_grouped_gemm_frag", self._h, L.addr(x), L.addr(wf), L.addr(scales),
                zero_point, group_size, L.addr(y), M, N, K)
 

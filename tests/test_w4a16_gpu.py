@@ -110,12 +110,19 @@ def test_prepack_w4_frag_layout(gpu, K, N):
 @pytest.mark.parametrize("M,N,K,G,zp", [
     (1, 14336, 4096, 128, 8),    # decode shape
     (4, 14336, 4096, 128, 0),
-    (16, 14336, 4096, 128, 8),   # four 4-row passes
+    (16, 14336, 4096, 128, 8),   # column pairs, one 16-row pass
     (3, 1000, 512, 64, 8),       # fewer column groups than SMs on some CTAs, G = 64
     (1, 4104, 4128, 32, 8),      # K not a multiple of 128, G = 32
     (2, 4096, 8192, 256, 15),    # eight blocks per warp, G = 256
     (1, 22016, 4096, 128, 8),    # 19 column groups on some CTAs
     (5, 8, 32, 32, 8),           # one column group, one partial block, two passes
+    # more than 4 rows, N % 16 == 0: 16-column pairs, 16-row passes
+    (8, 4096, 4096, 64, 8),      # one 8-row tile
+    (12, 4112, 1024, 32, 3),     # 12 of 16 rows, group 32, 257 pairs
+    (16, 1024, 4128, 32, 8),     # K not a multiple of 128
+    (33, 2048, 2048, 128, 8),    # passes of 16, 16 and 1 rows
+    (2, 131072, 512, 128, 8),    # wide N: the columns go out in several chunks
+    (16, 65536, 1024, 64, 8),    # wide N on column pairs: several chunks
 ])
 def test_grouped_frag_path(gpu, oracle, M, N, K, G, zp):
     x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M * 5 + N + K + G)
