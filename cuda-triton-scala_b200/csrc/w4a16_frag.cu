@@ -6,12 +6,14 @@
 // Weight layout ("frag", made once by qgemm_prepack_w4_frag).  The unit is one
 // 8-column group c times one 128-row block kb: 512 bytes, 16 per lane of a warp.
 //     frag[c][kb][lane][step] (uint32), lane = 4g + t, step s = 0..3 (32 rows each)
-// Word (c, kb, lane, s) holds the eight nibbles of column 8c+g at rows sb + {2t,
-// 16+2t, 2t+8, 24+2t, 2t+1, 17+2t, 2t+9, 25+2t} (sb = 128kb + 32s), nibble i at bits
-// 4i..4i+3, zero past K.  `(word >> 4i) & 0x000F000F | 0x43004300` is then, exactly,
-// the bf16 pair 128+q of A-fragment register i of mma.m16n8k16 whose 16 rows are
-// (column g, k half h): rows g take the first 16 rows of the step, rows g+8 the
-// second 16.  The B operand carries the matching halves of x: column n = 4h + m is
+// Word (c, kb, lane, s) holds the eight nibbles of column 8c+g at rows sb + 8t +
+// {0, 4, 2, 6, 1, 5, 3, 7} (sb = 128kb + 32s), nibble i at bits 4i..4i+3, zero past
+// K.  `(word >> 4i) & 0x000F000F | 0x43004300` is then, exactly, the bf16 pair 128+q
+// of A-fragment register i of mma.m16n8k16 whose 16 rows are (column g, k half h).
+// The MMA sums over k, so the k order is free as long as A and B share it: lane t's
+// MMA k positions {2t, 2t+1, 2t+8, 2t+9} of half h are rows 8t + 4h + {0, 1, 2, 3},
+// which makes each lane's activations for a step one contiguous run of x (a single
+// vector load).  The B operand carries the matching halves of x: column n = 4h + m is
 // activation row m over k half h, so one MMA covers 8 columns x 32 k for up to 4
 // activation rows and the useful outputs are D[g][n] (h=0, t<2) and D[g+8][n]
 // (h=1, t>=2).  An all-ones MMA gives sum_k x per (h, m), which seeds the weight
@@ -101,7 +103,7 @@ __host__ __device__ inline Smem smem_layout(int nkb, int stages, int srows, int 
   m.ring = 0;
   m.sc = m.ring + (size_t)stages * nkb * 512;
   m.red = m.sc + ((size_t)srows * cg * 8 * 4 + 15) / 16 * 16;
-  m.bar = m.red + (size_t)NCW * MP * cg * 8 * 4;
+  m.bar = m.red + (size_t)NCW * MP * (cg * 8 + 4) * 4;
   m.total = m.bar + 8 * 2 * MAX_STAGES + 16;
   return m;
 }
@@ -208,12 +210,15 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_frag_kernel(const Params p) 
 #pragma unroll
     for (int j = 0; j < KBW; ++j)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int k = kbj[j] * KB + (e >> 1) * 32 + 16 * h + 2 * t + 8 * (e & 1);
-        // K % 16 == 0: a 16-row half lies wholly inside or wholly past K
-        bx[j][e] = (vj[j] && m < p.M && k < p.K)
-                       ? __ldg(reinterpret_cast<const uint32_t*>(p.x + (size_t)m * p.K + k))
-                       : 0u;
+      for (int s = 0; s < 4; ++s) {
+        // rows 8t + 4h .. +3 of the step: both B registers in one 8-byte load
+        const int k = kbj[j] * KB + s * 32 + 8 * t + 4 * h;
+        // K % 16 == 0: a lane's 8 rows of a step lie wholly inside or wholly past K
+        uint2 v = make_uint2(0u, 0u);
+        if (vj[j] && m < p.M && k < p.K)
+          v = __ldg(reinterpret_cast<const uint2*>(p.x + (size_t)m * p.K + k));
+        bx[j][2 * s] = v.x;
+        bx[j][2 * s + 1] = v.y;
       }
   }
 #pragma unroll
@@ -233,7 +238,8 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_frag_kernel(const Params p) 
     }
   }
 
-  float* redw = red + (size_t)warp * MP * ncol;
+  const int rs4 = ncol + 4;  // partial-sum row stride: rows 2t apart on different banks
+  float* redw = red + (size_t)warp * MP * rs4;
   int st = 0;
   uint32_t ph = 0;  // parity of the ring lap
   for (int c = 0; c < Cg; ++c) {
@@ -278,8 +284,8 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_frag_kernel(const Params p) 
     const float v0 = u0 + __shfl_down_sync(0xffffffffu, u0, 2);
     const float v1 = u1 + __shfl_down_sync(0xffffffffu, u1, 2);
     if (t < 2) {
-      redw[(2 * t) * ncol + c * 8 + g] = v0;
-      redw[(2 * t + 1) * ncol + c * 8 + g] = v1;
+      redw[(2 * t) * rs4 + c * 8 + g] = v0;
+      redw[(2 * t + 1) * rs4 + c * 8 + g] = v1;
     }
   }
   ptx::named_bar_sync(1, 32 * NCW);
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1) w4a16_frag_kernel(const Params p) 
     const int m = idx / ncol, r = idx - m * ncol;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < NCW; ++w) s += red[((size_t)w * MP + m) * ncol + r];
+    for (int w = 0; w < NCW; ++w) s += red[((size_t)w * MP + m) * rs4 + r];
     p.y[(size_t)m * p.N + (size_t)c0 * 8 + r] = __float2bfloat16_rn(s);
   }
 }
@@ -309,7 +315,7 @@ __host__ __device__ inline Smem smem_layout16(int nkb, int stages, int srows, in
   m.ring = 0;
   m.sc = m.ring + (size_t)stages * nkb * 1024;
   m.red = m.sc + ((size_t)srows * ncol * 4 + 15) / 16 * 16;
-  m.bar = m.red + (size_t)NCW * mr * ncol * 4;
+  m.bar = m.red + (size_t)NCW * mr * (ncol + 4) * 4;
   m.total = m.bar + 8 * MAX_STAGES + 4 * 2 * MAX_STAGES + 16;
   return m;
 }
@@ -390,17 +396,19 @@ __global__ void __launch_bounds__(32 * NCW, 1) w4a16_frag16_kernel(const Params 
 #pragma unroll
     for (int s = 0; s < 4; ++s)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-          const int m = 8 * nb + g;
-          const int k = kbj[j] * KB + s * 32 + 16 * h + 2 * t;
-          // K % 16 == 0: a 16-row half lies wholly inside or wholly past K
-          const bool ok = vj[j] && m < p.M && k < p.K;
-          const uint32_t* xp = reinterpret_cast<const uint32_t*>(p.x + (size_t)m * p.K + k);
-          bx[j][s][h][nb][0] = ok ? __ldg(xp) : 0u;
-          bx[j][s][h][nb][1] = ok ? __ldg(xp + 4) : 0u;
-        }
+      for (int nb = 0; nb < NB; ++nb) {
+        // rows 8t .. 8t+7 of the step: both k halves' B registers in one 16-byte load
+        const int m = 8 * nb + g;
+        const int k = kbj[j] * KB + s * 32 + 8 * t;
+        // K % 16 == 0: a lane's 8 rows of a step lie wholly inside or wholly past K
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (vj[j] && m < p.M && k < p.K)
+          v = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)m * p.K + k));
+        bx[j][s][0][nb][0] = v.x;
+        bx[j][s][0][nb][1] = v.y;
+        bx[j][s][1][nb][0] = v.z;
+        bx[j][s][1][nb][1] = v.w;
+      }
 #pragma unroll
   for (int j = 0; j < KBW; ++j) {
     const int kb = vj[j] ? kbj[j] : 0;
@@ -422,7 +430,8 @@ __global__ void __launch_bounds__(32 * NCW, 1) w4a16_frag16_kernel(const Params 
     }
   }
 
-  float* redw = red + (size_t)warp * MR * ncol;
+  const int rs4 = ncol + 4;  // partial-sum row stride: rows 2t apart on different banks
+  float* redw = red + (size_t)warp * MR * rs4;
   int st = 0;
   uint32_t ph = 0;
   for (int c = 0; c < Pg; ++c) {
@@ -490,11 +499,11 @@ __global__ void __launch_bounds__(32 * NCW, 1) w4a16_frag16_kernel(const Params 
     // D rows g / g+8 are columns 16c+g / 16c+8+g; D columns 2t, 2t+1 are rows 8nb+2t(+1)
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
-      float* r0 = redw + (size_t)(8 * nb + 2 * t) * ncol + c * 16 + g;
+      float* r0 = redw + (size_t)(8 * nb + 2 * t) * rs4 + c * 16 + g;
       r0[0] = acc[nb][0];
-      r0[ncol] = acc[nb][1];
+      r0[rs4] = acc[nb][1];
       r0[8] = acc[nb][2];
-      r0[ncol + 8] = acc[nb][3];
+      r0[rs4 + 8] = acc[nb][3];
     }
   }
   ptx::named_bar_sync(1, 32 * NCW);
@@ -511,7 +520,7 @@ __global__ void __launch_bounds__(32 * NCW, 1) w4a16_frag16_kernel(const Params 
     const int m = idx / ncol, r = idx - m * ncol;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < NCW; ++w) s += red[((size_t)w * MR + m) * ncol + r];
+    for (int w = 0; w < NCW; ++w) s += red[((size_t)w * MR + m) * rs4 + r];
     p.y[(size_t)m * p.N + (size_t)c0 * 8 + r] = __float2bfloat16_rn(s);
   }
 }
@@ -680,8 +689,8 @@ __global__ void prepack_w4_frag_kernel(const uint32_t* __restrict__ src, uint32_
     const int kb = (int)(unit % NKB), c = (int)(unit / NKB);
     const int g = lane >> 2, t = lane & 3;
     const int sb = kb * w4f::KB + s * 32;
-    const int ks[8] = {sb + 2 * t,     sb + 16 + 2 * t, sb + 2 * t + 8, sb + 24 + 2 * t,
-                       sb + 2 * t + 1, sb + 17 + 2 * t, sb + 2 * t + 9, sb + 25 + 2 * t};
+    const int r0 = sb + 8 * t;
+    const int ks[8] = {r0 + 0, r0 + 4, r0 + 2, r0 + 6, r0 + 1, r0 + 5, r0 + 3, r0 + 7};
     uint32_t v = 0;
 #pragma unroll
     for (int n = 0; n < 8; ++n)

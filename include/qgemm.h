@@ -229,7 +229,7 @@ QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_frag(qgemm_stream_t s, uint64_t 
 /* One-time int4 weight repack: uint32 [K, N/8] (reference nibble order) -> the
  * fragment order: unit (c, kb) = columns 8c..8c+7 x rows 128kb..128kb+127, 512 bytes,
  * units ordered c-major; inside a unit, lane 4g+t's four words (one per 32 rows)
- * hold column 8c+g at rows sb + {2t, 2t+16, 2t+8, 2t+24, 2t+1, 2t+17, 2t+9, 2t+25}
+ * hold column 8c+g at rows sb + 8t + {0, 4, 2, 6, 1, 5, 3, 7}
  * (sb = 128kb + 32*word), nibble i at bits 4i..4i+3, zero past K.
  * qgemm_w4_frag_bytes gives the buffer size (N/8 * ceil(K/128) * 512). */
 QGEMM_API qgemm_status qgemm_w4_frag_bytes(int K, int N, size_t* bytes);

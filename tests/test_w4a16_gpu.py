@@ -75,19 +75,19 @@ def frag(gpu, x, wq, sc, M, N, K, G, zp=8):
 
 def frag_layout_numpy(wq, K, N):
     """The documented fragment order: unit (c, kb) = columns 8c..8c+7 x rows
-    128kb..128kb+127; lane 4g+t, word s holds column 8c+g at rows 128kb + 32s +
-    {2t, 2t+16, 2t+8, 2t+24, 2t+1, 2t+17, 2t+9, 2t+25}, nibble i at bits 4i.."""
+    128kb..128kb+127; lane 4g+t, word s holds column 8c+g at rows 128kb + 32s + 8t +
+    {0, 4, 2, 6, 1, 5, 3, 7}, nibble i at bits 4i.."""
     nkb = (K + 127) // 128
     q = (wq[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 0xF   # [K, N/8, 8]
     q = q.reshape(K, N).astype(np.uint32)
     qp = np.zeros((nkb * 128, N), np.uint32)
     qp[:K] = q
     g, t = np.arange(32) // 4, np.arange(32) % 4
-    offs = np.array([0, 16, 8, 24, 1, 17, 9, 25])
+    offs = np.array([0, 4, 2, 6, 1, 5, 3, 7])
     out = np.zeros((N // 8, nkb, 32, 4), np.uint32)
     for kb in range(nkb):
         for s in range(4):
-            rows = kb * 128 + 32 * s + 2 * t[:, None] + offs[None, :]    # [32 lanes, 8 nibbles]
+            rows = kb * 128 + 32 * s + 8 * t[:, None] + offs[None, :]    # [32 lanes, 8 nibbles]
             for c in range(N // 8):
                 vals = qp[rows, 8 * c + g[:, None]]                        # [32, 8]
                 out[c, kb, :, s] = (vals << (4 * np.arange(8, dtype=np.uint32))).sum(axis=1)
