@@ -618,25 +618,32 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
     int4 group-128 weights (zero point 8, bf16 scales ~U[0.005, 0.02]), bf16
     activations ~N(0,1).  Prefill: batch x seq = 32 x 512 = 16384 rows through the
     prefill path; decode: 32 rows through the decode kernel (one CUDA graph per step).
-    One step = every linear of every layer once."""
+    One step = every linear of every layer once.  Each weight is stored once: in the
+    fragment order where the frag decode kernel takes it (K <= 4096: qkv, o, gate+up),
+    in 64-column tiles otherwise (down, K = 11008); prefill and decode read that copy."""
     import torch
     G = 128
     gen = torch.Generator(device="cuda")
     gen.manual_seed(2024)
-    W = []  # (name, K, N, tiled weights, scales)
+    W = []  # (name, K, N, prepacked weights, scales, layout)
     for _ in range(layers):
         for name, K, N in LLAMA_LINEARS:
             q = torch.randint(-2**31, 2**31 - 1, (K, N // 8), dtype=torch.int32, device="cuda",
                               generator=gen)
-            wt = torch.empty(ops.w4TiledBytes(K, N), dtype=torch.uint8, device="cuda")
-            ops.prepackW4Tiled(q, wt, K, N)
+            lay = "frag" if K <= 4096 else "tiled"
+            if lay == "frag":
+                wt = torch.empty(ops.w4FragBytes(K, N), dtype=torch.uint8, device="cuda")
+                ops.prepackW4Frag(q, wt, K, N)
+            else:
+                wt = torch.empty(ops.w4TiledBytes(K, N), dtype=torch.uint8, device="cuda")
+                ops.prepackW4Tiled(q, wt, K, N)
             sc = (torch.rand((K // G, N), device="cuda", generator=gen) * 0.015 + 0.005).to(
                 torch.bfloat16)
-            W.append((name, K, N, wt, sc))
+            W.append((name, K, N, wt, sc, lay))
             del q
     torch.cuda.synchronize()
-    weights_bytes = sum(K * N // 2 + (K // G) * N * 2 for _, K, N, _, _ in W)
-    flops_per_row = sum(2.0 * K * N for _, K, N, _, _ in W)
+    weights_bytes = sum(K * N // 2 + (K // G) * N * 2 for _, K, N, _, _, _ in W)
+    flops_per_row = sum(2.0 * K * N for _, K, N, _, _, _ in W)
     res = {"layers": layers, "group_size": G, "weight_bytes": weights_bytes}
 
     # ---- prefill ----
@@ -649,9 +656,9 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
 
     def prefill_step():
-        for _, K, N, wt, sc in W:
-            ops.w4a16GemmGroupedPrefill(xs[K], wt, sc, ys[N], M, N, K, ws, ws_bytes,
-                                        zero_point=8, group_size=G)
+        for _, K, N, wt, sc, lay in W:
+            f = ops.w4a16GemmGroupedPrefillFrag if lay == "frag" else ops.w4a16GemmGroupedPrefill
+            f(xs[K], wt, sc, ys[N], M, N, K, ws, ws_bytes, zero_point=8, group_size=G)
 
     prefill_step()
     torch.cuda.synchronize()
@@ -683,8 +690,9 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
     o = type(ops)(q)
 
     def decode_step():
-        for _, K, N, wt, sc in W:
-            o.w4a16GemmGroupedTiled(xd[K], wt, sc, yd[N], M, N, K, zero_point=8, group_size=G)
+        for _, K, N, wt, sc, lay in W:
+            f = o.w4a16GemmGroupedFrag if lay == "frag" else o.w4a16GemmGroupedTiled
+            f(xd[K], wt, sc, yd[N], M, N, K, zero_point=8, group_size=G)
 
     cap.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(cap):
@@ -703,7 +711,7 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
     e1.record()
     torch.cuda.synchronize()
     t = e0.elapsed_time(e1) / 1e3 / decode_steps
-    bytes_step = weights_bytes + sum(M * K * 2 + M * N * 2 for _, K, N, _, _ in W)
+    bytes_step = weights_bytes + sum(M * K * 2 + M * N * 2 for _, K, N, _, _, _ in W)
     res["decode"] = {"M": M, "ms_per_step": t * 1e3, "GB_s": bytes_step / t / 1e9,
                      "frac_of_hbm": bytes_step / t / 1e9 / peaks["hbm_gbs"],
                      "bytes_per_step": bytes_step}

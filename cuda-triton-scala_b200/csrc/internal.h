@@ -169,9 +169,10 @@ size_t w4_frag_bytes(int K, int N);
 qgemm_status launch_prepack_w4_frag(qgemm_stream_s* s, const uint32_t* src, uint32_t* dst, int K,
                                     int N);
 size_t w4a16_prefill_workspace_bytes(int K, int N);
+// frag: wt is in the fragment order of qgemm_prepack_w4_frag instead of 64-column tiles
 qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
                                   const void* scales, int zp, int G, void* y, int M, int N,
-                                  int K, void* ws, size_t ws_bytes);
+                                  int K, void* ws, size_t ws_bytes, bool frag);
 qgemm_status launch_w4a16_grouped(qgemm_stream_s* s, const void* x, const uint32_t* wq,
                                   const void* scales, int zp, int group, void* y, int M,
                                   int N, int K);

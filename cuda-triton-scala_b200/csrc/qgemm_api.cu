@@ -532,10 +532,9 @@ qgemm_status qgemm_w4a16_prefill_workspace_bytes(int K, int N, size_t* bytes) {
   return QGEMM_OK;
 }
 
-qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint64_t wt,
-                                              uint64_t scales, int zero_point, int group_size,
-                                              uint64_t y, int M, int N, int K, uint64_t workspace,
-                                              size_t workspace_bytes) {
+static qgemm_status prefill_entry(qgemm_stream_t s, uint64_t x, uint64_t wt, uint64_t scales,
+                                  int zero_point, int group_size, uint64_t y, int M, int N,
+                                  int K, uint64_t workspace, size_t workspace_bytes, bool frag) {
   QG_TRY(enter(s));
   QG_TRY(check_dims(M, N, K));
   if (group_size <= 0) return fail(QGEMM_ERR_INVALID_ARG, "group_size %d <= 0", group_size);
@@ -547,6 +546,10 @@ qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint
   if (M == 0 || N == 0) return QGEMM_OK;
   if (K == 0) return fail(QGEMM_ERR_UNSUPPORTED, "K == 0 on the prefill path");
   if (K % 8 != 0) return fail(QGEMM_ERR_UNSUPPORTED, "K %d is not a multiple of 8", K);
+  if (frag && (K % 16 != 0 || !(group_size == 32 || group_size == 64 || group_size % 128 == 0)))
+    return fail(QGEMM_ERR_UNSUPPORTED,
+                "fragment-ordered weights need K %% 16 == 0 and group_size 32, 64 or a "
+                "multiple of 128 (K=%d, group_size=%d)", K, group_size);
   if (!s->dev->tcgen05) return fail(QGEMM_ERR_UNSUPPORTED, "device is not sm_100");
   QG_TRY(need(x, "x")); QG_TRY(need(wt, "wt")); QG_TRY(need(scales, "scales"));
   QG_TRY(need(y, "y")); QG_TRY(need(workspace, "workspace"));
@@ -557,7 +560,24 @@ qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint
                               reinterpret_cast<const uint8_t*>(wt),
                               reinterpret_cast<const void*>(scales), zero_point, group_size,
                               reinterpret_cast<void*>(y), M, N, K,
-                              reinterpret_cast<void*>(workspace), workspace_bytes);
+                              reinterpret_cast<void*>(workspace), workspace_bytes, frag);
+}
+
+qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint64_t wt,
+                                              uint64_t scales, int zero_point, int group_size,
+                                              uint64_t y, int M, int N, int K, uint64_t workspace,
+                                              size_t workspace_bytes) {
+  return prefill_entry(s, x, wt, scales, zero_point, group_size, y, M, N, K, workspace,
+                       workspace_bytes, false);
+}
+
+qgemm_status qgemm_w4a16_grouped_gemm_prefill_frag(qgemm_stream_t s, uint64_t x, uint64_t wf,
+                                                   uint64_t scales, int zero_point,
+                                                   int group_size, uint64_t y, int M, int N,
+                                                   int K, uint64_t workspace,
+                                                   size_t workspace_bytes) {
+  return prefill_entry(s, x, wf, scales, zero_point, group_size, y, M, N, K, workspace,
+                       workspace_bytes, true);
 }
 
 qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t out, int ldc,

@@ -83,6 +83,64 @@ __global__ void __launch_bounds__(256) dequant_slab_kernel(
   }
 }
 
+// The same expansion from the fragment order of w4a16_frag.cu (unit (c, kb) = columns
+// 8c..8c+7 x rows 128kb..128kb+127, 512 bytes, c-major; lane 4g+t's word s holds
+// column 8c+g at rows 128kb + 32s + 8t + {0, 4, 2, 6, 1, 5, 3, 7}, nibble i at bits
+// 4i).  One CTA: 8 consecutive column groups (64 columns) x one 128-row block; thread
+// 32u + lane loads that lane's 16 bytes of unit u and places its 32 weights in the
+// transposed shared tiles; the write-out is the one above.
+__global__ void __launch_bounds__(256) dequant_slab_frag_kernel(
+    const uint4* __restrict__ wf, const __nv_bfloat16* __restrict__ scales, int zp, int G,
+    __nv_bfloat16* __restrict__ dst, int K, int Kp, int N, int NKB, int n0, int ncols) {
+  __shared__ __align__(16) __nv_bfloat16 tr[2][TW][KR + PAD];  // 34.8 KB
+  const int col0 = n0 + blockIdx.x * TW;  // first column of this CTA (a multiple of 8)
+  const int kb = blockIdx.y, k0 = kb * KR;
+  const int u = threadIdx.x >> 5, ln = threadIdx.x & 31;
+  const int g = ln >> 2, t = ln & 3;
+  const int cg = col0 / 8 + u;            // column group
+  const int c = 8 * u + g;                // column within the CTA
+  const int n = col0 + c;
+  const int srows = K / G;
+  uint4 w = make_uint4(0u, 0u, 0u, 0u);
+  if (n < N) w = __ldg(wf + ((size_t)cg * NKB + kb) * 32 + ln);
+  const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+  const float fzp = (float)zp;
+  const int off[8] = {0, 4, 2, 6, 1, 5, 3, 7};
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int rb = 32 * s + 8 * t;        // this lane's 8 rows of step s: rb .. rb+7
+    const int grow = (k0 + rb) / G;       // one scale group (G >= 32 and G | 32s)
+    const float sc = (n < N && k0 + rb < K && grow < srows)
+                         ? __bfloat162float(scales[(size_t)grow * N + n]) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = rb + off[i];
+      float v = 0.f;
+      if (n < N && k0 + r < K) v = ((float)((wv[s] >> (4 * i)) & 0xFu) - fzp) * sc;  // exact
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      tr[0][c][r] = hi;
+      tr[1][c][r] = __float2bfloat16_rn(v - __bfloat162float(hi));  // exact
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = lane >> 4;                  // lanes 0-15 write hi, 16-31 write lo
+  const int kk = 8 * (lane & 15);           // this lane's 8 elements (16 bytes)
+#pragma unroll
+  for (int i = 0; i < TW / 8; ++i) {
+    const int cc = warp * (TW / 8) + i;
+    const int nn = col0 + cc - n0;          // slab row
+    if (nn >= ncols || k0 + kk >= Kp) continue;  // Kp % 64 == 0: whole 16-byte pieces
+    __nv_bfloat16* drow = dst + (size_t)nn * 2 * Kp + (size_t)h * Kp + k0 + kk;
+    if (k0 + kk + 8 <= K) {
+      *reinterpret_cast<uint4*>(drow) = *reinterpret_cast<const uint4*>(&tr[h][cc][kk]);
+    } else {  // the tail of K and the zero padding up to Kp
+      for (int e = 0; e < 8; ++e)
+        drow[e] = (k0 + kk + e < K) ? tr[h][cc][kk + e] : __float2bfloat16_rn(0.f);
+    }
+  }
+}
+
 }  // namespace w4p
 
 static size_t padded_k(int K) { return ((size_t)K + 63) / 64 * 64; }
@@ -94,7 +152,7 @@ size_t w4a16_prefill_workspace_bytes(int K, int N) {
 
 qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
                                   const void* scales, int zp, int G, void* y, int M, int N,
-                                  int K, void* ws, size_t ws_bytes) {
+                                  int K, void* ws, size_t ws_bytes, bool frag) {
   using namespace w4p;
   // slab width: as many columns as the workspace holds, a multiple of 256 (so that
   // every slab but the last fills whole 256-column GEMM tiles)
@@ -112,9 +170,14 @@ qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_
   for (size_t n0 = 0; n0 < (size_t)N; n0 += cols) {
     const int ncols = (int)(((size_t)N - n0) < cols ? ((size_t)N - n0) : cols);
     dim3 grid2((ncols + TW - 1) / TW, (unsigned)((Kp + KR - 1) / KR));
-    dequant_slab_kernel<<<grid2, 256, 0, s->stream>>>(
-        wt, static_cast<const __nv_bfloat16*>(scales), zp, G, slab, K, (int)Kp, N, (int)n0,
-        ncols);
+    if (frag)  // Kp rounds K up to 64, the layout to 128: the grid's blocks are the layout's
+      dequant_slab_frag_kernel<<<grid2, 256, 0, s->stream>>>(
+          reinterpret_cast<const uint4*>(wt), static_cast<const __nv_bfloat16*>(scales), zp, G,
+          slab, K, (int)Kp, N, (K + KR - 1) / KR, (int)n0, ncols);
+    else
+      dequant_slab_kernel<<<grid2, 256, 0, s->stream>>>(
+          wt, static_cast<const __nv_bfloat16*>(scales), zp, G, slab, K, (int)Kp, N, (int)n0,
+          ncols);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "dequant_slab launch");
     const qgemm_status st = launch_bf16_gemm_nk(

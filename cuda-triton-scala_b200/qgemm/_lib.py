@@ -91,6 +91,8 @@ SIGNATURES = {
     "qgemm_w4a16_grouped_gemm_frag": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I]),
     "qgemm_w4_frag_bytes": (_S, [_I, _I, ctypes.POINTER(_SZ)]),
     "qgemm_prepack_w4_frag": (_S, [_P, _U64, _U64, _I, _I]),
+    "qgemm_w4a16_grouped_gemm_prefill_frag": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I,
+                                                   _I, _U64, _SZ]),
     "qgemm_w4a16_prefill_workspace_bytes": (_S, [_I, _I, ctypes.POINTER(_SZ)]),
     "qgemm_w4a16_grouped_gemm_prefill": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I,
                                                _U64, _SZ]),

@@ -111,6 +111,15 @@ class QuantizedGemmOps:
                L.addr(scales), zero_point, group_size, L.addr(y), M, N, K, L.addr(workspace),
                workspace_bytes)
 
+    def w4a16GemmGroupedPrefillFrag(self, x, wf, scales, y, M: int, N: int, K: int, workspace,
+                                    workspace_bytes: int, *, zero_point: int = 8,
+                                    group_size: int = 128):
+        """The prefill GEMM on prepackW4Frag weights (one weight copy for prefill and
+        decode)."""
+        L.call("qgemm_w4a16_grouped_gemm_prefill_frag", self._h, L.addr(x), L.addr(wf),
+               L.addr(scales), zero_point, group_size, L.addr(y), M, N, K, L.addr(workspace),
+               workspace_bytes)
+
     def gemmBf16NK(self, A, B, out, M: int, N: int, K: int, *, ldc: int | None = None):
         """out[M, ldc] bf16 = A[M,K] (bf16) x B[N,K]^T (bf16), fp32 sums."""
         L.call("qgemm_gemm_bf16_nk", self._h, L.addr(A), L.addr(B), L.addr(out),

@@ -251,6 +251,16 @@ QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64
                                                         int group_size, uint64_t y, int M, int N,
                                                         int K, uint64_t workspace,
                                                         size_t workspace_bytes);
+/* The same prefill GEMM on weights in the fragment order of qgemm_prepack_w4_frag,
+ * so that one stored copy serves both prefill and the frag decode path.  The
+ * workspace is as above; additionally requires K % 16 == 0 and group_size 32, 64 or
+ * a multiple of 128. */
+QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_prefill_frag(qgemm_stream_t s, uint64_t x,
+                                                             uint64_t wf, uint64_t scales,
+                                                             int zero_point, int group_size,
+                                                             uint64_t y, int M, int N, int K,
+                                                             uint64_t workspace,
+                                                             size_t workspace_bytes);
 
 /* bf16 GEMM on the tcgen05 kernels (no counterpart among the reference's quantized
  * operators; it is the multiply of the W4A16 prefill path):

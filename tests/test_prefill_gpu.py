@@ -115,6 +115,50 @@ def test_prefill_and_decode_paths_agree(gpu):
     assert rel_err(a, b) <= TOL_BF16
 
 
+def prefill_frag(gpu, x, wq, sc, M, N, K, G, zp=8, ws_bytes=None):
+    """The same prefill GEMM on fragment-ordered weights (qgemm_prepack_w4_frag)."""
+    dev, st, ops = gpu
+    wf = Out(dev, st, ops.w4FragBytes(K, N))
+    ops.prepackW4Frag(dev_array(gpu, wq), wf, K, N)
+    full = ops.w4PrefillWorkspaceBytes(K, N)
+    ws_bytes = full if ws_bytes is None else ws_bytes
+    ws = Out(dev, st, max(ws_bytes, 16))
+    y = Out(dev, st, M * N * 2)
+    ops.w4a16GemmGroupedPrefillFrag(dev_array(gpu, x), wf, dev_array(gpu, sc), y, M, N, K, ws,
+                                    ws_bytes, zero_point=zp, group_size=G)
+    st.sync()
+    return y.read(np.uint16, (M, N))
+
+
+@pytest.mark.parametrize("M,N,K,G,zp", [
+    (300, 512, 1024, 128, 8),
+    (256, 768, 2048, 64, 3),
+    (300, 520, 1056, 32, 8),     # N % 64 == 8 and K % 128 == 32: partial last CTA and block
+    (64, 4096, 4096, 256, 15),
+])
+def test_prefill_frag_vs_oracle_and_tiled(gpu, oracle, M, N, K, G, zp):
+    """Against the oracle, and bit for bit against the tiled-weight prefill: both
+    expand to the same bf16 slab and run the same GEMM."""
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M + N + K + G + 1)
+    y = prefill_frag(gpu, x, wq, sc, M, N, K, G, zp)
+    ref, _ = oracle.w4a16_grouped(wq, sc, zp, G, x)
+    assert rel_err(syn.bf16_to_float(y), ref) <= TOL_BF16
+    np.testing.assert_array_equal(y, prefill(gpu, x, wq, sc, M, N, K, G, zp))
+
+
+def test_prefill_frag_slab_width_and_refusals(gpu):
+    M, N, K, G = 200, 1000, 768, 64
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=74)
+    kp = (K + 63) // 64 * 64
+    np.testing.assert_array_equal(prefill_frag(gpu, x, wq, sc, M, N, K, G),
+                                  prefill_frag(gpu, x, wq, sc, M, N, K, G, ws_bytes=256 * kp * 4))
+    x, wq, sc = syn.w4a16_inputs(8, 64, 96, group=48, seed=75)
+    with pytest.raises(qgemm.QGemmError) as e:
+        prefill_frag(gpu, x, wq, sc, 8, 64, 96, 48)
+    assert e.value.status == qgemm._lib.ERR_UNSUPPORTED
+    gpu[1].sync()
+
+
 def test_prefill_errors(gpu):
     dev, st, ops = gpu
     M, N, K, G = 256, 256, 512, 128
