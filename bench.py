@@ -339,8 +339,8 @@ def library_int8_context(hb, steps):
 
 
 def w4a16_profile(ops, steps, warmup):
-    """The M = 1 decode GEMV as warmup + steps plain launches (no graph), for ncu: the
-    64-column-tile kernel, then the fragment-order kernel, each on its own layout."""
+    """The decode GEMV as warmup + steps plain launches each (no graph), for ncu: M = 1
+    on the 64-column-tile kernel, then M = 1 and M = 16 on the fragment order."""
     import torch
     N, K, G, R = 14336, 4096, 128, 8
     gen = torch.Generator(device="cuda")
@@ -366,8 +366,13 @@ def w4a16_profile(ops, steps, warmup):
         ops.prepackW4Frag(w0, wf[-1], K, N)
     for i in range(warmup + steps):
         ops.w4a16GemmGroupedFrag(x, wf[i % R], sc[i % R], y, 1, N, K, zero_point=8, group_size=G)
+    x16 = torch.randn((16, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y16 = torch.empty((16, N), dtype=torch.bfloat16, device="cuda")
+    for i in range(warmup + steps):
+        ops.w4a16GemmGroupedFrag(x16, wf[i % R], sc[i % R], y16, 16, N, K, zero_point=8,
+                                 group_size=G)
     torch.cuda.synchronize()
-    return {"launches": warmup + steps, "M": 1, "N": N, "K": K}
+    return {"launches": warmup + steps, "M": [1, 16], "N": N, "K": K}
 
 
 def w4a16_decode(ops, peaks):
