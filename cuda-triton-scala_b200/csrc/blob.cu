@@ -6,7 +6,8 @@
 //   bytes 0..63    header
 //     0   char[8]  magic "QGEMMBLB"
 //     8   u32      format version (QGEMM_BLOB_VERSION)
-//     12  i32      kind (QGEMM_BLOB_W4_TILED, QGEMM_BLOB_W8_KN, QGEMM_BLOB_W8_NK)
+//     12  i32      kind (QGEMM_BLOB_W4_TILED, QGEMM_BLOB_W8_KN, QGEMM_BLOB_W8_NK,
+//                   QGEMM_BLOB_W4_FRAG)
 //     16  i32      K
 //     20  i32      N
 //     24  i32      group_size (W4) or 0
@@ -22,6 +23,7 @@
 //   W4_TILED  weights: qgemm_w4_tiled_bytes(K, N); scales: bf16 [K/group_size, N]
 //   W8_KN     weights: int8 [K, N] (the reference wInt8 layout); scales: f32 [N]
 //   W8_NK     weights: int8 [N, K]; scales: f32 [N]
+//   W4_FRAG   weights: qgemm_w4_frag_bytes(K, N); scales: bf16 [K/group_size, N]
 // CRC-32 is the common reflected polynomial 0xEDB88320 (initial and final value
 // 0xFFFFFFFF).
 #include <cstdio>
@@ -74,12 +76,13 @@ bool expected_sizes(const qgemm_blob_info& in, uint64_t* wb, uint64_t* sb, const
   if (in.K <= 0 || in.N <= 0) { *why = "K and N must be positive"; return false; }
   switch (in.kind) {
     case QGEMM_BLOB_W4_TILED:
+    case QGEMM_BLOB_W4_FRAG:
       if (in.N % 8 != 0) { *why = "N must be a multiple of 8 for int4 weights"; return false; }
       if (in.group_size <= 0 || in.K % in.group_size != 0) {
         *why = "group_size must be positive and divide K"; return false;
       }
       if (in.zero_point < 0 || in.zero_point > 15) { *why = "zero_point outside [0,15]"; return false; }
-      *wb = w4_tiled_bytes(in.K, in.N);
+      *wb = in.kind == QGEMM_BLOB_W4_FRAG ? w4_frag_bytes(in.K, in.N) : w4_tiled_bytes(in.K, in.N);
       *sb = (uint64_t)(in.K / in.group_size) * (uint64_t)in.N * 2;
       return true;
     case QGEMM_BLOB_W8_KN:

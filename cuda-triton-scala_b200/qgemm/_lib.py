@@ -37,6 +37,7 @@ BLOB_VERSION = 1
 BLOB_W4_TILED = 1
 BLOB_W8_KN = 2
 BLOB_W8_NK = 3
+BLOB_W4_FRAG = 4
 
 
 class BlobInfo(ctypes.Structure):

@@ -344,7 +344,8 @@ QGEMM_API qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name,
 enum {
   QGEMM_BLOB_W4_TILED = 1,  /* qgemm_prepack_w4_tiled layout + bf16 scales [K/G, N]   */
   QGEMM_BLOB_W8_KN = 2,     /* int8 [K, N] (reference wInt8 layout) + f32 scales [N]  */
-  QGEMM_BLOB_W8_NK = 3      /* int8 [N, K] + f32 scales [N]                           */
+  QGEMM_BLOB_W8_NK = 3,     /* int8 [N, K] + f32 scales [N]                           */
+  QGEMM_BLOB_W4_FRAG = 4    /* qgemm_prepack_w4_frag layout + bf16 scales [K/G, N]    */
 };
 typedef struct qgemm_blob_info {
   uint32_t version;      /* filled in by qgemm_blob_info_read                         */

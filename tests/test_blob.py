@@ -30,6 +30,23 @@ def test_round_trip_w4(tmp_path):
     assert os.path.getsize(p) == 64 + w.nbytes + s.nbytes
 
 
+def test_round_trip_w4_frag(tmp_path):
+    """The fragment-order kind: weight bytes N/8 * ceil(K/128) * 512 (K = 160: two
+    128-row blocks, the second partly past K)."""
+    K, N, G = 160, 24, 32
+    rng = np.random.default_rng(3)
+    w = rng.integers(0, 256, (N // 8) * 2 * 512, dtype=np.uint8)
+    s = rng.integers(0, 2**16, (K // G, N), dtype=np.uint16)
+    p = str(tmp_path / "f.qgb")
+    blob.save(p, "w4_frag", K, N, w, s, group_size=G, zero_point=8)
+    meta, w2, s2 = blob.load(p)
+    assert meta["kind"] == "w4_frag" and meta["weight_bytes"] == w.nbytes
+    np.testing.assert_array_equal(w2, w)
+    np.testing.assert_array_equal(s2.view(np.uint16).reshape(K // G, N), s)
+    with pytest.raises(ValueError):  # a weight section of the wrong size
+        blob.save(p, "w4_frag", K, N, w[:1024], s, group_size=G, zero_point=8)
+
+
 @pytest.mark.parametrize("kind", ["w8_kn", "w8_nk"])
 def test_round_trip_w8(tmp_path, kind):
     K, N = 300, 128

@@ -303,6 +303,31 @@ def test_grouped_rejects_bad_args(gpu):
     st.sync()
 
 
+def test_frag_blob_round_trip_through_the_device(gpu, tmp_path):
+    """Fragment-ordered weights saved as a blob and loaded straight into device memory
+    decode to the same bits as the freshly prepacked ones."""
+    from qgemm import blob
+    dev, st, ops = gpu
+    M, N, K, G = 2, 1024, 2048, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=82)
+    nbytes = ops.w4FragBytes(K, N)
+    wf = Out(dev, st, nbytes)
+    ops.prepackW4Frag(dev_array(gpu, wq), wf, K, N)
+    st.sync()
+    p = str(tmp_path / "layer_frag.qgb")
+    blob.save(p, "w4_frag", K, N, wf.read(np.uint8, (nbytes,)), sc, group_size=G, zero_point=8)
+    wf2 = Out(dev, st, nbytes)
+    sc2 = Out(dev, st, sc.nbytes)
+    blob.load_to_device(st, p, wf2, nbytes, sc2, sc.nbytes)
+    ys = []
+    for w_, s_ in ((wf, dev_array(gpu, sc)), (wf2, sc2)):
+        y = Out(dev, st, M * N * 2)
+        ops.w4a16GemmGroupedFrag(dev_array(gpu, x), w_, s_, y, M, N, K, group_size=G)
+        st.sync()
+        ys.append(y.read(np.uint16, (M, N)).copy())
+    np.testing.assert_array_equal(ys[0], ys[1])
+
+
 def test_blob_round_trip_through_the_device(gpu, tmp_path):
     """Prepacked weights saved as a blob and loaded straight into device memory run
     the tiled GEMM to the same bits as the freshly prepacked ones."""
