@@ -11,12 +11,14 @@
 // with IEEE fp32 division and multiplication (no fused or approximate forms), so the
 // result is bit-identical to the reference arithmetic.  x is fp32 or bf16 (widened).
 //
-// One CTA per row.  Rows of up to 256 x 4 vectors of 16 bytes (bf16: K <= 8192,
-// fp32: K <= 4096) with 16-byte aligned rows are read once into registers with vector
-// loads, reduced to maxAbs, quantised from the registers and written with vector
-// stores (quantize_rows_vec_kernel).  Other rows take two passes: maxAbs, then the
-// int8 row, the second pass served from L2 (quantize_rows_kernel).  HBM-bound: one
-// read of x, one write of q.
+// Rows of up to 512 vectors of 16 bytes (bf16: K <= 4096, fp32: K <= 2048) with
+// 16-byte aligned rows: one warp per row (quantize_rows_warp_kernel).  Each lane issues
+// all its 16-byte loads at once (a whole 8 KB row in flight per warp), the maximum is a
+// warp shuffle reduction (no block barrier), and the row is quantised from registers.
+// Longer rows of up to 256 x 4 vectors: one CTA per row, the same in registers with a
+// block-wide maximum (quantize_rows_vec_kernel).  Other rows take two passes: maxAbs,
+// then the int8 row, the second pass served from L2 (quantize_rows_kernel).
+// HBM-bound: one read of x, one write of q.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -190,6 +192,86 @@ __global__ void __launch_bounds__(THREADS) quantize_rows_vec_kernel(const T* __r
   }
 }
 
+// One row per warp, 8 warps per CTA; NVW vectors of 16 bytes per lane kept as loaded
+// (raw bits) and widened twice, once for the maximum and once to quantise.
+template <typename T, int NVW>
+__global__ void __launch_bounds__(256, (sizeof(T) == 2 && NVW == 16) ? 2 : 3) quantize_rows_warp_kernel(const T* __restrict__ x,
+                                                                 int8_t* __restrict__ q,
+                                                                 float* __restrict__ sA, int M,
+                                                                 int K) {
+  constexpr int VEC = Vec<T>::N;
+  // The GEMM that consumes q and sA may begin its set-up; it reads them only after
+  // griddepcontrol.wait, i.e. after this grid has finished.
+  ptx::grid_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (m >= M) return;
+  const T* row = x + (size_t)m * K;
+  const int nvec = K / VEC;
+  uint4 raw[NVW];
+#pragma unroll
+  for (int j = 0; j < NVW; ++j) {
+    const int vi = lane + 32 * j;
+    raw[j] = vi < nvec ? __ldcs(reinterpret_cast<const uint4*>(row) + vi)
+                       : make_uint4(0u, 0u, 0u, 0u);
+  }
+  auto widen = [](const uint4& u, float (&v)[VEC]) {
+    if constexpr (VEC == 8) {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    } else {
+      v[0] = __uint_as_float(u.x); v[1] = __uint_as_float(u.y);
+      v[2] = __uint_as_float(u.z); v[3] = __uint_as_float(u.w);
+    }
+  };
+  // maxAbs in the "if (v > m) m = v" form (NaN never replaces a number); lanes past the
+  // row hold zeros, which never exceed a maximum that starts at zero
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NVW; ++j) {
+    float v[VEC];
+    widen(raw[j], v);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const float a = fabsf(v[i]);
+      if (a > mx) mx = a;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, mx, off);
+    if (o > mx) mx = o;
+  }
+  const float mul = (mx > 1e-6f) ? __fdiv_rn(127.0f, mx) : 1.0f;
+  if (lane == 0) sA[m] = __fdiv_rn(mx, 127.0f);
+  int8_t* qrow = q + (size_t)m * K;
+#pragma unroll
+  for (int j = 0; j < NVW; ++j) {
+    const int vi = lane + 32 * j;
+    if (vi < nvec) {
+      float v[VEC];
+      widen(raw[j], v);
+      uint32_t packed[VEC / 4];
+#pragma unroll
+      for (int w = 0; w < VEC / 4; ++w) {
+        uint32_t b = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          b |= (uint32_t)(uint8_t)quant(v[4 * w + i], mul) << (8 * i);
+        packed[w] = b;
+      }
+      if constexpr (VEC == 8)
+        *reinterpret_cast<uint2*>(qrow + (size_t)vi * VEC) = make_uint2(packed[0], packed[1]);
+      else
+        *reinterpret_cast<uint32_t*>(qrow + (size_t)vi * VEC) = packed[0];
+    }
+  }
+}
+
 }  // namespace qtok
 
 qgemm_status launch_quantize_tokens(qgemm_stream_s* s, const void* x, int in_dtype, int8_t* q,
@@ -201,6 +283,24 @@ qgemm_status launch_quantize_tokens(qgemm_stream_s* s, const void* x, int in_dty
   const bool vec = K > 0 && K % VEC == 0 && nv <= 4 && aligned((uint64_t)x, 16) &&
                    ((uint64_t)K * (bf ? 2 : 4)) % 16 == 0 && aligned((uint64_t)q, VEC) &&
                    K % VEC == 0;
+  const int nvec = VEC > 0 ? K / VEC : 0;
+  if (vec && nvec <= 16 * 32) {
+    // a warp per row: vectors per lane 4, 8 or 16
+    const int nvw = nvec <= 4 * 32 ? 4 : nvec <= 8 * 32 ? 8 : 16;
+    const unsigned grid = (unsigned)((M + 7) / 8);
+    if (bf) {
+      const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+      if (nvw == 4) quantize_rows_warp_kernel<__nv_bfloat16, 4><<<grid, 256, 0, s->stream>>>(xb, q, sA, M, K);
+      else if (nvw == 8) quantize_rows_warp_kernel<__nv_bfloat16, 8><<<grid, 256, 0, s->stream>>>(xb, q, sA, M, K);
+      else quantize_rows_warp_kernel<__nv_bfloat16, 16><<<grid, 256, 0, s->stream>>>(xb, q, sA, M, K);
+    } else {
+      const float* xf = static_cast<const float*>(x);
+      if (nvw == 4) quantize_rows_warp_kernel<float, 4><<<grid, 256, 0, s->stream>>>(xf, q, sA, M, K);
+      else if (nvw == 8) quantize_rows_warp_kernel<float, 8><<<grid, 256, 0, s->stream>>>(xf, q, sA, M, K);
+      else quantize_rows_warp_kernel<float, 16><<<grid, 256, 0, s->stream>>>(xf, q, sA, M, K);
+    }
+    return cuda_fail(cudaGetLastError(), "quantize_rows_warp launch");
+  }
   if (vec) {
     if (bf) {
       const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
