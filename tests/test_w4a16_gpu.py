@@ -132,6 +132,25 @@ def test_grouped_frag_path(gpu, oracle, M, N, K, G, zp):
     assert err <= TOL_BF16, err
 
 
+@pytest.mark.parametrize("M,N", [(4, 2048), (16, 2048)])
+def test_frag_activation_magnitudes(gpu, oracle, M, N):
+    """Rows of very different magnitude (bf16 values from 1e-30 to 1e30, and an all-zero
+    row): the frag kernels' fp16 arithmetic scales activations by powers of two, so the
+    results stay within the tolerance at every magnitude."""
+    K, G = 2048, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=83)
+    xf = syn.bf16_to_float(x).astype(np.float32)
+    mags = np.array([1.0, 1e30, 1e-30, 0.0, 3e4, 1e-5, 7e12, 2.0] * 2, np.float32)[:M]
+    xf = xf * mags[:, None]
+    xf[M - 1, : K // 2] *= 1e6  # one row whose first half is much larger than its second
+    xb = syn.bf16_bits(xf)
+    y = frag(gpu, xb, wq, sc, M, N, K, G)
+    ref, _ = oracle.w4a16_grouped(wq, sc, 8, G, xb)
+    got = syn.bf16_to_float(y).astype(np.float64)
+    for m in range(M):  # per row: the floor of rel_err scales with the row
+        assert rel_err(got[m], ref[m]) <= TOL_BF16, (m, mags[m])
+
+
 def test_frag_deterministic_and_matches_tiled(gpu):
     M, N, K, G = 4, 14336, 4096, 128
     x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=64)
