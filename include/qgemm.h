@@ -20,6 +20,14 @@
  *    QGEMM_ERR_TIMEOUT.
  *  - Handles are thread-safe per distinct stream; a device handle may be
  *    shared across threads.
+ *  - Kernels use programmatic dependent launch: one may start while the previous
+ *    kernel on the stream finishes, and it waits for that kernel before it reads
+ *    anything the kernel may have written.  The exception is the prepacked weights
+ *    and scales of the W4A16 decode paths (_tiled, _frag), which are static model
+ *    data and are read before that wait.  A caller's kernel that writes them and
+ *    triggers programmatic launch early must be separated from the decode call
+ *    (an event, or a launch without the programmatic attribute); this library's own
+ *    kernels, memcpys and ordinary launches need nothing.
  */
 #ifndef QGEMM_H
 #define QGEMM_H
