@@ -38,9 +38,10 @@ for _p in (ROOT, PKG):
 METRIC = "W8A8 GEMM TOPS & W4A16 GEMV HBM GB/s at 1/2/4/8 B200, % of roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch from one `ncu --set full` capture of the same
-# kernel on the same workload (profiles/w8a8_tcgen05_pair_4096.md, profiles/w4a16_tile_m1.md).
+# kernel on the same workload (profiles/w8a8_tcgen05_pair_4096.md; the M = 1 decode on
+# the fragment order, the faster layout there: profiles/w4a16_frag_m1.md).
 NCU_TRAFFIC_W8A8_4096 = 33694208 + 3904000
-NCU_TRAFFIC_W4A16_M1 = 30312704 + 256
+NCU_TRAFFIC_W4A16_M1 = 30306304 + 0
 # dram__bytes_read.sum + dram__bytes_write.sum of one tf32 GEMM launch of the fp32
 # matmul at 4096^3 (ncu --set full, profiles/f32_tf32_pair_4096.md)
 NCU_TRAFFIC_F32_GEMM_4096 = 985069568 + 61620736
