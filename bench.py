@@ -752,17 +752,22 @@ def w8a8_large(ops, st, rank, world, steps, warmup):
            "value": 2.0 * M * NT * K * steps / t_max / 1e12, "unit": "TOPS",
            "ms_per_step": t_max / steps * 1e3, "scaling": "strong"}
     if world > 1:
-        res["allgather"] = gather_output(st, out, rank, world, M, NL)
+        res["allgather"] = gather_output(st, out, rank, world, M, NL, (A, B, sA, sB, K))
     return res
 
 
-def gather_output(st, out, rank, world, M, NL):
+def gather_output(st, out, rank, world, M, NL, gemm):
     """All-gather of the bf16 output slabs through libqgemm's NCCL communicator,
-    then the [world][M][NL] -> [M][N] unshard kernel; timed separately."""
+    then the [world][M][NL] -> [M][N] unshard kernel; timed separately.  Then the
+    whole sharded layer two ways: the GEMM, the gather and the unshard one after
+    the other on one stream, and qgemm_w8a8_gemm_allgather_bf16, which gathers
+    chunk i of M rows on a second stream while the GEMM of chunk i+1 runs."""
     import ctypes
     import torch
     import torch.distributed as dist
     import qgemm._lib as L
+    from qgemm import B_KN, BF16
+    from qgemm import QuantizedGemmOps as qgemm_ops
     uid = ctypes.create_string_buffer(128)
     if rank == 0:
         L.call("qgemm_comm_unique_id", uid)
@@ -790,8 +795,41 @@ def gather_output(st, out, rank, world, M, NL):
         tg, _ = timed(gather, reps, world)
         tu, _ = timed(unshard, reps, world)
         recv = (world - 1) * M * NL * 2
-        return {"ms": tg / reps * 1e3, "recv_GB_s_per_rank": recv / (tg / reps) / 1e9,
-                "unshard_ms": tu / reps * 1e3, "bytes_total": world * M * NL * 2}
+        res = {"ms": tg / reps * 1e3, "recv_GB_s_per_rank": recv / (tg / reps) / 1e9,
+               "unshard_ms": tu / reps * 1e3, "bytes_total": world * M * NL * 2}
+        A, B, sA, sB, K = gemm
+        ops = qgemm_ops(st)
+
+        def serial(i):
+            ops.w8a8Gemm(A, B, sA, sB, out, M, NL, K, b_layout=B_KN, out_dtype=BF16)
+            gather(i)
+            unshard(i)
+
+        side = torch.cuda.Stream()
+        q_side = st.dev.wrap_stream(side.cuda_stream)
+        for i in range(2):
+            serial(i)
+        ts, _ = timed(serial, reps, world)
+        res["serial_ms"] = ts / reps * 1e3
+        ref = full.clone()
+        for R in (4096, 2048, 1024):
+            wb = L.lib().qgemm_w8a8_allgather_work_bytes(world, R, NL)
+            work = torch.empty(wb, dtype=torch.uint8, device="cuda")
+
+            def piped(i):
+                L.call("qgemm_w8a8_gemm_allgather_bf16", comm, st.handle, q_side.handle,
+                       A.data_ptr(), B.data_ptr(), B_KN, sA.data_ptr(), sB.data_ptr(),
+                       full.data_ptr(), M, NL, K, R, work.data_ptr(), wb)
+
+            full.zero_()
+            for i in range(2):
+                piped(i)
+            tp, _ = timed(piped, reps, world)
+            res[f"pipelined_ms_rows{R}"] = tp / reps * 1e3
+            res[f"pipelined_equal_rows{R}"] = bool(torch.equal(full, ref))
+            del work
+        q_side.destroy()
+        return res
     finally:
         torch.cuda.synchronize()
         L.call("qgemm_comm_destroy", comm)

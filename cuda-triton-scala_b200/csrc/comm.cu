@@ -23,6 +23,9 @@ struct qgemm_comm_s {
   ncclComm_t comm = nullptr;
   qgemm_device_s* dev = nullptr;
   int rank = 0, world = 1;
+  // events of the pipelined GEMM + all-gather, made on its first call
+  cudaEvent_t ev_gemm[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
+  cudaEvent_t ev_end = nullptr;
 };
 
 namespace qg {
@@ -148,6 +151,8 @@ qgemm_status qgemm_comm_init(qgemm_device_t dev, const void* uid, int rank, int 
 
 qgemm_status qgemm_comm_destroy(qgemm_comm_t c) {
   if (!c) return fail(QGEMM_ERR_BAD_HANDLE, "null communicator");
+  for (cudaEvent_t e : {c->ev_gemm[0], c->ev_gemm[1], c->ev_done[0], c->ev_done[1], c->ev_end})
+    if (e) cudaEventDestroy(e);
   NcclApi& n = nccl();
   ncclResult_t r = ncclSuccess;
   if (c->comm && n.CommDestroy) r = n.CommDestroy(c->comm);
@@ -179,6 +184,69 @@ qgemm_status qgemm_comm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, uint64_
     r = as;
   }
   if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+  return QGEMM_OK;
+}
+
+size_t qgemm_w8a8_allgather_work_bytes(int world, int chunk_rows, int n_local) {
+  if (world < 1 || chunk_rows < 1 || n_local < 1) return 0;
+  return (size_t)2 * world * chunk_rows * n_local * 2;
+}
+
+qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, qgemm_stream_t cs,
+                                            uint64_t A, uint64_t B, int b_layout, uint64_t sA,
+                                            uint64_t sB, uint64_t out, int M, int N_local, int K,
+                                            int chunk_rows, uint64_t work, size_t work_bytes) {
+  if (!c || !c->comm) return fail(QGEMM_ERR_BAD_HANDLE, "null communicator");
+  qgemm_status st = enter(cs);
+  if (st != QGEMM_OK) return st;
+  st = enter(s);
+  if (st != QGEMM_OK) return st;
+  if (s->dev != c->dev || cs->dev != c->dev)
+    return fail(QGEMM_ERR_INVALID_ARG, "streams and communicator are on different devices");
+  if (s == cs || s->stream == cs->stream)
+    return fail(QGEMM_ERR_INVALID_ARG, "the GEMM and the gather need two different streams");
+  if (M < 0 || N_local < 0 || K < 0 || chunk_rows < 1)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad sizes M=%d N_local=%d K=%d chunk_rows=%d", M,
+                N_local, K, chunk_rows);
+  if (M == 0 || N_local == 0) return QGEMM_OK;
+  const int world = c->world, rank = c->rank;
+  const int R = chunk_rows < M ? chunk_rows : M;
+  const size_t need = qgemm_w8a8_allgather_work_bytes(world, R, N_local);
+  if (!work || work_bytes < need)
+    return fail(QGEMM_ERR_INVALID_ARG, "work buffer of %zu bytes; %zu needed", work_bytes, need);
+  if (!aligned(work, 16)) return fail(QGEMM_ERR_BAD_ALIGN, "work must be 16-byte aligned");
+  for (cudaEvent_t* e : {&c->ev_gemm[0], &c->ev_gemm[1], &c->ev_done[0], &c->ev_done[1], &c->ev_end})
+    if (!*e) {
+      cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
+      if (ce != cudaSuccess) return cuda_fail(ce, "cudaEventCreate");
+    }
+  const size_t slot_bytes = (size_t)world * R * N_local * 2;
+  const int N = N_local * world;
+  const int nchunks = (M + R - 1) / R;
+  for (int i = 0; i < nchunks; ++i) {
+    const int b = i & 1, m0 = i * R, rows = (M - m0) < R ? (M - m0) : R;
+    const uint64_t buf = work + (uint64_t)b * slot_bytes;  // [world][rows][N_local]
+    const size_t blk = (size_t)rows * N_local;             // bf16 elements per rank
+    const uint64_t mine = buf + (uint64_t)rank * blk * 2;
+    cudaError_t ce = cudaSuccess;
+    if (i >= 2) ce = cudaStreamWaitEvent(s->stream, c->ev_done[b], 0);  // chunk i-2 let go of buf
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamWaitEvent");
+    st = qgemm_w8a8_gemm(s, A + (uint64_t)m0 * K, B, b_layout, sA + (uint64_t)m0 * 4, sB, mine,
+                         QGEMM_BF16, N_local, rows, N_local, K, 0, QGEMM_ALGO_AUTO);
+    if (st != QGEMM_OK) return st;
+    if ((ce = cudaEventRecord(c->ev_gemm[b], s->stream)) != cudaSuccess ||
+        (ce = cudaStreamWaitEvent(cs->stream, c->ev_gemm[b], 0)) != cudaSuccess)
+      return cuda_fail(ce, "event between the GEMM and the gather");
+    st = qgemm_comm_allgather_bf16(c, cs, mine, buf, blk);  // in place
+    if (st != QGEMM_OK) return st;
+    st = qgemm_unshard_columns_bf16(cs, buf, out + (uint64_t)m0 * N * 2, world, rows, N_local);
+    if (st != QGEMM_OK) return st;
+    if ((ce = cudaEventRecord(c->ev_done[b], cs->stream)) != cudaSuccess)
+      return cuda_fail(ce, "cudaEventRecord");
+  }
+  cudaError_t ce = cudaEventRecord(c->ev_end, cs->stream);
+  if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s->stream, c->ev_end, 0);
+  if (ce != cudaSuccess) return cuda_fail(ce, "joining the gather stream");
   return QGEMM_OK;
 }
 

@@ -118,6 +118,9 @@ SIGNATURES = {
     "qgemm_comm_destroy": (_S, [_P]),
     "qgemm_comm_allgather_bf16": (_S, [_P, _P, _U64, _U64, _SZ]),
     "qgemm_unshard_columns_bf16": (_S, [_P, _U64, _U64, _I, _I, _I]),
+    "qgemm_w8a8_allgather_work_bytes": (_SZ, [_I, _I, _I]),
+    "qgemm_w8a8_gemm_allgather_bf16": (_S, [_P, _P, _P, _U64, _U64, _I, _U64, _U64, _U64, _I, _I,
+                                            _I, _I, _U64, _SZ]),
 }
 
 _lib = None

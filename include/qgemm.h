@@ -395,6 +395,26 @@ QGEMM_API qgemm_status qgemm_comm_allgather_bf16(qgemm_comm_t comm, qgemm_stream
 QGEMM_API qgemm_status qgemm_unshard_columns_bf16(qgemm_stream_t s, uint64_t gathered, uint64_t out,
                                         int world, int M, int ncols);
 
+/* The column-sharded W8A8 GEMM followed by its output all-gather, pipelined over
+ * chunks of `chunk_rows` rows of M (the NCCL all-gather step of NCCLOps.ncclAllGather,
+ * NCCLOps.scala:302-320, fed by the GEMM instead of host arrays): the GEMM of chunk i
+ * runs on stream s while the in-place all-gather and unshard of chunk i-1 run on
+ * stream cs, on every rank of `comm`.  This rank's B [K, N_local] (b_layout as in
+ * qgemm_w8a8_gemm) and sB [N_local]; A [M, K] and sA [M] are the same on every rank.
+ * out: bf16 [M, N_local * world], the whole output, on every rank.  work: at least
+ * qgemm_w8a8_allgather_work_bytes(world, min(chunk_rows, M), N_local) bytes, 16-byte
+ * aligned (two chunks of gather buffers).  s and cs must differ; when the call
+ * returns, s is ordered after all of its work (cs too has finished it).  The events it
+ * needs are made on the communicator's first call.  Every rank must make the same
+ * calls in the same order. */
+QGEMM_API size_t qgemm_w8a8_allgather_work_bytes(int world, int chunk_rows, int n_local);
+QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t comm, qgemm_stream_t s,
+                                                      qgemm_stream_t cs, uint64_t A, uint64_t B,
+                                                      int b_layout, uint64_t sA, uint64_t sB,
+                                                      uint64_t out, int M, int N_local, int K,
+                                                      int chunk_rows, uint64_t work,
+                                                      size_t work_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,106 @@
+"""Column-sharded W8A8 with its output all-gather on two GPUs, one process per GPU.
+
+qgemm_w8a8_gemm_allgather_bf16 runs each rank's GEMM slice chunk by chunk of M and
+all-gathers every chunk over NCCL while the next chunk's GEMM runs (NCCLOps.scala:302-320
+is the reference's all-gather).  Every rank must end with the whole [M, N] output,
+bit for bit the unsharded product from the oracle.  Skipped with fewer than two GPUs.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CASES = [  # M, N, K, chunk_rows
+    (300, 512, 256, 64),     # five chunks, the last one 44 rows
+    (256, 1024, 512, 1000),  # one chunk
+    (130, 528, 96, 16),      # many chunks; 264 columns per rank
+]
+
+
+def _rank_main(rank, world, q_id, q_out):
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "cuda-triton-scala_b200")]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import ctypes
+    import qgemm
+    import qgemm._lib as L
+    import qgemm.synthetic as syn
+    dev = qgemm.Device(rank)
+    s, cs = dev.stream(), dev.stream()
+    uid = ctypes.create_string_buffer(128)
+    if rank == 0:
+        L.call("qgemm_comm_unique_id", uid)
+        for _ in range(world - 1):
+            q_id.put(bytes(uid.raw))
+    else:
+        uid = ctypes.create_string_buffer(q_id.get(timeout=60), 128)
+    comm = ctypes.c_void_p()
+    L.call("qgemm_comm_init", dev.handle, uid, rank, world, ctypes.byref(comm))
+    results, errors = [], []
+    try:
+        for M, N, K, R in CASES:
+            A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K)
+            n0, n1 = qgemm.shard_columns(N, world, rank, 8)
+            bufs = [qgemm.Buffer.from_numpy(dev, s, a) for a in
+                    (A, np.ascontiguousarray(B[:, n0:n1]), sA, np.ascontiguousarray(sB[n0:n1]))]
+            out = qgemm.Buffer(dev, M * N * 2)
+            wb = L.lib().qgemm_w8a8_allgather_work_bytes(world, min(R, M), n1 - n0)
+            work = qgemm.Buffer(dev, wb)
+            args = [b.address for b in bufs]
+            L.call("qgemm_w8a8_gemm_allgather_bf16", comm, s.handle, cs.handle, args[0], args[1],
+                   qgemm.B_KN, args[2], args[3], out.address, M, n1 - n0, K, R, work.address, wb)
+            s.sync()
+            results.append(out.to_numpy(s, np.uint16, (M, N)))
+        # refusals, made identically on every rank before any collective
+        M, N, K, R = CASES[0]
+        st1 = L.try_call("qgemm_w8a8_gemm_allgather_bf16", comm, s.handle, s.handle, 16, 16,
+                         qgemm.B_KN, 16, 16, 16, M, N // world, K, R, 256, 1 << 20)
+        st2 = L.try_call("qgemm_w8a8_gemm_allgather_bf16", comm, s.handle, cs.handle, 16, 16,
+                         qgemm.B_KN, 16, 16, 16, M, N // world, K, R, 256, 64)
+        errors = [st1, st2]
+        q_out.put((rank, results, errors))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q_out.put((rank, None, repr(e)))
+    finally:
+        s.sync()
+        cs.sync()
+        L.call("qgemm_comm_destroy", comm)
+
+
+@pytest.mark.gpu
+def test_pipelined_gemm_allgather_matches_full(oracle):
+    import qgemm
+    import qgemm._lib as L
+    import qgemm.synthetic as syn
+    if qgemm.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q_id, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, q_id, q_out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q_out.get(timeout=240) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank, results, errors in res:
+        assert results is not None, f"rank {rank}: {errors}"
+        for (M, N, K, _), y in zip(CASES, results):
+            A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K)
+            yo, _ = oracle.w8a32_gemm(B, sB, A, sA)
+            np.testing.assert_array_equal(y, oracle.bf16_rne(yo))
+        assert errors == [L.ERR_INVALID_ARG, L.ERR_INVALID_ARG]
+    for p in procs:
+        assert p.exitcode == 0
+
+
+def test_allgather_work_bytes():
+    import qgemm._lib as L
+    assert L.lib().qgemm_w8a8_allgather_work_bytes(2, 64, 256) == 2 * 2 * 64 * 256 * 2
+    assert L.lib().qgemm_w8a8_allgather_work_bytes(0, 64, 256) == 0
