@@ -759,9 +759,10 @@ def w8a8_large(ops, st, rank, world, steps, warmup):
 def gather_output(st, out, rank, world, M, NL, gemm):
     """All-gather of the bf16 output slabs through libqgemm's NCCL communicator,
     then the [world][M][NL] -> [M][N] unshard kernel; timed separately.  Then the
-    whole sharded layer two ways: the GEMM, the gather and the unshard one after
-    the other on one stream, and qgemm_w8a8_gemm_allgather_bf16, which gathers
-    chunk i of M rows on a second stream while the GEMM of chunk i+1 runs."""
+    whole sharded layer three ways: the GEMM, the gather and the unshard one after
+    the other on one stream; qgemm_w8a8_gemm_allgather_bf16, which gathers chunk i
+    of M rows on a second stream while the GEMM of chunk i+1 runs; and its window
+    form, where copy-engine copies write each chunk into the peers' outputs."""
     import ctypes
     import torch
     import torch.distributed as dist
@@ -828,6 +829,28 @@ def gather_output(st, out, rank, world, M, NL, gemm):
             res[f"pipelined_ms_rows{R}"] = tp / reps * 1e3
             res[f"pipelined_equal_rows{R}"] = bool(torch.equal(full, ref))
             del work
+        # the window form: the copy engines write each finished chunk into the peers'
+        # registered output buffers, in the final layout
+        win = ctypes.c_void_p()
+        L.call("qgemm_comm_window_register", comm, st.handle, full.data_ptr(),
+               full.numel() * 2, ctypes.byref(win))
+        try:
+            for R in (4096, 2048, 1024):
+                def windowed(i):
+                    L.call("qgemm_w8a8_gemm_allgather_window_bf16", win, st.handle,
+                           q_side.handle, A.data_ptr(), B.data_ptr(), B_KN, sA.data_ptr(),
+                           sB.data_ptr(), M, NL, K, R)
+
+                full.zero_()
+                for i in range(2):
+                    windowed(i)
+                tw, _ = timed(windowed, reps, world)
+                res[f"window_ms_rows{R}"] = tw / reps * 1e3
+                res[f"window_equal_rows{R}"] = bool(torch.equal(full, ref))
+        finally:
+            torch.cuda.synchronize()
+            barrier(world)
+            L.call("qgemm_comm_window_release", win)
         q_side.destroy()
         return res
     finally:

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "internal.h"
 
@@ -25,7 +26,19 @@ struct qgemm_comm_s {
   int rank = 0, world = 1;
   // events of the pipelined GEMM + all-gather, made on its first call
   cudaEvent_t ev_gemm[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
-  cudaEvent_t ev_end = nullptr;
+  cudaEvent_t ev_end = nullptr, ev_start = nullptr;
+};
+
+// A buffer that every rank of a communicator registered together: this rank's
+// address, and every peer's buffer mapped into this process (CUDA IPC), so that
+// copies on this GPU's copy engines can write into the peers' buffers over NVLink.
+struct qgemm_window_s {
+  qgemm_comm_s* comm = nullptr;
+  uint64_t local = 0;
+  size_t bytes = 0;
+  std::vector<uint64_t> peer;  // peer[r]: rank r's buffer as mapped here (peer[rank] = local)
+  std::vector<void*> opened;   // allocation bases cudaIpcOpenMemHandle returned
+  void* sync = nullptr;        // bf16 [world]: the barrier gathers
 };
 
 namespace qg {
@@ -151,7 +164,8 @@ qgemm_status qgemm_comm_init(qgemm_device_t dev, const void* uid, int rank, int 
 
 qgemm_status qgemm_comm_destroy(qgemm_comm_t c) {
   if (!c) return fail(QGEMM_ERR_BAD_HANDLE, "null communicator");
-  for (cudaEvent_t e : {c->ev_gemm[0], c->ev_gemm[1], c->ev_done[0], c->ev_done[1], c->ev_end})
+  for (cudaEvent_t e : {c->ev_gemm[0], c->ev_gemm[1], c->ev_done[0], c->ev_done[1], c->ev_end,
+                        c->ev_start})
     if (e) cudaEventDestroy(e);
   NcclApi& n = nccl();
   ncclResult_t r = ncclSuccess;
@@ -184,6 +198,180 @@ qgemm_status qgemm_comm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, uint64_
     r = as;
   }
   if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+  return QGEMM_OK;
+}
+
+// One rank's part of qgemm_comm_window_register, gathered over NCCL.
+struct WindowRecord {
+  cudaIpcMemHandle_t handle;  // of the allocation that holds the buffer
+  uint64_t offset;            // buffer - allocation base
+  uint64_t bytes;
+  int32_t ok;                 // 0: this rank could not export its buffer
+  int32_t pad[5];
+};
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t is 64 bytes");
+static_assert(sizeof(WindowRecord) == 104, "WindowRecord layout");
+
+static qgemm_status window_barrier(qgemm_window_s* w, qgemm_stream_s* s) {
+  const int r = w->comm->rank;
+  return qgemm_comm_allgather_bf16(w->comm, s, reinterpret_cast<uint64_t>(w->sync) + 2 * r,
+                                   reinterpret_cast<uint64_t>(w->sync), 1);
+}
+
+qgemm_status qgemm_comm_window_register(qgemm_comm_t c, qgemm_stream_t s, uint64_t buf,
+                                        size_t bytes, qgemm_window_t* out) {
+  if (!out) return fail(QGEMM_ERR_INVALID_ARG, "out is null");
+  *out = nullptr;
+  if (!c || !c->comm) return fail(QGEMM_ERR_BAD_HANDLE, "null communicator");
+  qgemm_status st = enter(s);
+  if (st != QGEMM_OK) return st;
+  if (s->dev != c->dev) return fail(QGEMM_ERR_INVALID_ARG, "stream and communicator devices differ");
+  using GetRange = int (*)(uint64_t*, size_t*, uint64_t);  // cuMemGetAddressRange
+  static GetRange get_range = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) !=
+            cudaSuccess || q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<GetRange>(f);
+  }();
+  // Every rank takes part in the record gather even when its own export failed, so
+  // that all ranks reach the same verdict instead of some of them waiting.
+  WindowRecord mine;
+  memset(&mine, 0, sizeof(mine));
+  uint64_t base = 0;
+  size_t range = 0;
+  if (buf && bytes && aligned(buf, 16) && get_range && get_range(&base, &range, buf) == 0 &&
+      buf + bytes <= base + range &&
+      cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base)) == cudaSuccess) {
+    mine.offset = buf - base;
+    mine.bytes = bytes;
+    mine.ok = 1;
+  }
+  cudaGetLastError();
+  const int world = c->world;
+  const size_t rec = sizeof(WindowRecord);
+  void* d = nullptr;
+  cudaError_t ce = cudaMalloc(&d, rec * world + 2 * world);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMalloc");
+  std::vector<WindowRecord> all(world);
+  uint8_t* dm = static_cast<uint8_t*>(d);
+  ce = cudaMemcpyAsync(dm + rec * c->rank, &mine, rec, cudaMemcpyHostToDevice, s->stream);
+  if (ce != cudaSuccess) { cudaFree(d); return cuda_fail(ce, "cudaMemcpyAsync"); }
+  // rec is a multiple of 2 bytes: the records travel as bf16 elements
+  st = qgemm_comm_allgather_bf16(c, s, reinterpret_cast<uint64_t>(dm + rec * c->rank),
+                                 reinterpret_cast<uint64_t>(dm), rec / 2);
+  if (st != QGEMM_OK) { cudaFree(d); return st; }
+  ce = cudaMemcpyAsync(all.data(), dm, rec * world, cudaMemcpyDeviceToHost, s->stream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(s->stream);
+  if (ce != cudaSuccess) { cudaFree(d); return cuda_fail(ce, "gathering the window records"); }
+  for (int r = 0; r < world; ++r)
+    if (!all[r].ok || all[r].bytes != bytes) {
+      cudaFree(d);
+      return fail(QGEMM_ERR_INVALID_ARG,
+                  "rank %d registered no exportable buffer of %zu bytes (a 16-byte aligned "
+                  "cudaMalloc allocation, the same size on every rank)", r, bytes);
+    }
+  qgemm_window_s* w = new (std::nothrow) qgemm_window_s();
+  if (!w) { cudaFree(d); return fail(QGEMM_ERR_OOM, "host allocation failed"); }
+  w->comm = c;
+  w->local = buf;
+  w->bytes = bytes;
+  w->sync = dm + rec * world;
+  w->peer.assign(world, 0);
+  for (int r = 0; r < world; ++r) {
+    if (r == c->rank) { w->peer[r] = buf; continue; }
+    void* p = nullptr;
+    ce = cudaIpcOpenMemHandle(&p, all[r].handle, cudaIpcMemLazyEnablePeerAccess);
+    if (ce != cudaSuccess) {
+      qgemm_comm_window_release(w);
+      return cuda_fail(ce, "cudaIpcOpenMemHandle");
+    }
+    w->opened.push_back(p);
+    w->peer[r] = reinterpret_cast<uint64_t>(p) + all[r].offset;
+  }
+  *out = w;
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_comm_window_release(qgemm_window_t w) {
+  if (!w) return fail(QGEMM_ERR_BAD_HANDLE, "null window");
+  cudaError_t first = cudaSuccess;
+  if (w->comm && w->comm->dev) cudaSetDevice(w->comm->dev->ordinal);
+  for (void* p : w->opened) {
+    cudaError_t e = cudaIpcCloseMemHandle(p);
+    if (first == cudaSuccess) first = e;
+  }
+  // the barrier bytes sit at the end of the record block allocated with them
+  if (w->sync) {
+    uint8_t* base = static_cast<uint8_t*>(w->sync) - sizeof(WindowRecord) * w->peer.size();
+    cudaError_t e = cudaFree(base);
+    if (first == cudaSuccess) first = e;
+  }
+  delete w;
+  if (first != cudaSuccess) return cuda_fail(first, "releasing the window");
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_stream_t s,
+                                                   qgemm_stream_t cs, uint64_t A, uint64_t B,
+                                                   int b_layout, uint64_t sA, uint64_t sB, int M,
+                                                   int N_local, int K, int chunk_rows) {
+  if (!w || !w->comm || !w->comm->comm) return fail(QGEMM_ERR_BAD_HANDLE, "null window");
+  qgemm_comm_s* c = w->comm;
+  qgemm_status st = enter(cs);
+  if (st != QGEMM_OK) return st;
+  st = enter(s);
+  if (st != QGEMM_OK) return st;
+  if (s->dev != c->dev || cs->dev != c->dev)
+    return fail(QGEMM_ERR_INVALID_ARG, "streams and communicator are on different devices");
+  if (s == cs || s->stream == cs->stream)
+    return fail(QGEMM_ERR_INVALID_ARG, "the GEMM and the copies need two different streams");
+  if (M < 0 || N_local < 0 || K < 0 || chunk_rows < 1)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad sizes M=%d N_local=%d K=%d chunk_rows=%d", M,
+                N_local, K, chunk_rows);
+  const int world = c->world, rank = c->rank;
+  const size_t N = (size_t)N_local * world;
+  if ((size_t)M * N * 2 > w->bytes)
+    return fail(QGEMM_ERR_INVALID_ARG, "the window holds %zu bytes; [%d, %zu] bf16 needs %zu",
+                w->bytes, M, N, (size_t)M * N * 2);
+  if (M == 0 || N_local == 0) return QGEMM_OK;
+  for (cudaEvent_t* e : {&c->ev_gemm[0], &c->ev_gemm[1], &c->ev_end, &c->ev_start})
+    if (!*e) {
+      cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
+      if (ce != cudaSuccess) return cuda_fail(ce, "cudaEventCreate");
+    }
+  // every rank is done with its earlier uses of the buffer before a peer writes into it
+  cudaError_t ce = cudaEventRecord(c->ev_start, s->stream);
+  if (ce == cudaSuccess) ce = cudaStreamWaitEvent(cs->stream, c->ev_start, 0);
+  if (ce != cudaSuccess) return cuda_fail(ce, "ordering the copy stream after the caller's work");
+  if ((st = window_barrier(w, cs)) != QGEMM_OK) return st;
+  const int R = chunk_rows < M ? chunk_rows : M;
+  const size_t pitch = N * 2, width = (size_t)N_local * 2;
+  for (int m0 = 0, i = 0; m0 < M; m0 += R, ++i) {
+    const int rows = (M - m0) < R ? (M - m0) : R;
+    const size_t off = (size_t)m0 * pitch + (size_t)rank * width;  // this rank's columns
+    st = qgemm_w8a8_gemm(s, A + (uint64_t)m0 * K, B, b_layout, sA + (uint64_t)m0 * 4, sB,
+                         w->local + off, QGEMM_BF16, (int)N, rows, N_local, K, 0,
+                         QGEMM_ALGO_AUTO);
+    if (st != QGEMM_OK) return st;
+    cudaEvent_t ev = c->ev_gemm[i & 1];
+    if ((ce = cudaEventRecord(ev, s->stream)) != cudaSuccess ||
+        (ce = cudaStreamWaitEvent(cs->stream, ev, 0)) != cudaSuccess)
+      return cuda_fail(ce, "event between the GEMM and the copies");
+    for (int j = 1; j < world; ++j) {  // peers in rank order from this rank's right
+      const int p = (rank + j) % world;
+      ce = cudaMemcpy2DAsync(reinterpret_cast<void*>(w->peer[p] + off), pitch,
+                             reinterpret_cast<const void*>(w->local + off), pitch, width, rows,
+                             cudaMemcpyDeviceToDevice, cs->stream);
+      if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemcpy2DAsync to a peer");
+    }
+  }
+  // every peer's columns have landed here once every rank has finished its copies
+  if ((st = window_barrier(w, cs)) != QGEMM_OK) return st;
+  ce = cudaEventRecord(c->ev_end, cs->stream);
+  if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s->stream, c->ev_end, 0);
+  if (ce != cudaSuccess) return cuda_fail(ce, "joining the copy stream");
   return QGEMM_OK;
 }
 

@@ -121,6 +121,10 @@ SIGNATURES = {
     "qgemm_w8a8_allgather_work_bytes": (_SZ, [_I, _I, _I]),
     "qgemm_w8a8_gemm_allgather_bf16": (_S, [_P, _P, _P, _U64, _U64, _I, _U64, _U64, _U64, _I, _I,
                                             _I, _I, _U64, _SZ]),
+    "qgemm_comm_window_register": (_S, [_P, _P, _U64, _SZ, ctypes.POINTER(_P)]),
+    "qgemm_comm_window_release": (_S, [_P]),
+    "qgemm_w8a8_gemm_allgather_window_bf16": (_S, [_P, _P, _P, _U64, _U64, _I, _U64, _U64, _I,
+                                                   _I, _I, _I]),
 }
 
 _lib = None

@@ -80,6 +80,7 @@ enum {
 typedef struct qgemm_device_s* qgemm_device_t;
 typedef struct qgemm_stream_s* qgemm_stream_t;
 typedef struct qgemm_comm_s* qgemm_comm_t;
+typedef struct qgemm_window_s* qgemm_window_t;
 
 /* ---- errors ----------------------------------------------------------------
  * Replaces the reference's swallowed exceptions (runtime/CUDARuntime.scala:216,
@@ -414,6 +415,33 @@ QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t comm, qgemm_s
                                                       uint64_t out, int M, int N_local, int K,
                                                       int chunk_rows, uint64_t work,
                                                       size_t work_bytes);
+
+/* A buffer registered by every rank of `comm` together (collective; every rank passes
+ * its own buffer of the same size): `buf` must lie in one cudaMalloc allocation and be
+ * 16-byte aligned.  Each rank maps the peers' buffers into its own address space (CUDA
+ * IPC), so one process per GPU; one window per allocation at a time.  `s` carries the
+ * exchange and is synchronised.  Release a window (a local call) after the work that
+ * uses it has finished on every rank and before qgemm_comm_destroy. */
+QGEMM_API qgemm_status qgemm_comm_window_register(qgemm_comm_t comm, qgemm_stream_t s,
+                                                  uint64_t buf, size_t bytes,
+                                                  qgemm_window_t* out);
+QGEMM_API qgemm_status qgemm_comm_window_release(qgemm_window_t w);
+
+/* The same sharded GEMM + all-gather into a registered window, [M, N_local * world]
+ * bf16 on every rank.  The GEMM of each chunk of `chunk_rows` rows writes this rank's
+ * columns of the window in place (ldc = N_local * world) on stream s; the copy engines
+ * then write those columns into every peer's window over NVLink on stream cs while
+ * the GEMM of the next chunk runs.  No gather buffer and no unshard pass: the copies
+ * land in the final layout.  Two barriers on cs (one-element NCCL gathers) bracket
+ * the copies: no rank writes into a peer's window before the peer has finished its
+ * earlier work on s, and the call completes on s only when every peer's columns have
+ * arrived.  Every rank must make the same calls in the same order. */
+QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_stream_t s,
+                                                             qgemm_stream_t cs, uint64_t A,
+                                                             uint64_t B, int b_layout,
+                                                             uint64_t sA, uint64_t sB, int M,
+                                                             int N_local, int K,
+                                                             int chunk_rows);
 
 #ifdef __cplusplus
 }

@@ -2,8 +2,10 @@
 
 qgemm_w8a8_gemm_allgather_bf16 runs each rank's GEMM slice chunk by chunk of M and
 all-gathers every chunk over NCCL while the next chunk's GEMM runs (NCCLOps.scala:302-320
-is the reference's all-gather).  Every rank must end with the whole [M, N] output,
-bit for bit the unsharded product from the oracle.  Skipped with fewer than two GPUs.
+is the reference's all-gather); qgemm_w8a8_gemm_allgather_window_bf16 instead copies each
+chunk into the peers' registered output windows.  Every rank must end with the whole
+[M, N] output, bit for bit the unsharded product from the oracle.  Skipped with fewer
+than two GPUs.
 """
 import os
 import sys
@@ -52,7 +54,22 @@ def _rank_main(rank, world, q_id, q_out):
             L.call("qgemm_w8a8_gemm_allgather_bf16", comm, s.handle, cs.handle, args[0], args[1],
                    qgemm.B_KN, args[2], args[3], out.address, M, n1 - n0, K, R, work.address, wb)
             s.sync()
-            results.append(out.to_numpy(s, np.uint16, (M, N)))
+            y = out.to_numpy(s, np.uint16, (M, N))
+            # the registered-window form, twice into the same window
+            win_buf = qgemm.Buffer(dev, M * N * 2)
+            s.memset(win_buf.address, 0, M * N * 2)
+            win = ctypes.c_void_p()
+            L.call("qgemm_comm_window_register", comm, s.handle, win_buf.address, M * N * 2,
+                   ctypes.byref(win))
+            ys = []
+            for _ in range(2):
+                L.call("qgemm_w8a8_gemm_allgather_window_bf16", win, s.handle, cs.handle,
+                       args[0], args[1], qgemm.B_KN, args[2], args[3], M, n1 - n0, K, R)
+                ys.append(win_buf.to_numpy(s, np.uint16, (M, N)))
+            s.sync()
+            cs.sync()
+            L.call("qgemm_comm_window_release", win)
+            results.append((y, ys[0], ys[1]))
         # refusals, made identically on every rank before any collective
         M, N, K, R = CASES[0]
         st1 = L.try_call("qgemm_w8a8_gemm_allgather_bf16", comm, s.handle, s.handle, 16, 16,
@@ -91,10 +108,11 @@ def test_pipelined_gemm_allgather_matches_full(oracle):
                 p.kill()
     for rank, results, errors in res:
         assert results is not None, f"rank {rank}: {errors}"
-        for (M, N, K, _), y in zip(CASES, results):
+        for (M, N, K, _), ys in zip(CASES, results):
             A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K)
             yo, _ = oracle.w8a32_gemm(B, sB, A, sA)
-            np.testing.assert_array_equal(y, oracle.bf16_rne(yo))
+            for y in ys:  # gather buffers, then the window (twice)
+                np.testing.assert_array_equal(y, oracle.bf16_rne(yo))
         assert errors == [L.ERR_INVALID_ARG, L.ERR_INVALID_ARG]
     for p in procs:
         assert p.exitcode == 0
