@@ -832,8 +832,13 @@ def gather_output(st, out, rank, world, M, NL, gemm):
         # the window form: the copy engines write each finished chunk into the peers'
         # registered output buffers, in the final layout
         win = ctypes.c_void_p()
-        L.call("qgemm_comm_window_register", comm, st.handle, full.data_ptr(),
-               full.numel() * 2, ctypes.byref(win))
+        try:  # a refusal here is the same on every rank (the records are gathered first)
+            L.call("qgemm_comm_window_register", comm, st.handle, full.data_ptr(),
+                   full.numel() * 2, ctypes.byref(win))
+        except L.QGemmError as e:
+            res["window_error"] = str(e)
+            q_side.destroy()
+            return res
         try:
             for R in (4096, 2048, 1024):
                 def windowed(i):
