@@ -840,18 +840,23 @@ def gather_output(st, out, rank, world, M, NL, gemm):
             q_side.destroy()
             return res
         try:
-            for R in (4096, 2048, 1024):
+            # the peer copies on one stream (the default), then on one stream per peer
+            for R, ncp in ((4096, None), (2048, None), (1024, None), (4096, world - 1)):
                 def windowed(i):
                     L.call("qgemm_w8a8_gemm_allgather_window_bf16", win, st.handle,
                            q_side.handle, A.data_ptr(), B.data_ptr(), B_KN, sA.data_ptr(),
                            sB.data_ptr(), M, NL, K, R)
 
+                if ncp:
+                    os.environ["QGEMM_COPY_STREAMS"] = str(ncp)
                 full.zero_()
                 for i in range(2):
                     windowed(i)
                 tw, _ = timed(windowed, reps, world)
-                res[f"window_ms_rows{R}"] = tw / reps * 1e3
-                res[f"window_equal_rows{R}"] = bool(torch.equal(full, ref))
+                os.environ.pop("QGEMM_COPY_STREAMS", None)
+                tag = f"rows{R}" + (f"_copy_streams{ncp}" if ncp else "")
+                res[f"window_ms_{tag}"] = tw / reps * 1e3
+                res[f"window_equal_{tag}"] = bool(torch.equal(full, ref))
         finally:
             torch.cuda.synchronize()
             barrier(world)

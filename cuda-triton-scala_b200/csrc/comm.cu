@@ -26,7 +26,10 @@ struct qgemm_comm_s {
   int rank = 0, world = 1;
   // events of the pipelined GEMM + all-gather, made on its first call
   cudaEvent_t ev_gemm[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
-  cudaEvent_t ev_end = nullptr, ev_start = nullptr;
+  cudaEvent_t ev_end = nullptr, ev_start = nullptr, ev_open = nullptr;
+  // the window copies' streams, one per peer at most, and an event on each
+  std::vector<cudaStream_t> cp;
+  std::vector<cudaEvent_t> ev_cp;
 };
 
 // A buffer that every rank of a communicator registered together: this rank's
@@ -164,9 +167,12 @@ qgemm_status qgemm_comm_init(qgemm_device_t dev, const void* uid, int rank, int 
 
 qgemm_status qgemm_comm_destroy(qgemm_comm_t c) {
   if (!c) return fail(QGEMM_ERR_BAD_HANDLE, "null communicator");
+  if (c->dev) cudaSetDevice(c->dev->ordinal);
   for (cudaEvent_t e : {c->ev_gemm[0], c->ev_gemm[1], c->ev_done[0], c->ev_done[1], c->ev_end,
-                        c->ev_start})
+                        c->ev_start, c->ev_open})
     if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : c->ev_cp) cudaEventDestroy(e);
+  for (cudaStream_t x : c->cp) cudaStreamDestroy(x);
   NcclApi& n = nccl();
   ncclResult_t r = ncclSuccess;
   if (c->comm && n.CommDestroy) r = n.CommDestroy(c->comm);
@@ -211,6 +217,18 @@ struct WindowRecord {
 };
 static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t is 64 bytes");
 static_assert(sizeof(WindowRecord) == 104, "WindowRecord layout");
+
+// Streams that carry the window copies: QGEMM_COPY_STREAMS (1 .. world-1), by
+// default 1.  Copies to different peers side by side on 3 streams measured slower at
+// 4 ranks (layer 2.03 ms against 1.38 ms with one stream).
+static int copy_streams(int world) {
+  int n = 1;
+  if (const char* e = getenv("QGEMM_COPY_STREAMS")) {
+    const int v = atoi(e);
+    if (v > 0) n = v;
+  }
+  return n < 1 ? 1 : n > world - 1 ? world - 1 : n;
+}
 
 static qgemm_status window_barrier(qgemm_window_s* w, qgemm_stream_s* s) {
   const int r = w->comm->rank;
@@ -336,16 +354,31 @@ qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_strea
     return fail(QGEMM_ERR_INVALID_ARG, "the window holds %zu bytes; [%d, %zu] bf16 needs %zu",
                 w->bytes, M, N, (size_t)M * N * 2);
   if (M == 0 || N_local == 0) return QGEMM_OK;
-  for (cudaEvent_t* e : {&c->ev_gemm[0], &c->ev_gemm[1], &c->ev_end, &c->ev_start})
+  for (cudaEvent_t* e : {&c->ev_gemm[0], &c->ev_gemm[1], &c->ev_end, &c->ev_start, &c->ev_open})
     if (!*e) {
       cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
       if (ce != cudaSuccess) return cuda_fail(ce, "cudaEventCreate");
     }
+  const int ncp = copy_streams(world);
+  while ((int)c->cp.size() < ncp) {
+    cudaStream_t x = nullptr;
+    cudaEvent_t e = nullptr;
+    cudaError_t ce = cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamCreate");
+    ce = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    if (ce != cudaSuccess) { cudaStreamDestroy(x); return cuda_fail(ce, "cudaEventCreate"); }
+    c->cp.push_back(x);
+    c->ev_cp.push_back(e);
+  }
   // every rank is done with its earlier uses of the buffer before a peer writes into it
   cudaError_t ce = cudaEventRecord(c->ev_start, s->stream);
   if (ce == cudaSuccess) ce = cudaStreamWaitEvent(cs->stream, c->ev_start, 0);
   if (ce != cudaSuccess) return cuda_fail(ce, "ordering the copy stream after the caller's work");
   if ((st = window_barrier(w, cs)) != QGEMM_OK) return st;
+  ce = cudaEventRecord(c->ev_open, cs->stream);
+  for (int k = 0; k < ncp && ce == cudaSuccess; ++k)
+    ce = cudaStreamWaitEvent(c->cp[k], c->ev_open, 0);
+  if (ce != cudaSuccess) return cuda_fail(ce, "ordering the copies after the barrier");
   const int R = chunk_rows < M ? chunk_rows : M;
   const size_t pitch = N * 2, width = (size_t)N_local * 2;
   for (int m0 = 0, i = 0; m0 < M; m0 += R, ++i) {
@@ -356,17 +389,23 @@ qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_strea
                          QGEMM_ALGO_AUTO);
     if (st != QGEMM_OK) return st;
     cudaEvent_t ev = c->ev_gemm[i & 1];
-    if ((ce = cudaEventRecord(ev, s->stream)) != cudaSuccess ||
-        (ce = cudaStreamWaitEvent(cs->stream, ev, 0)) != cudaSuccess)
-      return cuda_fail(ce, "event between the GEMM and the copies");
+    if ((ce = cudaEventRecord(ev, s->stream)) != cudaSuccess)
+      return cuda_fail(ce, "cudaEventRecord");
+    for (int k = 0; k < ncp; ++k)
+      if ((ce = cudaStreamWaitEvent(c->cp[k], ev, 0)) != cudaSuccess)
+        return cuda_fail(ce, "event between the GEMM and the copies");
     for (int j = 1; j < world; ++j) {  // peers in rank order from this rank's right
       const int p = (rank + j) % world;
       ce = cudaMemcpy2DAsync(reinterpret_cast<void*>(w->peer[p] + off), pitch,
                              reinterpret_cast<const void*>(w->local + off), pitch, width, rows,
-                             cudaMemcpyDeviceToDevice, cs->stream);
+                             cudaMemcpyDeviceToDevice, c->cp[(j - 1) % ncp]);
       if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemcpy2DAsync to a peer");
     }
   }
+  for (int k = 0; k < ncp; ++k)
+    if ((ce = cudaEventRecord(c->ev_cp[k], c->cp[k])) != cudaSuccess ||
+        (ce = cudaStreamWaitEvent(cs->stream, c->ev_cp[k], 0)) != cudaSuccess)
+      return cuda_fail(ce, "joining the copy streams");
   // every peer's columns have landed here once every rank has finished its copies
   if ((st = window_barrier(w, cs)) != QGEMM_OK) return st;
   ce = cudaEventRecord(c->ev_end, cs->stream);

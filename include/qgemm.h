@@ -430,8 +430,9 @@ QGEMM_API qgemm_status qgemm_comm_window_release(qgemm_window_t w);
 /* The same sharded GEMM + all-gather into a registered window, [M, N_local * world]
  * bf16 on every rank.  The GEMM of each chunk of `chunk_rows` rows writes this rank's
  * columns of the window in place (ldc = N_local * world) on stream s; the copy engines
- * then write those columns into every peer's window over NVLink on stream cs while
- * the GEMM of the next chunk runs.  No gather buffer and no unshard pass: the copies
+ * then write those columns into every peer's window over NVLink while the GEMM of the
+ * next chunk runs, on a stream the communicator owns (or on as many as the environment
+ * variable QGEMM_COPY_STREAMS says, 1 .. world-1, one peer's copies on each).  No gather buffer and no unshard pass: the copies
  * land in the final layout.  Two barriers on cs (one-element NCCL gathers) bracket
  * the copies: no rank writes into a peer's window before the peer has finished its
  * earlier work on s, and the call completes on s only when every peer's columns have
