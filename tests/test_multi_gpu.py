@@ -122,3 +122,76 @@ def test_allgather_work_bytes():
     import qgemm._lib as L
     assert L.lib().qgemm_w8a8_allgather_work_bytes(2, 64, 256) == 2 * 2 * 64 * 256 * 2
     assert L.lib().qgemm_w8a8_allgather_work_bytes(0, 64, 256) == 0
+
+
+def _rank_main_facade(rank, world, q_id, q_out):
+    """One case through qgemm.NCCLCommunicator / OutputWindow instead of raw calls."""
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "cuda-triton-scala_b200")]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import qgemm
+    import qgemm.synthetic as syn
+    from qgemm import NCCLCommunicator
+    dev = qgemm.Device(rank)
+    s, cs = dev.stream(), dev.stream()
+    if rank == 0:
+        uid = NCCLCommunicator.unique_id()
+        for _ in range(world - 1):
+            q_id.put(uid)
+    else:
+        uid = q_id.get(timeout=60)
+    comm = NCCLCommunicator(dev, rank, world, uid)
+    try:
+        M, N, K, R = CASES[0]
+        A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K)
+        n0, n1 = qgemm.shard_columns(N, world, rank, 8)
+        bufs = [qgemm.Buffer.from_numpy(dev, s, a) for a in
+                (A, np.ascontiguousarray(B[:, n0:n1]), sA, np.ascontiguousarray(sB[n0:n1]))]
+        out = qgemm.Buffer(dev, M * N * 2)
+        wb = NCCLCommunicator.gemmAllGatherWorkBytes(world, R, n1 - n0)
+        work = qgemm.Buffer(dev, wb)
+        comm.w8a8GemmAllGather(s, cs, *bufs, out, M, n1 - n0, K, R, work, wb)
+        y = out.to_numpy(s, np.uint16, (M, N))
+        win_buf = qgemm.Buffer(dev, M * N * 2)
+        win = comm.registerWindow(s, win_buf, M * N * 2)
+        win.w8a8GemmAllGather(s, cs, *bufs, M, n1 - n0, K, R)
+        yw = win_buf.to_numpy(s, np.uint16, (M, N))
+        cs.sync()
+        win.release()
+        q_out.put((rank, [(y, yw)], []))
+    except Exception as e:
+        q_out.put((rank, None, repr(e)))
+    finally:
+        s.sync()
+        cs.sync()
+        comm.destroy()
+
+
+@pytest.mark.gpu
+def test_communicator_facade_matches_full(oracle):
+    import qgemm
+    import qgemm.synthetic as syn
+    if qgemm.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q_id, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank_main_facade, args=(r, world, q_id, q_out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q_out.get(timeout=240) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    M, N, K, _ = CASES[0]
+    A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K)
+    yo, _ = oracle.w8a32_gemm(B, sB, A, sA)
+    for rank, results, err in res:
+        assert results is not None, f"rank {rank}: {err}"
+        for y in results[0]:
+            np.testing.assert_array_equal(y, oracle.bf16_rne(yo))
+    for p in procs:
+        assert p.exitcode == 0
