@@ -17,6 +17,11 @@ struct qgemm_device_s {
   size_t smem_optin = 0;
   bool tcgen05 = false;       // sm_100 family: tcgen05 / TMEM / TMA kernels run
   int* d_err = nullptr;       // device error word written by bounded waits
+  // Limit of every bounded wait in the tcgen05 GEMM kernels launched on this device
+  // (qgemm_device_set_wait_limit), and the split hold-back test hook
+  // (qgemm_debug_hold_split).
+  unsigned long long wait_ns = 2000000000ull;
+  int hold_split = 0;
   std::mutex mu;
   bool open = false;
 };
@@ -78,7 +83,13 @@ struct TcArgs {
   uint64_t a_pitch = 0, b_pitch = 0;  // row pitch in bytes, also the rows' extent (0: K)
   const float* sA = nullptr;          // KIND_I8: y = (float(acc) * sB[n]) * sA[m]
   const float* sB = nullptr;
-  int32_t* acc = nullptr;             // KIND_I8: optional int32 accumulators [M, N]
+  int32_t* acc = nullptr;             // KIND_I8: optional int32 accumulators [M, acc_ld]
+  int acc_ld = 0;                     // row pitch of acc in elements (0: N)
+  const int32_t* acc_c = nullptr;     // optional int32 addend of acc, [M, acc_c_ld]
+  int acc_c_ld = 0;
+  int no_out = 0;                     // 1: acc is the only output (out, sA, sB unused)
+  uint64_t a_extent = 0;              // bytes of each A row that exist (0: a_pitch)
+  uint64_t b_kn_pitch = 0;            // b_kn: row pitch of B [K, N] in bytes (0: N)
   void* out = nullptr;
   int out_dtype = QGEMM_F32;
   int ldc = 0;

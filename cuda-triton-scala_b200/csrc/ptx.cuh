@@ -72,28 +72,30 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 
 // Bounded wait that sleeps between polls (for warps that have nothing else to do).
 __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity,
-                                                const volatile int* abort) {
+                                                const volatile int* abort,
+                                                unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 10000u)) return true;
     if (abort && *abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
 
 // Waits for the phase with the given parity to complete.  Returns false when
-// the wait runs past kWaitLimitNs or when *abort (shared memory) becomes
-// non-zero, so that no wait can spin forever.
+// the wait runs past limit_ns or when *abort (shared memory) becomes non-zero,
+// so that no wait can spin forever.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          const volatile int* abort) {
+                                          const volatile int* abort,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (abort && *abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (globaltimer() - t0 > limit_ns) return false;
     }
   }
 }

@@ -190,6 +190,28 @@ qgemm_status qgemm_device_info(qgemm_device_t d, int* sm_count, int* cc_major, i
   return QGEMM_OK;
 }
 
+qgemm_status qgemm_device_set_wait_limit(qgemm_device_t d, uint64_t limit_ns) {
+  if (!d || !d->open) return fail(QGEMM_ERR_BAD_HANDLE, "null or closed device");
+  if (limit_ns < 1000 || limit_ns > 60000000000ull)
+    return fail(QGEMM_ERR_INVALID_ARG, "wait limit %llu ns outside [1 us, 60 s]",
+                (unsigned long long)limit_ns);
+  d->wait_ns = limit_ns;
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_device_get_wait_limit(qgemm_device_t d, uint64_t* limit_ns) {
+  if (!d || !d->open) return fail(QGEMM_ERR_BAD_HANDLE, "null or closed device");
+  if (!limit_ns) return fail(QGEMM_ERR_INVALID_ARG, "limit_ns is null");
+  *limit_ns = d->wait_ns;
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_debug_hold_split(qgemm_device_t d, int enable) {
+  if (!d || !d->open) return fail(QGEMM_ERR_BAD_HANDLE, "null or closed device");
+  d->hold_split = enable ? 1 : 0;
+  return QGEMM_OK;
+}
+
 // ---- streams ----
 
 qgemm_status qgemm_stream_create(qgemm_device_t d, qgemm_stream_t* out) {
@@ -815,7 +837,153 @@ qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name, const uint
     QG_TRY(want(3, 2));
     return qgemm_gemv_f32(s, b[0], b[1], b[2], v[0], v[1]);
   }
+  if (!strcmp(name, "tensorCoreGemmInt8")) {
+    QG_TRY(want(6, 8));
+    return qgemm_tensor_core_gemm_int8(s, b[0], b[1], b[2], b[3], b[4], b[5], v[0], v[1], v[2],
+                                       v[3], v[4], v[5], v[6], v[7]);
+  }
   return fail(QGEMM_ERR_INVALID_ARG, "unknown kernel name '%s'", name);
+}
+
+// ---- the Java bridge's by-name form ----
+//
+// One row per reference method: its Ptr parameters in declaration order, which of them
+// the bridge's bufferAddrs(0) names (the result buffer), and its scalar parameters in
+// declaration order with their types (i: Int, b: Bool, f: Float).  Scalars left out of
+// scalarKeys take the default in `defaults` (NaN: no default).
+
+namespace {
+
+struct BridgeOp {
+  const char* name;
+  const char* ptrs[8];
+  int nptrs;
+  int out;                 // index into ptrs of bufferAddrs(0)
+  const char* scalars[16];
+  const char* types;       // one letter per scalar
+  float defaults[16];
+};
+
+constexpr float NO_DEFAULT = __builtin_nanf("");
+
+const BridgeOp kBridgeOps[] = {
+    {"w8a32Gemm", {"wInt8", "scalesW", "x", "scalesX", "y"}, 5, 4, {"M", "N", "K"}, "iii",
+     {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT}},
+    {"w4a16Gemm", {"wInt4", "scalesW", "x", "y"}, 4, 3, {"M", "N", "K"}, "iii",
+     {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT}},
+    {"w8a16Gemm", {"wInt8", "scalesW", "x", "bias", "y"}, 5, 4, {"M", "N", "K", "hasBias"},
+     "iiib", {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT}},
+    {"w8a16GemmRowWise", {"wInt8", "scalesW", "x", "y"}, 4, 3, {"M", "N", "K"}, "iii",
+     {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT}},
+    {"dynamicQuantize", {"weight", "scales", "qWeight"}, 3, 2, {"K", "N", "qBits"}, "iii",
+     {NO_DEFAULT, NO_DEFAULT, 8.f}},
+    {"weightOnlyQuantizePerChannel", {"weight", "scales", "qWeight", "zeros"}, 4, 2, {"K", "N"},
+     "ii", {NO_DEFAULT, NO_DEFAULT}},
+    {"dequantize", {"qWeight", "scales", "weight"}, 3, 2, {"K", "N"}, "ii",
+     {NO_DEFAULT, NO_DEFAULT}},
+    {"matmul", {"A", "B", "C"}, 3, 2, {"M", "N", "K"}, "iii", {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT}},
+    {"matmulAddBias", {"A", "B", "bias", "C"}, 4, 3, {"M", "N", "K"}, "iii",
+     {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT}},
+    {"sgemm", {"A", "B", "C"}, 3, 2, {"M", "N", "K", "alpha", "beta"}, "iiiff",
+     {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT}},
+    {"gemv", {"A", "x", "y"}, 3, 2, {"M", "N"}, "ii", {NO_DEFAULT, NO_DEFAULT}},
+    {"tensorCoreGemmInt8", {"a", "b", "scalesA", "scalesB", "c", "d"}, 6, 5,
+     {"M", "N", "K", "lda", "ldb", "ldc", "ldd", "hasC"}, "iiiiiiib",
+     {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT,
+      NO_DEFAULT}},
+    {"int8GemmKernel", {"D", "A", "B"}, 3, 0,
+     {"M", "N", "K", "lda", "ldb", "ldd", "scaleA", "scaleB"}, "iiiiiiff",
+     {NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT, NO_DEFAULT,
+      NO_DEFAULT}},
+};
+
+// An Int passed as a Float must be integral and exactly representable (|v| <= 2^24).
+bool float_to_int(float f, int* out) {
+  if (!(f == f) || f < -16777216.f || f > 16777216.f) return false;
+  const int v = (int)f;
+  if ((float)v != f) return false;
+  *out = v;
+  return true;
+}
+
+}  // namespace
+
+int64_t qgemm_bridge_launch_kernel(qgemm_stream_t s, const char* name, int gridX, int gridY,
+                                   int gridZ, int blockX, int blockY, int blockZ,
+                                   const uint64_t* bufferAddrs, int nbufs,
+                                   const float* scalarVals, const char* const* scalarKeys,
+                                   int nscalars) {
+  (void)gridX; (void)gridY; (void)gridZ; (void)blockX; (void)blockY; (void)blockZ;
+  if (!name) { fail(QGEMM_ERR_INVALID_ARG, "name is null"); return -1; }
+  const BridgeOp* op = nullptr;
+  for (const BridgeOp& o : kBridgeOps)
+    if (!strcmp(o.name, name)) op = &o;
+  if (!op) { fail(QGEMM_ERR_INVALID_ARG, "unknown kernel name '%s'", name); return -1; }
+  if (nbufs != op->nptrs || !bufferAddrs) {
+    fail(QGEMM_ERR_INVALID_ARG, "%s takes %d buffers (got %d)", name, op->nptrs, nbufs);
+    return -1;
+  }
+  const int nsc = (int)strlen(op->types);
+  if (nscalars < 0 || nscalars > nsc || (nscalars > 0 && !scalarVals)) {
+    fail(QGEMM_ERR_INVALID_ARG, "%s takes up to %d scalars (got %d)", name, nsc, nscalars);
+    return -1;
+  }
+  // Buffers: bufferAddrs(0) is the result buffer, the rest follow in declaration order.
+  uint64_t b[8] = {};
+  b[op->out] = bufferAddrs[0];
+  for (int i = 0, j = 1; i < op->nptrs; ++i)
+    if (i != op->out) b[i] = bufferAddrs[j++];
+  // Scalars: by key when keys are given, else by position.
+  float sv[16];
+  bool set[16] = {};
+  for (int i = 0; i < nscalars; ++i) {
+    int slot = i;
+    if (scalarKeys) {
+      slot = -1;
+      if (!scalarKeys[i]) { fail(QGEMM_ERR_INVALID_ARG, "scalar key %d is null", i); return -1; }
+      for (int k = 0; k < nsc; ++k)
+        if (!strcmp(scalarKeys[i], op->scalars[k])) slot = k;
+      if (slot < 0) {
+        fail(QGEMM_ERR_INVALID_ARG, "%s has no scalar '%s'", name, scalarKeys[i]);
+        return -1;
+      }
+      if (set[slot]) {
+        fail(QGEMM_ERR_INVALID_ARG, "scalar '%s' given twice", scalarKeys[i]);
+        return -1;
+      }
+    }
+    sv[slot] = scalarVals[i];
+    set[slot] = true;
+  }
+  int iv[16] = {};
+  float fv[16] = {};
+  for (int k = 0; k < nsc; ++k) {
+    if (!set[k]) {
+      if (op->defaults[k] != op->defaults[k]) {
+        fail(QGEMM_ERR_INVALID_ARG, "%s: scalar '%s' missing", name, op->scalars[k]);
+        return -1;
+      }
+      sv[k] = op->defaults[k];
+    }
+    if (op->types[k] == 'f') {
+      fv[k] = sv[k];
+    } else if (!float_to_int(sv[k], &iv[k]) ||
+               (op->types[k] == 'b' && iv[k] != 0 && iv[k] != 1)) {
+      fail(QGEMM_ERR_INVALID_ARG, "%s: scalar '%s' = %g is not a%s", name, op->scalars[k],
+           (double)sv[k], op->types[k] == 'b' ? " Bool (0 or 1)" : "n exact Int");
+      return -1;
+    }
+  }
+  qgemm_status st;
+  if (!strcmp(name, "sgemm")) {
+    st = qgemm_sgemm(s, b[0], b[1], b[2], iv[0], iv[1], iv[2], fv[3], fv[4]);
+  } else if (!strcmp(name, "int8GemmKernel")) {
+    st = qgemm_int8_gemm_kernel(s, b[0], b[1], b[2], iv[0], iv[1], iv[2], iv[3], iv[4], iv[5],
+                                fv[6], fv[7]);
+  } else {
+    st = qgemm_launch_by_name(s, name, b, op->nptrs, iv, nsc);
+  }
+  return st == QGEMM_OK ? (int64_t)bufferAddrs[0] : -1;
 }
 
 // ---- sharding ----

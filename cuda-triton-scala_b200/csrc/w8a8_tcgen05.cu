@@ -103,6 +103,17 @@ struct Params {
   int split_w, split_s;
   int32_t* part;   // [(tail tile * 2 + rank) * split_s + part][128 x 256 words, part_index]
   int* cnt;        // [tail tile * 2 + rank], zero between launches
+  // int32 accumulator output: row pitch acc_ld (elements); when acc_c is set, c[m, n]
+  // (row pitch acc_c_ld) is added to each sum before it is stored (int32, wrapping).
+  int acc_ld;
+  const int32_t* acc_c;
+  int acc_c_ld;
+  int no_out;      // 1: the int32 accumulators are the only output (no scales, no out)
+  // Every bounded wait of the kernel gives up after wait_ns of %globaltimer.
+  unsigned long long wait_ns;
+  // Test hook: the final K part of a split tile waits for one count-in more than the
+  // other parts make, so that its bounded wait runs out (the timeout path).
+  int hold_split;
 };
 
 // Work item i of pair `pair`: a whole tile, or one K part of a tail tile.  Returns
@@ -190,11 +201,37 @@ __device__ __forceinline__ void report_pair(int* err, int code, volatile int* ab
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer), "r"(1) : "memory");
 }
 
+// The int32 accumulators of 32 consecutive columns of one row (row < M, n0 < N), plus
+// the addend c when there is one.
+__device__ __forceinline__ void store_acc(const Params& p, int row, int n0, bool full,
+                                          const uint32_t (&r)[32]) {
+  int32_t* dst = p.acc + (size_t)row * p.acc_ld + n0;
+  const int32_t* c = p.acc_c ? p.acc_c + (size_t)row * p.acc_c_ld + n0 : nullptr;
+  if (full && p.acc_vec) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      int4 v = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+      if (c) {
+        v.x = (int)((uint32_t)v.x + (uint32_t)__ldg(c + j));
+        v.y = (int)((uint32_t)v.y + (uint32_t)__ldg(c + j + 1));
+        v.z = (int)((uint32_t)v.z + (uint32_t)__ldg(c + j + 2));
+        v.w = (int)((uint32_t)v.w + (uint32_t)__ldg(c + j + 3));
+      }
+      *reinterpret_cast<int4*>(dst + j) = v;
+    }
+  } else {
+    for (int j = 0; j < 32 && n0 + j < p.N; ++j)
+      dst[j] = (int)(r[j] + (c ? (uint32_t)__ldg(c + j) : 0u));
+  }
+}
+
 // Epilogue for 32 consecutive columns of one row.
 __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, float sa,
                                             const uint32_t (&r)[32]) {
   if (row >= p.M || n0 >= p.N) return;
   const bool full = (n0 + 32 <= p.N);
+  if (p.acc) store_acc(p, row, n0, full, r);
+  if (p.no_out) return;
   float sb[32];
   if (p.fp_acc) {
 #pragma unroll
@@ -208,17 +245,6 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j) sb[j] = (n0 + j < p.N) ? __ldg(p.sB + n0 + j) : 0.f;
-  }
-  if (p.acc) {
-    int32_t* dst = p.acc + (size_t)row * p.N + n0;
-    if (full && p.acc_vec) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<int4*>(dst + j) =
-            make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
-    } else {
-      for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (int)r[j];
-    }
   }
   float v[32];
 #pragma unroll
@@ -307,7 +333,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
                                               size_t part_stride = 0, bool add_tmem = false) {
   const int row = row0 + q * 32 + lane;
   const int rl = q * 32 + lane;  // row within the staging block
-  const float sa = (!p.fp_acc && row < p.M) ? __ldg(p.sA + row) : 0.f;
+  const float sa = (!p.fp_acc && !p.no_out && row < p.M) ? __ldg(p.sA + row) : 0.f;
   const bool skip = p.skip_flag != nullptr && *reinterpret_cast<const volatile int*>(p.skip_flag) != 0;
   if (!p.tma_store) {
 #pragma unroll 1
@@ -362,10 +388,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
 #pragma unroll
         for (int j = 0; j < 32; ++j) sb[j] = (nc + j < p.N) ? __ldg(p.sB + nc + j) : 0.f;
       }
-      if (p.acc && row < p.M) {
-        int32_t* dst = p.acc + (size_t)row * p.N + nc;
-        for (int j = 0; j < 32 && nc + j < p.N; ++j) dst[j] = (int)r[j];
-      }
+      if (p.acc && row < p.M && nc < p.N) store_acc(p, row, nc, nc + 32 <= p.N, r);
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j)
@@ -468,7 +491,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int mb, nb;
         tile_coords(tile, p, mb, nb);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_ns)) {
             if (!*abort_flag) report(p.err, DEVERR_TIMEOUT_PRODUCER, abort_flag);
             ok = false;
             break;
@@ -493,7 +516,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (long long f = (issued > STAGES ? issued - STAGES : 0); f < issued; ++f) {
         const int s = (int)(f % STAGES);
         const uint32_t par = (uint32_t)((f / STAGES) & 1);
-        if (!ptx::mbar_wait(full_bar(s), par, nullptr)) {
+        if (!ptx::mbar_wait(full_bar(s), par, nullptr, p.wait_ns)) {
           report(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag);
           break;
         }
@@ -513,7 +536,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
         const int a = it & 1;
         const uint32_t aphase = (uint32_t)((it >> 1) & 1);
-        if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag)) {
+        if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag, p.wait_ns)) {
           if (!*abort_flag) report(p.err, DEVERR_TIMEOUT_MMA, abort_flag);
           ok = false;
           break;
@@ -521,7 +544,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(a * BN);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag)) {
+          if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag, p.wait_ns)) {
             if (!*abort_flag) report(p.err, DEVERR_TIMEOUT_MMA, abort_flag);
             ok = false;
             break;
@@ -558,7 +581,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok && issued_any) {
         // Wait for the MMAs already issued before TMEM is released.
         ptx::umma_commit(drain_bar);
-        if (!ptx::mbar_wait(drain_bar, 0, nullptr)) report(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag);
+        if (!ptx::mbar_wait(drain_bar, 0, nullptr, p.wait_ns)) report(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag);
       }
     }
   } else {
@@ -573,7 +596,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(tile, p, mb, nb);
       const int a = it & 1;
       const uint32_t aphase = (uint32_t)((it >> 1) & 1);
-      bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag);
+      bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag, p.wait_ns);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is .sync.aligned
       if (!ok && lane == 0 && !*abort_flag) report(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag);
       ptx::tc_fence_after();
@@ -687,7 +710,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         int mb, nb;
         tile_coords(tile, p, mb, nb);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_ns)) {
             if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_PRODUCER, abort_flag, rank);
             ok = false;
             break;
@@ -710,7 +733,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       // Drain: the even CTA's full barriers count both CTAs' copies.
       if (rank == 0) {
         for (long long f = (issued > STAGES ? issued - STAGES : 0); f < issued; ++f) {
-          if (!ptx::mbar_wait(full_bar((int)(f % STAGES)), (uint32_t)((f / STAGES) & 1), nullptr)) {
+          if (!ptx::mbar_wait(full_bar((int)(f % STAGES)), (uint32_t)((f / STAGES) & 1), nullptr, p.wait_ns)) {
             report_pair(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag, rank);
             break;
           }
@@ -732,7 +755,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       for (; ok && pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part); ++it) {
         const int a = it & 1;
         const uint32_t aphase = (uint32_t)((it >> 1) & 1);
-        if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag)) {
+        if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag, p.wait_ns)) {
           if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_MMA, abort_flag, rank);
           ok = false;
           break;
@@ -740,7 +763,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(a * BN);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag)) {
+          if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag, p.wait_ns)) {
             if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_MMA, abort_flag, rank);
             ok = false;
             break;
@@ -770,7 +793,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok && issued_any) {
         ptx::umma_commit_pair(drain_bar, 0x1);
-        if (!ptx::mbar_wait(drain_bar, 0, nullptr)) report_pair(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag, rank);
+        if (!ptx::mbar_wait(drain_bar, 0, nullptr, p.wait_ns)) report_pair(p.err, DEVERR_TIMEOUT_DRAIN, abort_flag, rank);
       }
     }
   } else {
@@ -790,7 +813,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tile_coords(tile, p, mb, nb);
       const int a = it & 1;
       const uint32_t aphase = (uint32_t)((it >> 1) & 1);
-      bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag);
+      bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag, p.wait_ns);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is .sync.aligned
       if (!ok && lane == 0 && !*abort_flag)
         report_pair(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag, rank);
@@ -840,8 +863,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         bool got = false;
         const unsigned long long t0 = ptx::globaltimer();
         for (;;) {
-          if (ptx::ld_acquire_gpu(p.cnt + tt) >= p.split_s - 1) { got = true; break; }
-          if (*abort_flag || ptx::globaltimer() - t0 > ptx::kWaitLimitNs) break;
+          if (ptx::ld_acquire_gpu(p.cnt + tt) >= p.split_s - 1 + p.hold_split) { got = true; break; }
+          if (*abort_flag || ptx::globaltimer() - t0 > p.wait_ns) break;
           __nanosleep(64);
         }
         if (!got && !*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag, rank);
@@ -1013,12 +1036,14 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   const int bm = use_pair ? pair::BM : BM, bn = use_pair ? pair::BN : BN;
   const uint64_t a_pitch = a.a_pitch ? a.a_pitch : (uint64_t)K;
   const uint64_t b_pitch = a.b_pitch ? a.b_pitch : (uint64_t)K;
+  const uint64_t a_extent = a.a_extent ? a.a_extent : a_pitch;
+  const uint64_t kn_pitch = a.b_kn_pitch ? a.b_kn_pitch : (uint64_t)N;
   CUtensorMap tmA, tmB;
-  if (!make_map_u8(&tmA, a.A, a_pitch, (uint64_t)M, a_pitch, BK, 128))
+  if (!make_map_u8(&tmA, a.A, a_extent, (uint64_t)M, a_pitch, BK, 128))
     return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for A [%d,%d]", M, K);
   // B boxes: [K,N] -> 128 columns x 128 k-rows; [N,K] -> 128 k-bytes x (bn per CTA) rows.
   const uint32_t nk_rows = use_pair ? 128 : BN;
-  bool okb = a.b_kn ? make_map_u8(&tmB, a.B, (uint64_t)N, (uint64_t)K, (uint64_t)N, 128, BK)
+  bool okb = a.b_kn ? make_map_u8(&tmB, a.B, (uint64_t)N, (uint64_t)K, kn_pitch, 128, BK)
                     : make_map_u8(&tmB, a.B, b_pitch, (uint64_t)N, b_pitch, BK, nk_rows);
   if (!okb) return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for B");
 
@@ -1034,14 +1059,21 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   p.b_seg = a.b_seg;
   p.num_tiles = t.num_tiles;
   p.sA = a.sA; p.sB = a.sB; p.out = a.out; p.acc = a.acc;
+  p.acc_ld = a.acc_ld ? a.acc_ld : N;
+  p.acc_c = a.acc_c;
+  p.acc_c_ld = a.acc_c_ld;
+  p.no_out = a.no_out;
+  p.wait_ns = s->dev->wait_ns;
+  p.hold_split = s->dev->hold_split ? 1 : 0;
   p.fp_acc = a.kind != KIND_I8;
   p.alpha = a.alpha; p.beta = a.beta; p.bias = a.bias;
   p.ep_alpha = a.ep_alpha; p.ep_beta = a.ep_beta;
   p.skip_flag = a.skip_flag;
   p.err = s->dev->d_err;
   const int esize = a.out_dtype == QGEMM_BF16 ? 2 : 4;
-  p.out_vec = aligned((uint64_t)a.out, 16) && ((uint64_t)a.ldc * esize) % 16 == 0;
-  p.acc_vec = a.acc != nullptr && aligned((uint64_t)a.acc, 16) && N % 4 == 0;
+  p.out_vec = !a.no_out && aligned((uint64_t)a.out, 16) && ((uint64_t)a.ldc * esize) % 16 == 0;
+  p.acc_vec = a.acc != nullptr && aligned((uint64_t)a.acc, 16) && p.acc_ld % 4 == 0 &&
+              (a.acc_c == nullptr || (aligned((uint64_t)a.acc_c, 16) && a.acc_c_ld % 4 == 0));
   // Output tensor map for TMA stores: [M rows, N columns] with row pitch ldc, boxes of
   // 128 rows x 128 bytes, 128-byte swizzle (matching the staging buffer).
   CUtensorMap tmO;

@@ -64,6 +64,9 @@ SIGNATURES = {
     "qgemm_device_close": (_S, [_P]),
     "qgemm_device_info": (_S, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
                                ctypes.POINTER(_SZ), ctypes.POINTER(_I)]),
+    "qgemm_device_set_wait_limit": (_S, [_P, _U64]),
+    "qgemm_device_get_wait_limit": (_S, [_P, ctypes.POINTER(_U64)]),
+    "qgemm_debug_hold_split": (_S, [_P, _I]),
     "qgemm_stream_create": (_S, [_P, ctypes.POINTER(_P)]),
     "qgemm_stream_wrap": (_S, [_P, _P, ctypes.POINTER(_P)]),
     "qgemm_stream_destroy": (_S, [_P]),
@@ -83,6 +86,10 @@ SIGNATURES = {
     "qgemm_weight_only_quantize_per_channel": (_S, [_P, _U64, _U64, _U64, _U64, _I, _I]),
     "qgemm_dequantize": (_S, [_P, _U64, _U64, _U64, _I, _I]),
     "qgemm_w8a8_gemm": (_S, [_P, _U64, _U64, _I, _U64, _U64, _U64, _I, _I, _I, _I, _I, _U64, _I]),
+    "qgemm_tensor_core_gemm_int8": (_S, [_P, _U64, _U64, _U64, _U64, _U64, _U64, _I, _I, _I, _I,
+                                         _I, _I, _I, _I]),
+    "qgemm_int8_gemm_kernel": (_S, [_P, _U64, _U64, _U64, _I, _I, _I, _I, _I, _I, ctypes.c_float,
+                                    ctypes.c_float]),
     "qgemm_w8a8_gemm_static_scratch": (_S, [_P, _U64, _U64, _I, _U64, _U64, _U64, _I, _I, _I, _I,
                                              _I, _U64, _I]),
     "qgemm_w4a16_grouped_gemm": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I]),
@@ -108,6 +115,10 @@ SIGNATURES = {
     "qgemm_prepack_w8_nk": (_S, [_P, _U64, _U64, _I, _I]),
     "qgemm_launch_by_name": (_S, [_P, ctypes.c_char_p, ctypes.POINTER(_U64), _I,
                                   ctypes.POINTER(_I), _I]),
+    "qgemm_bridge_launch_kernel": (ctypes.c_int64, [_P, ctypes.c_char_p, _I, _I, _I, _I, _I, _I,
+                                                    ctypes.POINTER(_U64), _I,
+                                                    ctypes.POINTER(ctypes.c_float),
+                                                    ctypes.POINTER(ctypes.c_char_p), _I]),
     "qgemm_blob_save": (_S, [ctypes.c_char_p, ctypes.POINTER(BlobInfo), _P, _P]),
     "qgemm_blob_info_read": (_S, [ctypes.c_char_p, ctypes.POINTER(BlobInfo)]),
     "qgemm_blob_load": (_S, [ctypes.c_char_p, _P, _SZ, _P, _SZ]),

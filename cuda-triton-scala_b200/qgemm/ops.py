@@ -161,6 +161,61 @@ class QuantizedGemmOps:
         L.call("qgemm_launch_by_name", self._h, name.encode(), bufs, len(buffers), iv, len(ints))
 
 
+class CUDARuntimeJavaBridge:
+    """``CUDARuntimeJavaBridge.launchKernel`` (driver/CUDARuntimeJavaBridge.scala:121-165):
+    launch by name with the result buffer first in ``bufferAddrs`` and Float scalars named
+    by ``scalarKeys`` (or positional when keys are None).  Returns the result buffer's
+    address, or -1 on failure, as the bridge does; ``last_error()`` then says why."""
+
+    def __init__(self, stream):
+        self.stream = stream
+        self._h = stream.handle
+
+    def launchKernel(self, name: str, gridX: int, gridY: int, gridZ: int, blockX: int,
+                     blockY: int, blockZ: int, bufferAddrs, scalarVals=None,
+                     scalarKeys=None) -> int:
+        bufs = (ctypes.c_uint64 * max(1, len(bufferAddrs)))(*[L.addr(b) for b in bufferAddrs])
+        n = 0 if scalarVals is None else len(scalarVals)
+        vals = (ctypes.c_float * max(1, n))(*[float(v) for v in (scalarVals or [])])
+        keys = None
+        if scalarKeys is not None:
+            if len(scalarKeys) != n:
+                raise ValueError("scalarKeys and scalarVals differ in length")
+            keys = (ctypes.c_char_p * max(1, n))(*[k.encode() for k in scalarKeys])
+        return int(L.lib().qgemm_bridge_launch_kernel(
+            self._h, name.encode(), gridX, gridY, gridZ, blockX, blockY, blockZ, bufs,
+            len(bufferAddrs), vals if n else None, keys, n))
+
+
+class TensorCoreOps:
+    """``TensorCoreOps.tensorCoreGemmInt8`` (operators/intrinsic/TensorCoreOps.scala:294-340):
+    same parameters; d = a x b (+ c) with int32 sums, on the W8A8 tensor-core kernel."""
+
+    def __init__(self, stream):
+        self.stream = stream
+        self._h = stream.handle
+
+    def tensorCoreGemmInt8(self, a, b, scalesA, scalesB, c, d, M: int, N: int, K: int,
+                           lda: int, ldb: int, ldc: int, ldd: int, hasC: bool):
+        L.call("qgemm_tensor_core_gemm_int8", self._h, L.addr(a), L.addr(b), L.addr(scalesA),
+               L.addr(scalesB), L.addr(c), L.addr(d), M, N, K, lda, ldb, ldc, ldd,
+               1 if hasC else 0)
+
+
+class CutlassGemm:
+    """``CutlassGemm.int8GemmKernel`` (cutlass/CutlassGemm.scala:987-1041): same parameters;
+    D = (A x B) * scaleA * scaleB for int8 values held in Int arrays."""
+
+    def __init__(self, stream):
+        self.stream = stream
+        self._h = stream.handle
+
+    def int8GemmKernel(self, D, A, B, M: int, N: int, K: int, lda: int, ldb: int, ldd: int,
+                       scaleA: float, scaleB: float):
+        L.call("qgemm_int8_gemm_kernel", self._h, L.addr(D), L.addr(A), L.addr(B), M, N, K,
+               lda, ldb, ldd, float(scaleA), float(scaleB))
+
+
 class MatrixOps:
     """The fp32 entry points of ``object MatrixOps``
     (src/main/scala/cuda/dsl/operators/linalg/MatrixOps.scala): same names, parameter

@@ -42,6 +42,21 @@ class Device:
             L.call("qgemm_device_close", self.handle)
             self.handle = None
 
+    @property
+    def wait_limit_ns(self) -> int:
+        """Limit of every bounded device-side wait of the tensor-core GEMM kernels."""
+        v = ctypes.c_uint64()
+        L.call("qgemm_device_get_wait_limit", self.handle, ctypes.byref(v))
+        return v.value
+
+    @wait_limit_ns.setter
+    def wait_limit_ns(self, ns: int):
+        L.call("qgemm_device_set_wait_limit", self.handle, int(ns))
+
+    def debug_hold_split(self, enable: bool):
+        """Test hook: make the W8A8 GEMM's split waits run out (the timeout path)."""
+        L.call("qgemm_debug_hold_split", self.handle, 1 if enable else 0)
+
     def stream(self) -> "Stream":
         return Stream(self)
 

@@ -98,6 +98,19 @@ QGEMM_API qgemm_status qgemm_device_close(qgemm_device_t dev);
 /* sm_count, compute capability, L2 bytes, and whether tcgen05 kernels run. */
 QGEMM_API qgemm_status qgemm_device_info(qgemm_device_t dev, int* sm_count, int* cc_major,
                                int* cc_minor, size_t* l2_bytes, int* has_tcgen05);
+/* Limit, in nanoseconds of the GPU's global timer, of every bounded device-side wait
+ * in the tensor-core GEMM kernels (W8A8, bf16, fp32 entry points) launched on this
+ * device from now on; default 2 s, accepted range 1 us .. 60 s.  A wait that runs out
+ * ends its kernel early and qgemm_stream_sync() then reports QGEMM_ERR_TIMEOUT.  No
+ * counterpart in the reference, whose launches never wait on the device. */
+QGEMM_API qgemm_status qgemm_device_set_wait_limit(qgemm_device_t dev, uint64_t limit_ns);
+QGEMM_API qgemm_status qgemm_device_get_wait_limit(qgemm_device_t dev, uint64_t* limit_ns);
+/* Test hook for the timeout path (no counterpart in the reference): with enable != 0,
+ * the final K part of every tile the W8A8 GEMM's last-wave split cuts waits for one
+ * count-in more than the other parts make, so its bounded wait runs out after the
+ * device's wait limit; the call then ends in QGEMM_ERR_TIMEOUT at qgemm_stream_sync()
+ * (its output is undefined) and the stream stays usable.  Leave it off otherwise. */
+QGEMM_API qgemm_status qgemm_debug_hold_split(qgemm_device_t dev, int enable);
 
 /* ---- streams ---------------------------------------------------------------
  * Replaces driver/TritonDriverAPINative.scala:78-122 (NativeCUDAStream). */
@@ -168,13 +181,43 @@ QGEMM_API qgemm_status qgemm_dequantize(qgemm_stream_t s, uint64_t qWeight, uint
  *   sA   f32 [M] (per token, `scalesX`);  sB f32 [N] (per channel, `scalesW`)
  *   out  [M, ldc] of out_dtype (QGEMM_F32 or QGEMM_BF16, RNE); ldc >= N
  *   acc_i32  optional int32 [M, N] (ld N) raw accumulators, 0 for none
- * Also the target of TensorCoreOps.tensorCoreGemmInt8
- * (operators/intrinsic/TensorCoreOps.scala:294-340) and CutlassGemm.int8GemmKernel
- * (cutlass/CutlassGemm.scala:987-1041) names; their broken arithmetic (the -128
- * offset, strided k, shared accumulator) is deliberately not reproduced. */
+ * The int8 GEMM names of TensorCoreOps and CutlassGemm (below) run on the same
+ * kernel. */
 QGEMM_API qgemm_status qgemm_w8a8_gemm(qgemm_stream_t s, uint64_t A, uint64_t B, int b_layout,
                              uint64_t sA, uint64_t sB, uint64_t out, int out_dtype,
                              int ldc, int M, int N, int K, uint64_t acc_i32, int algo);
+
+/* TensorCoreOps.tensorCoreGemmInt8 (operators/intrinsic/TensorCoreOps.scala:294-340),
+ * same parameters in the same order:
+ *   d[m*ldd + n] = sum_k a[m*lda + k] * b[k*ldb + n]  (+ c[m*ldc + n] when hasC != 0)
+ * a, b int8; c, d int32; sums wrap modulo 2^32 like Scala Int.  scalesA / scalesB are
+ * accepted and not read (the reference body never reads them either).  The body's
+ * -128 offset on signed bytes, its visiting only every 16th k and its one output per
+ * 16 x 16 block are not reproduced: every output gets the whole sum.  Runs on the
+ * tensor cores (sums plus c written from the accumulators) when lda and ldb are
+ * multiples of 16 and a, b are 16-byte aligned, else on an exact CUDA-core kernel;
+ * both give the same bits.  Requires lda >= K, ldb >= N, ldd >= N (ldc >= N with c),
+ * 4-byte aligned c, d. */
+QGEMM_API qgemm_status qgemm_tensor_core_gemm_int8(qgemm_stream_t s, uint64_t a, uint64_t b,
+                                                   uint64_t scalesA, uint64_t scalesB,
+                                                   uint64_t c, uint64_t d, int M, int N, int K,
+                                                   int lda, int ldb, int ldc, int ldd, int hasC);
+
+/* CutlassGemm.int8GemmKernel (cutlass/CutlassGemm.scala:987-1041), same parameters in
+ * the same order:
+ *   D[m*ldd + n] = (sum_k float(A[m*lda + k]) * float(B[k*ldb + n])) * scaleA * scaleB
+ * A, B int32 arrays holding int8 values; D fp32.  Values in [-128, 127] run on the
+ * tensor cores as an exact integer sum rounded once to fp32, then (x * scaleA) * scaleB:
+ * bit-identical to the reference's fp32 loop while no partial sum leaves +-2^24 (always
+ * for K <= 1040), the correctly rounded sum beyond that.  If any value lies outside
+ * [-128, 127], the reference's own fp32 loop (k ascending, each product and sum rounded
+ * on its own) computes the whole output on CUDA cores instead.  One accumulator per
+ * output (the body shares one among 64 outputs).  Requires lda >= K, ldb >= N,
+ * ldd >= N, M <= 65535, 4-byte aligned pointers.  Packed operands live in the stream
+ * handle's scratch (made or grown by the call; make one call before graph capture). */
+QGEMM_API qgemm_status qgemm_int8_gemm_kernel(qgemm_stream_t s, uint64_t D, uint64_t A,
+                                              uint64_t B, int M, int N, int K, int lda, int ldb,
+                                              int ldd, float scaleA, float scaleB);
 
 /* qgemm_w8a8_gemm for callers that must not allocate device memory during the call
  * (no counterpart in the reference).  qgemm_w8a8_gemm may make scratch on the stream
@@ -327,16 +370,34 @@ QGEMM_API qgemm_status qgemm_prepack_w8_nk(qgemm_stream_t s, uint64_t src_kn, ui
                                  int K, int N);
 
 /* Launch by reference kernel name, the by-name path of
- * TritonKernelRunner.launchKernel (dsl/TritonKernelRunner.scala:68-73) and
- * CUDARuntimeJavaBridge.launchKernel (driver/CUDARuntimeJavaBridge.scala:121-165).
+ * TritonKernelRunner.launchKernel (dsl/TritonKernelRunner.scala:68-73).
  * bufs are device addresses in the reference method's parameter order, ints
  * the Int parameters in order (Bool as 0/1).  Names: "w8a32Gemm", "w4a16Gemm",
  * "w8a16Gemm", "w8a16GemmRowWise", "dynamicQuantize",
- * "weightOnlyQuantizePerChannel", "dequantize", "matmul", "matmulAddBias", "gemv"
- * (sgemm takes Float parameters: call qgemm_sgemm).  Unknown name -> INVALID_ARG. */
+ * "weightOnlyQuantizePerChannel", "dequantize", "matmul", "matmulAddBias", "gemv",
+ * "tensorCoreGemmInt8" (sgemm and int8GemmKernel take Float parameters: use
+ * qgemm_bridge_launch_kernel below).  Unknown name -> INVALID_ARG. */
 QGEMM_API qgemm_status qgemm_launch_by_name(qgemm_stream_t s, const char* name,
                                   const uint64_t* bufs, int nbufs,
                                   const int* ints, int nints);
+
+/* CUDARuntimeJavaBridge.launchKernel (driver/CUDARuntimeJavaBridge.scala:121-165), same
+ * parameters in the same order after the stream: a kernel name, the grid and block
+ * triples (accepted and not used: each kernel here picks its own launch shape),
+ * bufferAddrs with the result buffer first and the method's other Ptr parameters after
+ * it in declaration order, and scalarVals with scalarKeys naming the method's scalar
+ * parameters ("M", "alpha", "hasBias", ...).  Without keys (scalarKeys null) the values
+ * are the scalar parameters in declaration order.  Int and Bool parameters travel as
+ * Float, as in the bridge: they must be integral (|v| <= 2^24; Bool 0 or 1).  A scalar
+ * left out takes the method's default (qBits = 8) or is an error.  Names: every name of
+ * qgemm_launch_by_name plus "sgemm" (alpha, beta) and "int8GemmKernel" (scaleA,
+ * scaleB).  Returns bufferAddrs[0] once the launch is queued, -1 on any failure (the
+ * message in qgemm_last_error()), like the bridge's -1L. */
+QGEMM_API int64_t qgemm_bridge_launch_kernel(qgemm_stream_t s, const char* name, int gridX,
+                                             int gridY, int gridZ, int blockX, int blockY,
+                                             int blockZ, const uint64_t* bufferAddrs, int nbufs,
+                                             const float* scalarVals,
+                                             const char* const* scalarKeys, int nscalars);
 
 /* ---- weight blobs ------------------------------------------------------------
  * A versioned file holding quantised weights already in a kernel layout, with

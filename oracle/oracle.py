@@ -50,7 +50,7 @@ def lib():
         L.oracle_scala_f2i.restype = ctypes.c_int32
         L.oracle_scala_f2i.argtypes = [ctypes.c_float]
         L.oracle_w8a32_gemm.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _P]
-        L.oracle_w8a8_gemm_rows.argtypes = [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I]
+        L.oracle_w8a8_gemm_rows.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I]
         L.oracle_w4a16_gemm.argtypes = [_P, _P, _P, _P, _I, _I, _I]
         L.oracle_w4a16_grouped.argtypes = [_P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I]
         L.oracle_w8a16_gemm.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I]
@@ -61,6 +61,10 @@ def lib():
         L.oracle_matmul_f32.argtypes = [_P, _P, _P, _P, _I, _I, _I, ctypes.c_float,
                                         ctypes.c_float, _I, _I]
         L.oracle_gemv_f32.argtypes = [_P, _P, _P, _I, _I]
+        L.oracle_tensor_core_gemm_int8.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+                                                   _I]
+        L.oracle_int8_gemm_kernel.argtypes = [_P, _P, _P, _I, _I, _I, _I, _I, _I,
+                                              ctypes.c_float, ctypes.c_float, _I]
         L.oracle_max_threads.restype = _I
         _lib = L
     return _lib
@@ -121,22 +125,24 @@ def w8a32_gemm(wInt8, scalesW, x, scalesX):
 
 
 def w8a8_gemm_rows(wInt8, scalesW, x, scalesX, m0=0, m1=None, threads=0,
-                   want_f32=True, want_bf16=True):
+                   want_f32=True, want_bf16=True, want_acc=False):
     """Rows [m0, m1) of the W8A8 GEMM (same arithmetic as w8a32_gemm, OpenMP).
-    Returns (y fp32 [m1-m0, N] or None, y bf16 bits [m1-m0, N] or None)."""
+    Returns (y fp32 [m1-m0, N] or None, y bf16 bits [m1-m0, N] or None), and the int32
+    sums [m1-m0, N] as a third element when want_acc."""
     w = _c(wInt8, np.int8); sw = _c(scalesW, np.float32)
     xx = _c(x, np.int8); sx = _c(scalesX, np.float32)
     M, K = xx.shape
     N = w.shape[1]
     if m1 is None:
         m1 = M
-    rows = m1 - m0
-    # The C routine indexes outputs by absolute row; hand it views that start at row 0.
+    # The C routine indexes outputs by absolute row; hand it buffers that start at row 0.
     y = np.empty((M, N), np.float32) if want_f32 else None
     yb = np.empty((M, N), np.uint16) if want_bf16 else None
+    acc = np.empty((M, N), np.int32) if want_acc else None
     lib().oracle_w8a8_gemm_rows(_ptr(w), _ptr(sw), _ptr(xx), _ptr(sx), _ptr(y), _ptr(yb),
-                                M, N, K, m0, m1, threads)
-    return (y[m0:m1] if y is not None else None, yb[m0:m1] if yb is not None else None)
+                                _ptr(acc), M, N, K, m0, m1, threads)
+    out = (y[m0:m1] if y is not None else None, yb[m0:m1] if yb is not None else None)
+    return out + (acc[m0:m1],) if want_acc else out
 
 
 def w4a16_gemm(wInt4, scalesW, x, N):
@@ -239,3 +245,41 @@ def gemv_f32(A, x):
     y = np.empty(M, np.float32)
     lib().oracle_gemv_f32(_ptr(a), _ptr(xx), _ptr(y), M, N)
     return y
+
+
+# ---- the int8 GEMM names of TensorCoreOps / CutlassGemm ----------------------
+
+def tensor_core_gemm_int8(a, b, c=None, *, M, N, K, lda=None, ldb=None, ldc=None, ldd=None):
+    """TensorCoreOps.tensorCoreGemmInt8 (TensorCoreOps.scala:294-340), its arithmetic for
+    every output: d = a @ b (+ c), int32 wrapping, through leading dimensions.  a int8
+    with rows of lda, b int8 with rows of ldb, c int32 with rows of ldc (None: hasC
+    false).  Returns d int32 [M, ldd] (columns past N zero)."""
+    lda = K if lda is None else lda
+    ldb = N if ldb is None else ldb
+    ldd = N if ldd is None else ldd
+    aa = _c(a, np.int8); bb = _c(b, np.int8)
+    assert aa.size >= (M - 1) * lda + K if M and K else True
+    assert bb.size >= (K - 1) * ldb + N if K and N else True
+    cc = None
+    if c is not None:
+        ldc = N if ldc is None else ldc
+        cc = _c(c, np.int32)
+        assert cc.size >= (M - 1) * ldc + N if M and N else True
+    d = np.zeros((M, ldd), np.int32)
+    lib().oracle_tensor_core_gemm_int8(_ptr(aa), _ptr(bb), _ptr(cc), _ptr(d), M, N, K, lda, ldb,
+                                       ldc or 0, ldd, 1 if c is not None else 0)
+    return d
+
+
+def int8_gemm_kernel(A, B, scaleA, scaleB, *, M, N, K, lda=None, ldb=None, ldd=None, threads=0):
+    """CutlassGemm.int8GemmKernel (CutlassGemm.scala:987-1041) with one fp32 accumulator per
+    output: A, B int32 arrays (rows of lda / ldb); returns D fp32 [M, ldd] (columns past N
+    zero)."""
+    lda = K if lda is None else lda
+    ldb = N if ldb is None else ldb
+    ldd = N if ldd is None else ldd
+    aa = _c(A, np.int32); bb = _c(B, np.int32)
+    D = np.zeros((M, ldd), np.float32)
+    lib().oracle_int8_gemm_kernel(_ptr(D), _ptr(aa), _ptr(bb), M, N, K, lda, ldb, ldd,
+                                  float(scaleA), float(scaleB), int(threads))
+    return D

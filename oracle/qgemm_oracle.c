@@ -82,7 +82,7 @@ void oracle_w8a32_gemm(const int8_t* wInt8, const float* scalesW,
 
 void oracle_w8a8_gemm_rows(const int8_t* wInt8, const float* scalesW,
                            const int8_t* x, const float* scalesX,
-                           float* y, uint16_t* out_bf16,
+                           float* y, uint16_t* out_bf16, int32_t* acc,
                            int M, int N, int K, int m0, int m1, int threads) {
   if (m0 < 0) m0 = 0;
   if (m1 > M) m1 = M;
@@ -104,6 +104,7 @@ void oracle_w8a8_gemm_rows(const int8_t* wInt8, const float* scalesW,
       for (int col = 0; col < N; ++col) accrow[col] += xv * (uint32_t)(int32_t)wr[col];
     }
     for (int col = 0; col < N; ++col) {
+      if (acc) acc[(int64_t)row * N + col] = (int32_t)accrow[col];
       float v = ((float)(int32_t)accrow[col] * scalesW[col]) * scalesX[row];
       if (y) y[(int64_t)row * N + col] = v;
       if (out_bf16) out_bf16[(int64_t)row * N + col] = oracle_f32_to_bf16_rne(v);
@@ -318,4 +319,58 @@ void oracle_gemv_f32(const float* A, const float* x, float* y, int M, int N) {
     for (int j = 0; j < N; ++j) sum += A[(int64_t)i * N + j] * x[j];
     y[i] = sum;
   }
+}
+
+/* ---- the int8 GEMM names of TensorCoreOps and CutlassGemm ----
+ *
+ * TensorCoreOps.tensorCoreGemmInt8 (operators/intrinsic/TensorCoreOps.scala:294-340):
+ *   acc32 = sum over k of aVal * bVal   (Int, wraps modulo 2^32)
+ *   d(mStart*ldd + nStart) = acc32 + (if (hasC) c(mStart*ldc + nStart) else 0)
+ * restated as that arithmetic for every output (m, n) and every k, operands read
+ * through their leading dimensions: d[m*ldd+n] = sum_k a[m*lda+k]*b[k*ldb+n] + c.
+ * The body's own index arithmetic is not restated: it subtracts 128 from each
+ * signed byte, visits every 16th k only and writes one element per 16 x 16 block,
+ * which no caller can want.  scalesA / scalesB are parameters the body never reads;
+ * they are not parameters here either. */
+void oracle_tensor_core_gemm_int8(const int8_t* a, const int8_t* b, const int32_t* c,
+                                  int32_t* d, int M, int N, int K, int lda, int ldb,
+                                  int ldc, int ldd, int hasC) {
+  for (int m = 0; m < M; ++m) {
+    for (int n = 0; n < N; ++n) {
+      uint32_t acc32 = 0;
+      for (int k = 0; k < K; ++k)
+        acc32 += (uint32_t)((int32_t)a[(int64_t)m * lda + k] * (int32_t)b[(int64_t)k * ldb + n]);
+      if (hasC) acc32 += (uint32_t)c[(int64_t)m * ldc + n];
+      d[(int64_t)m * ldd + n] = (int32_t)acc32;
+    }
+  }
+}
+
+/* CutlassGemm.int8GemmKernel (cutlass/CutlassGemm.scala:987-1041):
+ *   var acc: Float = 0.0f
+ *   for kk: acc = acc + tl.load(A, aRow*lda + kk).toFloat * tl.load(B, kk*ldb + bCol).toFloat
+ *   tl.store(D, aRow*ldd + bCol, acc * scaleA * scaleB)
+ * restated with one accumulator per output element, k ascending, each product and
+ * sum rounded on its own (JVM float), then (acc * scaleA) * scaleB.  The body keeps
+ * one accumulator for all 64 outputs of a thread, so every one of them would get the
+ * same sum; that sharing is not restated. A and B are Int (32-bit) arrays. */
+void oracle_int8_gemm_kernel(float* D, const int32_t* A, const int32_t* B, int M, int N, int K,
+                             int lda, int ldb, int ldd, float scaleA, float scaleB,
+                             int threads) {
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+#endif
+  for (int m = 0; m < M; ++m) {
+    float* acc = (float*)malloc(sizeof(float) * (N > 0 ? N : 1));
+    for (int n = 0; n < N; ++n) acc[n] = 0.0f;
+    for (int k = 0; k < K; ++k) {
+      const float av = (float)A[(int64_t)m * lda + k];
+      const int32_t* br = B + (int64_t)k * ldb;
+      for (int n = 0; n < N; ++n) acc[n] = acc[n] + av * (float)br[n];
+    }
+    for (int n = 0; n < N; ++n) D[(int64_t)m * ldd + n] = acc[n] * scaleA * scaleB;
+    free(acc);
+  }
+  (void)threads;
 }

@@ -51,10 +51,11 @@ void oracle_w8a32_gemm(const int8_t* wInt8, const float* scalesW,
 /* Same arithmetic, loop-interchanged (m, k, n) and OpenMP-parallel over rows.
  * Integer sums are order-independent, so results are bit-identical to
  * oracle_w8a32_gemm.  out_bf16 (optional) receives RNE(y); y may be NULL
- * when only out_bf16 is wanted.  Rows [m0, m1) only (a bounded sample). */
+ * when only out_bf16 is wanted; acc (optional) receives the int32 sums.  Rows
+ * [m0, m1) only (a bounded sample). */
 void oracle_w8a8_gemm_rows(const int8_t* wInt8, const float* scalesW,
                            const int8_t* x, const float* scalesX,
-                           float* y, uint16_t* out_bf16,
+                           float* y, uint16_t* out_bf16, int32_t* acc,
                            int M, int N, int K, int m0, int m1, int threads);
 
 /* QuantizedGemmOps.w4a16Gemm (QuantizedGemmOps.scala:218-247).
@@ -106,6 +107,21 @@ void oracle_matmul_f32(const float* A, const float* B, const float* bias, float*
 
 /* MatrixOps.gemv (MatrixOps.scala:166-177): y = A x, A [M,N]. */
 void oracle_gemv_f32(const float* A, const float* x, float* y, int M, int N);
+
+/* TensorCoreOps.tensorCoreGemmInt8 (operators/intrinsic/TensorCoreOps.scala:294-340),
+ * its arithmetic for every output: d[m*ldd+n] = sum_k a[m*lda+k] * b[k*ldb+n]
+ * (+ c[m*ldc+n] when hasC), int32 wrapping. */
+void oracle_tensor_core_gemm_int8(const int8_t* a, const int8_t* b, const int32_t* c,
+                                  int32_t* d, int M, int N, int K, int lda, int ldb,
+                                  int ldc, int ldd, int hasC);
+
+/* CutlassGemm.int8GemmKernel (cutlass/CutlassGemm.scala:987-1041), one fp32
+ * accumulator per output: acc += float(A[m*lda+k]) * float(B[k*ldb+n]) in ascending
+ * k, then D[m*ldd+n] = (acc * scaleA) * scaleB.  A, B int32 arrays.  OpenMP over rows
+ * (threads <= 0: all); each element's order is unchanged. */
+void oracle_int8_gemm_kernel(float* D, const int32_t* A, const int32_t* B, int M, int N, int K,
+                             int lda, int ldb, int ldd, float scaleA, float scaleB,
+                             int threads);
 
 /* Threads the OpenMP build can use (1 without OpenMP). */
 int oracle_max_threads(void);

@@ -7,8 +7,10 @@
  *                        back and corrupted (no GPU needed)
  *   qgemm_c_client gpu   device 0: the reference w8a32Gemm at its own 64x512x512 case
  *                        and the W8A8 GEMM on the tensor cores (int32 accumulators and
- *                        fp32 outputs bit-exact against the loop below), and the fp32
- *                        MatrixOps.matmul within 1e-5 of sum |a*b|
+ *                        fp32 outputs bit-exact against the loop below), the fp32
+ *                        MatrixOps.matmul within 1e-5 of sum |a*b|, and the int8 GEMM
+ *                        names (tensorCoreGemmInt8 direct, int8GemmKernel through the
+ *                        Java bridge's by-name form) bit-exact against plain loops
  *
  * Exit status 0 when every check passes; each failure prints one line.
  */
@@ -214,7 +216,86 @@ static int gpu_checks(void) {
     free(A); free(B); free(C);
   }
 
-  /* 3. errors come back as statuses, and the handles stay usable */
+  /* 3. the int8 GEMM names: TensorCoreOps.tensorCoreGemmInt8 directly (d = a b + c through
+   *    leading dimensions, int32) and CutlassGemm.int8GemmKernel through the Java bridge's
+   *    by-name form (Float scalars named by keys, result buffer first), each against a
+   *    plain loop. */
+  {
+    const int M = 256, N = 272, K = 160, lda = 176, ldb = 288, ldc = 280, ldd = 284;
+    int8_t* a = (int8_t*)malloc((size_t)M * lda);
+    int8_t* b = (int8_t*)malloc((size_t)K * ldb);
+    int32_t* cc = (int32_t*)malloc(sizeof(int32_t) * M * ldc);
+    int32_t* d = (int32_t*)malloc(sizeof(int32_t) * M * ldd);
+    for (int i = 0; i < M * lda; ++i) a[i] = rand_i8();
+    for (int i = 0; i < K * ldb; ++i) b[i] = rand_i8();
+    for (int i = 0; i < M * ldc; ++i) cc[i] = (int32_t)(lcg() * 97u);
+    uint64_t da, db, dc, dd;
+    CALL(qgemm_buffer_alloc(dev, (size_t)M * lda, &da));
+    CALL(qgemm_buffer_alloc(dev, (size_t)K * ldb, &db));
+    CALL(qgemm_buffer_alloc(dev, sizeof(int32_t) * M * ldc, &dc));
+    CALL(qgemm_buffer_alloc(dev, sizeof(int32_t) * M * ldd, &dd));
+    CALL(qgemm_memcpy_h2d(st, da, a, (size_t)M * lda));
+    CALL(qgemm_memcpy_h2d(st, db, b, (size_t)K * ldb));
+    CALL(qgemm_memcpy_h2d(st, dc, cc, sizeof(int32_t) * M * ldc));
+    CALL(qgemm_tensor_core_gemm_int8(st, da, db, 0, 0, dc, dd, M, N, K, lda, ldb, ldc, ldd, 1));
+    CALL(qgemm_memcpy_d2h(st, d, dd, sizeof(int32_t) * M * ldd));
+    CALL(qgemm_stream_sync(st));
+    int bad = 0;
+    for (int m = 0; m < M; ++m)
+      for (int n = 0; n < N; ++n) {
+        uint32_t sum = (uint32_t)cc[(size_t)m * ldc + n];
+        for (int k = 0; k < K; ++k)
+          sum += (uint32_t)((int32_t)a[(size_t)m * lda + k] * (int32_t)b[(size_t)k * ldb + n]);
+        bad += d[(size_t)m * ldd + n] != (int32_t)sum;
+      }
+    CHECK(bad == 0, "tensorCoreGemmInt8: %d outputs differ", bad);
+
+    /* int8GemmKernel: A [M, K], B [K, N] int32 holding int8 values, D [M, N] fp32 */
+    int32_t* A = (int32_t*)malloc(sizeof(int32_t) * M * K);
+    int32_t* B = (int32_t*)malloc(sizeof(int32_t) * K * N);
+    float* D = (float*)malloc(sizeof(float) * M * N);
+    for (int i = 0; i < M * K; ++i) A[i] = rand_i8();
+    for (int i = 0; i < K * N; ++i) B[i] = rand_i8();
+    uint64_t dA, dB, dD;
+    CALL(qgemm_buffer_alloc(dev, sizeof(int32_t) * M * K, &dA));
+    CALL(qgemm_buffer_alloc(dev, sizeof(int32_t) * K * N, &dB));
+    CALL(qgemm_buffer_alloc(dev, sizeof(float) * M * N, &dD));
+    CALL(qgemm_memcpy_h2d(st, dA, A, sizeof(int32_t) * M * K));
+    CALL(qgemm_memcpy_h2d(st, dB, B, sizeof(int32_t) * K * N));
+    const uint64_t addrs[3] = {dD, dA, dB};
+    const float vals[8] = {(float)M, (float)N, (float)K, (float)K, (float)N, (float)N, 0.0625f,
+                           3.0f};
+    const char* keys[8] = {"M", "N", "K", "lda", "ldb", "ldd", "scaleA", "scaleB"};
+    const int64_t r = qgemm_bridge_launch_kernel(st, "int8GemmKernel", (N + 63) / 64,
+                                                 (M + 63) / 64, 1, 256, 1, 1, addrs, 3, vals,
+                                                 keys, 8);
+    CHECK(r == (int64_t)dD, "bridge returned %lld: %s", (long long)r, qgemm_last_error());
+    CALL(qgemm_memcpy_d2h(st, D, dD, sizeof(float) * M * N));
+    CALL(qgemm_stream_sync(st));
+    bad = 0;
+    for (int m = 0; m < M; ++m)
+      for (int n = 0; n < N; ++n) {
+        volatile float acc = 0.0f;
+        for (int k = 0; k < K; ++k) {
+          volatile float p = (float)A[(size_t)m * K + k] * (float)B[(size_t)k * N + n];
+          acc = acc + p;
+        }
+        volatile float t = acc * 0.0625f;
+        const float ref = t * 3.0f;
+        bad += memcmp(&ref, &D[(size_t)m * N + n], sizeof(float)) != 0;
+      }
+    CHECK(bad == 0, "int8GemmKernel: %d outputs differ", bad);
+    const char* bad_keys[1] = {"gamma"};
+    CHECK(qgemm_bridge_launch_kernel(st, "int8GemmKernel", 1, 1, 1, 1, 1, 1, addrs, 3, vals,
+                                     bad_keys, 1) == -1, "an unknown scalar key gives -1");
+    CALL(qgemm_buffer_free(dev, da)); CALL(qgemm_buffer_free(dev, db));
+    CALL(qgemm_buffer_free(dev, dc)); CALL(qgemm_buffer_free(dev, dd));
+    CALL(qgemm_buffer_free(dev, dA)); CALL(qgemm_buffer_free(dev, dB));
+    CALL(qgemm_buffer_free(dev, dD));
+    free(a); free(b); free(cc); free(d); free(A); free(B); free(D);
+  }
+
+  /* 4. errors come back as statuses, and the handles stay usable */
   CHECK(qgemm_w8a8_gemm(st, 0, 0, QGEMM_B_KN, 0, 0, 0, QGEMM_BF16, 8, 8, 8, 16, 0, 0) ==
             QGEMM_ERR_INVALID_ARG, "null operands");
   CALL(qgemm_stream_sync(st));

@@ -41,6 +41,17 @@ def rel_err(y: np.ndarray, ref: np.ndarray) -> float:
     return float(np.max(np.abs(y - ref) / np.maximum(np.abs(ref), floor)))
 
 
+def rel_errs(y: np.ndarray, ref: np.ndarray) -> tuple[float, float]:
+    """(floored, plain): rel_err above, and the plain elementwise max_i |y_i - r_i| / |r_i|
+    over the outputs with r_i != 0 (reported beside the gate: an output near zero makes
+    the plain figure large under any change of summation order)."""
+    y = y.astype(np.float64)
+    ref = ref.astype(np.float64)
+    nz = ref != 0
+    plain = float(np.max(np.abs(y[nz] - ref[nz]) / np.abs(ref[nz]))) if nz.any() else 0.0
+    return rel_err(y, ref), plain
+
+
 def gemm_bound_ratio(y, A, B, *, bias=None, C=None, alpha=1.0, beta=0.0) -> float:
     """max_ij |y_ij - exact_ij| / (|alpha| sum_k |A_ik B_kj| + |bias_j| + |beta C_ij|),
     the exact value taken in float64: the forward-error measure of a floating-point

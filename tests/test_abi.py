@@ -93,3 +93,38 @@ def test_by_name_rejects_unknown_without_a_stream():
     ints = (ctypes.c_int * 1)(0)
     assert L.lib().qgemm_launch_by_name(None, b"noSuchKernel", bufs, 1, ints, 1) == \
         L.ERR_INVALID_ARG
+
+
+def test_bridge_argument_errors_without_gpu():
+    """The Java bridge's by-name form (CUDARuntimeJavaBridge.scala:121-165) answers -1, as
+    the bridge's -1L, for a bad name, buffer count, scalar key or scalar value, before it
+    touches a device; a valid request on a null stream fails on the handle."""
+    import ctypes
+    import qgemm._lib as L
+    lib = L.lib()
+
+    def launch(name, nbufs, vals, keys):
+        bufs = (ctypes.c_uint64 * max(1, nbufs))(*([1] * nbufs))
+        n = len(vals)
+        v = (ctypes.c_float * max(1, n))(*vals)
+        k = None if keys is None else (ctypes.c_char_p * max(1, n))(*[x.encode() for x in keys])
+        return lib.qgemm_bridge_launch_kernel(None, name.encode(), 1, 1, 1, 1, 1, 1, bufs, nbufs,
+                                              v if n else None, k, n)
+
+    assert launch("noSuchKernel", 1, [], None) == -1
+    assert "unknown kernel name" in L.last_error()
+    assert launch("sgemm", 2, [4, 4, 4, 1, 0], None) == -1
+    assert "takes 3 buffers" in L.last_error()
+    assert launch("sgemm", 3, [4, 4, 4, 1, 0], ["M", "N", "K", "alpha", "gamma"]) == -1
+    assert "no scalar 'gamma'" in L.last_error()
+    assert launch("sgemm", 3, [4, 4, 4, 1, 0], ["M", "M", "K", "alpha", "beta"]) == -1
+    assert "given twice" in L.last_error()
+    assert launch("sgemm", 3, [4.5, 4, 4, 1, 0], None) == -1
+    assert "exact Int" in L.last_error()
+    assert launch("w8a16Gemm", 5, [4, 4, 4, 3], None) == -1
+    assert "Bool" in L.last_error()
+    assert launch("int8GemmKernel", 3, [4, 4, 4, 4, 4, 4, 1.0], None) == -1
+    assert "missing" in L.last_error()
+    # qBits of dynamicQuantize has a default (QuantizedGemmOps.scala:127): only the handle fails
+    assert launch("dynamicQuantize", 3, [4, 4], ["K", "N"]) == -1
+    assert "stream" in L.last_error()

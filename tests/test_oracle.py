@@ -150,6 +150,61 @@ def test_rows_variant_is_bit_identical(oracle):
     np.testing.assert_array_equal(yb, oracle.bf16_rne(y))
     _, ys = oracle.w8a8_gemm_rows(B, sB, A, sA, m0=10, m1=20, threads=2, want_f32=False)
     np.testing.assert_array_equal(ys, oracle.bf16_rne(y[10:20]))
+    _, _, acc_rows = oracle.w8a8_gemm_rows(B, sB, A, sA, m0=5, m1=9, want_acc=True)
+    np.testing.assert_array_equal(acc_rows, A[5:9].astype(np.int64) @ B.astype(np.int64))
+
+
+# ---- the int8 GEMM names (TensorCoreOps.tensorCoreGemmInt8, CutlassGemm.int8GemmKernel) ----
+
+def test_tensor_core_gemm_int8_known_answer(oracle):
+    """d = a @ b + c through leading dimensions; padding columns are never read."""
+    a = np.array([[1, 2, 9], [3, 4, 9]], np.int8)          # lda 3, K 2
+    b = np.array([[5, 6, 0, 0], [7, 8, 0, 0]], np.int8)    # ldb 4, N 2
+    c = np.array([[100, 200, 7], [300, 400, 7]], np.int32)  # ldc 3
+    d = oracle.tensor_core_gemm_int8(a, b, c, M=2, N=2, K=2, lda=3, ldb=4, ldc=3, ldd=3)
+    assert d.tolist() == [[119, 222, 0], [343, 450, 0]]
+    d = oracle.tensor_core_gemm_int8(a, b, None, M=2, N=2, K=2, lda=3, ldb=4)
+    assert d.tolist() == [[19, 22], [43, 50]]
+
+
+def test_tensor_core_gemm_int8_wraps_like_scala_int(oracle):
+    a = np.full((1, 4), -128, np.int8)
+    b = np.full((4, 1), -128, np.int8)
+    c = np.array([[2**31 - 65536]], np.int32)
+    d = oracle.tensor_core_gemm_int8(a, b, c, M=1, N=1, K=4)
+    assert int(d[0, 0]) == ((4 * 16384 + 2**31 - 65536 + 2**31) % 2**32) - 2**31
+
+
+def test_int8_gemm_kernel_known_answer(oracle):
+    """(acc * scaleA) * scaleB with one fp32 accumulator per output."""
+    A = np.array([[1, 2], [3, 4]], np.int32)
+    B = np.array([[5, 6], [7, 8]], np.int32)
+    D = oracle.int8_gemm_kernel(A, B, 0.5, 2.0, M=2, N=2, K=2)
+    assert D.tolist() == [[19.0, 22.0], [43.0, 50.0]]
+
+
+def test_int8_gemm_kernel_rounds_in_k_order(oracle):
+    """Past 2^24 the fp32 accumulator rounds: 2^24 + 1 + 1 stays 2^24 in k order, so the
+    result differs from the exact integer sum (2^24 + 2) -- the reference's own loop."""
+    A = np.array([[1, 1, 1]], np.int32)
+    B = np.array([[2**24], [1], [1]], np.int32)
+    D = oracle.int8_gemm_kernel(A, B, 1.0, 1.0, M=1, N=1, K=3)
+    assert float(D[0, 0]) == float(2**24)
+    B2 = np.array([[1], [1], [2**24]], np.int32)
+    D2 = oracle.int8_gemm_kernel(A, B2, 1.0, 1.0, M=1, N=1, K=3)
+    assert float(D2[0, 0]) == float(2**24 + 2)
+
+
+def test_int8_gemm_kernel_matches_exact_sums_in_range(oracle):
+    """int8-range values with K <= 1024 keep every partial sum below 2^24: the fp32 loop is
+    then the exact integer sum rounded once."""
+    rng = np.random.default_rng(21)
+    M, N, K = 9, 33, 1024
+    A = rng.integers(-128, 128, (M, K)).astype(np.int32)
+    B = rng.integers(-128, 128, (K, N)).astype(np.int32)
+    D = oracle.int8_gemm_kernel(A, B, 0.03, 1.7, M=M, N=N, K=K, threads=2)
+    exact = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
+    np.testing.assert_array_equal(D, (exact * np.float32(0.03)) * np.float32(1.7))
 
 
 def test_grouped_reduces_to_reference(oracle):
