@@ -3,21 +3,26 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Headline (`value`): the W8A8 GEMM of the prefill shape M = K = 4096 with a
-4096-column weight shard per GPU (N = 4096 * world, weights column-sharded,
-activations replicated, no collective on the data path): weak scaling, N = 1 is
-exactly the 4096^3 workload.  int8 x int8 -> int32, per-token x per-channel fp32
-dequant, bf16 output; one step = one GEMM launch through libqgemm.
+Headline (`value`): the column-sharded W8A8 GEMM M=16384, N=28672, K=8192 (strong
+scaling): rank r of N holds N/world weight columns and their per-channel scales, the
+activations A and per-token scales are the same on every rank, each rank's bf16 output
+block stays on its GPU.  One GPU runs the whole GEMM.  One step = one GEMM launch per
+rank through libqgemm; value = 2*M*N*K per step over the slowest rank's time.
 
 Also on the same line:
-  roofline      dominant kernel (w8a8_tcgen05) vs the int8 tensor peak
-  e2e           the same GEMM through the C-ABI with host buffers: H2D of the
-                step's activations + scales, the GEMM, D2H of the bf16 output
-  w4a16_decode  (world 1) the W4A16 group-128 GEMV at M = 1, 4, 16, GB/s vs HBM
-  w8a8_large    M=16384, N=28672, K=8192 column-sharded across the world
-                (strong scaling), plus the optional NCCL all-gather of the output
-  cpu_baseline  (world 1, rank 0) the CPU restatement on a bounded row sample
-  clocks        NVML SM clock and throttle reasons sampled during the run
+  roofline      the same kernel at 4096^3 on one GPU (the prefill-shaped GEMM) against
+                the dense int8 tensor peak (2 x the measured burst bf16 rate)
+  e2e           the headline through the C-ABI with host buffers: H2D of the step's
+                activations + scales, the GEMM, D2H of this rank's bf16 output block
+  parity        sampled rows of the headline output (and at N > 1, of every gathered
+                form) against the CPU oracle, outside the timed regions
+  allgather     (N > 1) the whole output on every rank: NCCL all-gather + unshard, and
+                the GEMM + gather in one call (NCCL pipelined, copy-engine window)
+  w8a8_4096     the 4096^3 GEMM itself: TOPS, cuBLASLt context, quantise + GEMM
+  w4a16_decode  (N = 1) the W4A16 group-128 GEMV at M = 1, 4, 16, GB/s vs HBM
+  cpu_baseline  (N = 1, rank 0) the CPU restatement on bounded samples (OpenMP and one
+                thread): the headline GEMM on a row slice, the W4A16 decode GEMV
+  clocks        NVML SM clock and throttle reasons sampled during the timed region
 """
 from __future__ import annotations
 
@@ -38,30 +43,42 @@ for _p in (ROOT, PKG):
 METRIC = "W8A8 GEMM TOPS & W4A16 GEMV HBM GB/s at 1/2/4/8 B200, % of roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch from one `ncu --set full` capture of the same
-# kernel on the same workload (profiles/w8a8_tcgen05_pair_4096.md; the M = 1 decode on
-# the fragment order, the faster layout there: profiles/w4a16_frag_m1.md).
+# kernel on the same workload: the W8A8 pair kernel at 4096^3, the M = 1 decode on the
+# fragment order, and the fp32 matmul's tf32 GEMM at 4096^3.
 NCU_TRAFFIC_W8A8_4096 = 33694208 + 3904000
 NCU_TRAFFIC_W4A16_M1 = 30306304 + 0
-# dram__bytes_read.sum + dram__bytes_write.sum of one tf32 GEMM launch of the fp32
-# matmul at 4096^3 (ncu --set full, profiles/f32_tf32_pair_4096.md)
 NCU_TRAFFIC_F32_GEMM_4096 = 985069568 + 61620736
+
+# The column-sharded GEMM of the headline: M x N x K, weight columns cut in units of 256.
+LARGE_M, LARGE_N, LARGE_K = 16384, 28672, 8192
+SHARD_ALIGN = 256
+SEED_A, SEED_B = 4321, 9000
+
+
+def headline_config(world: int) -> dict:
+    """The `config` of the headline, the same in both arms."""
+    return {"workload": "w8a8_gemm M=16384 N=28672 K=8192, weight columns sharded over the "
+                        "GPUs (N/world per rank, resident), activations replicated, "
+                        "per-token x per-channel fp32 scales, bf16 output resident per rank, "
+                        "B in the reference [K,N] layout",
+            "M": LARGE_M, "N": LARGE_N, "K": LARGE_K, "parallelism": f"col{world}",
+            "l2": "inputs larger than L2: A 134 MB + B shard >= 29 MB per rank > 126 MB"}
 
 
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--no-large", action="store_true", help="skip the sharded large GEMM")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-llama", action="store_true", help="skip the Llama-shaped W4A16 stack")
-    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "large", "llama", "f32", "side"],
+    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "llama", "f32", "side"],
                    default="all",
                    help="run one workload alone (for profiling); prints its own JSON line")
     p.add_argument("--profile", action="store_true",
                    help="with --only w8a8|w4a16: warmup + steps plain launches and nothing "
-                        "else (no sustained clock window, no graphs), for ncu captures")
+                        "else (no clock warm-up, no graphs), for ncu captures")
     return p.parse_args()
 
 
@@ -209,63 +226,114 @@ def timed(fn, steps, world):
     return max_over_ranks(local, world), local
 
 
-def w8a8_headline(ops, st, rank, world, steps, warmup, clocks, sustain=True):
-    """M = K = 4096, 4096 weight columns per rank, 8 rotating input sets."""
+def w8a8_4096(ops, steps, warmup, clocks):
+    """The 4096^3 GEMM (prefill shape, one GPU): 8 rotating input sets (256 MB > L2),
+    `warmup` launches and about 20 ms more of them to raise the clocks, then `steps`
+    launches timed with CUDA events on the launching stream (a burst, well short of
+    the power cap's time constant)."""
     import torch
     import qgemm
-    M, K, NL = 4096, 4096, 4096
-    R = 8  # 8 x (16 MB A + 16 MB B) = 256 MB rotating > 126 MB L2
+    M = N = K = 4096
+    R = 8
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(1234 + rank)
+    gen.manual_seed(1234)
     A = [rand_i8((M, K), gen) for _ in range(R)]
-    B = [rand_i8((K, NL), gen) for _ in range(R)]
+    B = [rand_i8((K, N), gen) for _ in range(R)]
     sA = [rand_u((M,), 0.001, 0.01, gen) for _ in range(R)]
-    sB = [rand_u((NL,), 0.0005, 0.005, gen) for _ in range(R)]
-    out = torch.empty((M, NL), dtype=torch.bfloat16, device="cuda")
+    sB = [rand_u((N,), 0.0005, 0.005, gen) for _ in range(R)]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
 
     def step(i):
         j = i % R
-        ops.w8a8Gemm(A[j], B[j], sA[j], sB[j], out, M, NL, K, b_layout=qgemm.B_KN,
+        ops.w8a8Gemm(A[j], B[j], sA[j], sB[j], out, M, N, K, b_layout=qgemm.B_KN,
                      out_dtype=qgemm.BF16, algo=qgemm.ALGO_TCGEN05)
+
+    for i in range(warmup + 320):
+        step(i)
+    torch.cuda.synchronize()
+    with clocks:
+        t, _ = timed(step, steps, 1)
+    per = t / steps
+    ops_per = 2.0 * M * N * K
+    return dict(TOPS=ops_per / per / 1e12, per_launch_s=per, ops_per_launch=ops_per,
+                A=A, B=B, sA=sA, sB=sB, M=M, N=N, K=K)
+
+
+def weight_unit(u: int, K: int):
+    """Columns [256u, 256u + 256) of the headline's global weights B [K, N] and of sB:
+    every unit has its own seed, so a rank can make any shard, and the global problem is
+    the same whatever the number of ranks."""
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED_B + u)
+    return rand_i8((K, SHARD_ALIGN), g), rand_u((SHARD_ALIGN,), 0.001, 0.01, g)
+
+
+def weight_columns(n0: int, n1: int, K: int):
+    """B[:, n0:n1] (contiguous [K, n1 - n0]) and sB[n0:n1] of the headline's weights."""
+    import torch
+    assert n0 % SHARD_ALIGN == 0 and n1 % SHARD_ALIGN == 0
+    parts = [weight_unit(u, K) for u in range(n0 // SHARD_ALIGN, n1 // SHARD_ALIGN)]
+    return (torch.cat([b for b, _ in parts], dim=1).contiguous(),
+            torch.cat([s for _, s in parts]).contiguous())
+
+
+def large_operands(rank, world):
+    """This rank's operands of the headline GEMM: A [M, K] and sA [M] (the same on every
+    rank), its weight columns B [K, NL] and sB [NL], and an output block [M, NL]."""
+    import torch
+    import qgemm
+    M, N, K = LARGE_M, LARGE_N, LARGE_K
+    n0, n1 = qgemm.shard_columns(N, world, rank, SHARD_ALIGN)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED_A)
+    A = rand_i8((M, K), g)
+    sA = rand_u((M,), 0.001, 0.01, g)
+    B, sB = weight_columns(n0, n1, K)
+    out = torch.empty((M, n1 - n0), dtype=torch.bfloat16, device="cuda")
+    return dict(A=A, sA=sA, B=B, sB=sB, out=out, n0=n0, n1=n1, NL=n1 - n0, M=M, N=N, K=K)
+
+
+def headline_large(ops, lo, world, steps, warmup, clocks):
+    """`warmup` untimed steps, then `steps` timed ones: one GEMM launch per rank each,
+    barrier + synchronize on both sides, CUDA events, the max over ranks."""
+    import torch
+    import qgemm
+    A, B, sA, sB, out = lo["A"], lo["B"], lo["sA"], lo["sB"], lo["out"]
+    M, NL, K = lo["M"], lo["NL"], lo["K"]
+
+    def step(i):
+        ops.w8a8Gemm(A, B, sA, sB, out, M, NL, K, b_layout=qgemm.B_KN, out_dtype=qgemm.BF16,
+                     algo=qgemm.ALGO_TCGEN05)
 
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
-    # keep the clock sampler's window under sustained load for >= ~1 s
     with clocks:
-        t0 = time.time()
-        i = 0
-        while sustain and time.time() - t0 < 1.0:
-            step(i)
-            i += 1
-            if i % 64 == 0:
-                torch.cuda.synchronize()
         t_max, t_local = timed(step, steps, world)
-    ops_per_step = 2.0 * M * NL * K
-    value = ops_per_step * world * steps / t_max / 1e12
-    per_launch_s = t_local / steps
-    return dict(value=value, t_max=t_max, per_launch_s=per_launch_s, ops_per_launch=ops_per_step,
-                A=A, B=B, sA=sA, sB=sB, M=M, N=NL, K=K)
+    total_ops = 2.0 * M * lo["N"] * K
+    return dict(value=total_ops * steps / t_max / 1e12, t_max=t_max, t_local=t_local,
+                ops_per_rank_launch=2.0 * M * NL * K)
 
 
-def w8a8_e2e(ops, st, hb, rank, world, steps):
-    """The headline GEMM through the C-ABI with host buffers.  Every step copies
-    that step's activations A and per-token scales sA from pinned host memory,
-    runs the GEMM on the resident weights and copies the bf16 output back to
-    pinned host memory.  Copies in, GEMMs and copies out run on three streams
-    with double-buffered device buffers, so step i's GEMM overlaps step i+1's
-    upload and step i-1's download (PCIe is full duplex)."""
+def e2e_large(ops, st, lo, world, steps):
+    """The headline GEMM through the C-ABI with host buffers.  Every step copies that
+    step's activations A and per-token scales sA from pinned host memory, runs the GEMM
+    on the resident weight columns and copies this rank's bf16 output block back to
+    pinned host memory.  Copies in, GEMMs and copies out run on three streams with
+    double-buffered device buffers, so step i's GEMM overlaps step i+1's upload and step
+    i-1's download (PCIe is full duplex)."""
     import torch
     import qgemm
-    M, N, K = hb["M"], hb["N"], hb["K"]
+    M, NL, K = lo["M"], lo["NL"], lo["K"]
     NB = 2
-    hA = [hb["A"][j].cpu().pin_memory() for j in range(NB)]
-    hsA = [hb["sA"][j].cpu().pin_memory() for j in range(NB)]
-    hout = [torch.empty((M, N), dtype=torch.bfloat16).pin_memory() for _ in range(NB)]
-    dA = [torch.empty_like(hb["A"][0]) for _ in range(NB)]
-    dsA = [torch.empty_like(hb["sA"][0]) for _ in range(NB)]
-    dout = [torch.empty((M, N), dtype=torch.bfloat16, device="cuda") for _ in range(NB)]
-    B, sB = hb["B"][0], hb["sB"][0]
+    hA = [lo["A"].cpu().pin_memory() for _ in range(NB)]
+    hsA = [lo["sA"].cpu().pin_memory() for _ in range(NB)]
+    hout = [torch.empty((M, NL), dtype=torch.bfloat16).pin_memory() for _ in range(NB)]
+    dA = [torch.empty_like(lo["A"]) for _ in range(NB)]
+    dsA = [torch.empty_like(lo["sA"]) for _ in range(NB)]
+    dout = [torch.empty((M, NL), dtype=torch.bfloat16, device="cuda") for _ in range(NB)]
+    B, sB = lo["B"], lo["sB"]
     s_in, s_mm, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
     q_in, q_mm, q_out = (st.dev.wrap_stream(x.cuda_stream) for x in (s_in, s_mm, s_out))
     mm_ops = type(ops)(q_mm)
@@ -273,7 +341,7 @@ def w8a8_e2e(ops, st, hb, rank, world, steps):
     uploaded = [ev() for _ in range(NB)]
     computed = [ev() for _ in range(NB)]
     downloaded = [ev() for _ in range(NB)]
-    consumed = [ev() for _ in range(NB)]   # GEMM finished reading dA/dsA[j]
+    consumed = [ev() for _ in range(NB)]   # the GEMM finished reading dA/dsA[j]
     used = [False] * NB
 
     def step(i):
@@ -285,12 +353,12 @@ def w8a8_e2e(ops, st, hb, rank, world, steps):
         q_in.h2d_ptr(dsA[j].data_ptr(), hsA[j].data_ptr(), hsA[j].numel() * 4)
         uploaded[j].record(s_in)
         s_mm.wait_event(uploaded[j])
-        mm_ops.w8a8Gemm(dA[j], B, dsA[j], sB, dout[j], M, N, K, b_layout=qgemm.B_KN,
+        mm_ops.w8a8Gemm(dA[j], B, dsA[j], sB, dout[j], M, NL, K, b_layout=qgemm.B_KN,
                         out_dtype=qgemm.BF16, algo=qgemm.ALGO_TCGEN05)
         computed[j].record(s_mm)
         consumed[j].record(s_mm)
         s_out.wait_event(computed[j])
-        q_out.d2h_ptr(hout[j].data_ptr(), dout[j].data_ptr(), M * N * 2)
+        q_out.d2h_ptr(hout[j].data_ptr(), dout[j].data_ptr(), M * NL * 2)
         downloaded[j].record(s_out)
         used[j] = True
 
@@ -303,16 +371,73 @@ def w8a8_e2e(ops, st, hb, rank, world, steps):
         for x in (s_in, s_mm, s_out):
             cur.wait_stream(x)
 
-    run(4)
+    run(3)
     torch.cuda.synchronize()
     t_max, _ = timed(lambda i: run(steps) if i == 0 else None, 1, world)
+    ok = bool(torch.equal(hout[(steps - 1) % NB].cuda(), lo["out"]))
     for q in (q_in, q_mm, q_out):
         q.destroy()
-    value = 2.0 * M * N * K * world * steps / t_max / 1e12
+    value = 2.0 * M * lo["N"] * K * steps / t_max / 1e12
     return {"value": value, "unit": "TOPS", "h2d_bytes_per_step": M * K + M * 4,
-            "d2h_bytes_per_step": M * N * 2, "ms_per_step": t_max / steps * 1e3,
+            "d2h_bytes_per_step": M * NL * 2, "steps": steps,
+            "ms_per_step": t_max / steps * 1e3,
+            "output_equals_device_run": ok,
             "pipelining": "H2D / GEMM / D2H on three streams, double-buffered",
-            "resident": "weights B [K,N] int8 and sB (loaded once, as model weights)"}
+            "resident": "weight columns B [K, N/world] int8 and sB (loaded once, as model "
+                        "weights)", "bytes_per_rank": "h2d and d2h are per rank"}
+
+
+def oracle_rows_check(lo, out, rows, n0, n1, B_host=None, sB_host=None):
+    """Rows `rows` of out[:, n0:n1] (bf16, on the device) against the CPU oracle's rows of
+    the same GEMM (QuantizedGemmOps.scala:102-113, RNE to bf16): True when bit-equal.
+    Runs outside every timed region, as the checker."""
+    import numpy as np
+    import torch
+    from oracle import oracle
+    ridx = torch.as_tensor(rows, device="cuda")
+    A_rows = lo["A"][ridx].cpu().numpy()
+    sA_rows = lo["sA"][ridx].cpu().numpy()
+    if B_host is None:
+        B_host, sB_host = (x.cpu().numpy() for x in weight_columns(n0, n1, lo["K"]))
+    _, yb = oracle.w8a8_gemm_rows(B_host, sB_host, A_rows, sA_rows, want_f32=False,
+                                  threads=host_cores())
+    got = out[ridx].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    return bool(np.array_equal(got, yb))
+
+
+def check_rows(M: int):
+    import numpy as np
+    rng = np.random.default_rng(7)
+    return np.unique(np.concatenate([[0, 1, M - 1], rng.choice(M, 13, replace=False)]))
+
+
+def host_cores() -> int:
+    """Host threads this process may run on (whatever OMP_NUM_THREADS says)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def all_ranks_true(flag: bool, world: int) -> bool:
+    if world == 1:
+        return flag
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
 
 
 def library_int8_context(hb, steps):
@@ -726,49 +851,33 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
     return res
 
 
-def w8a8_large(ops, st, rank, world, steps, warmup):
-    """M=16384, N=28672, K=8192, column-sharded (strong scaling) + optional gather."""
-    import torch
-    import qgemm
-    M, NT, K = 16384, 28672, 8192
-    n0, n1 = qgemm.shard_columns(NT, world, rank, 256)
-    NL = n1 - n0
-    gen = torch.Generator(device="cuda")
-    gen.manual_seed(4321 + rank)
-    A = rand_i8((M, K), gen)          # 134 MB > L2: no rotation needed
-    B = rand_i8((K, NL), gen)
-    sA = rand_u((M,), 0.001, 0.01, gen)
-    sB = rand_u((NL,), 0.001, 0.01, gen)
-    out = torch.empty((M, NL), dtype=torch.bfloat16, device="cuda")
-
-    def step(i):
-        ops.w8a8Gemm(A, B, sA, sB, out, M, NL, K, b_layout=qgemm.B_KN, out_dtype=qgemm.BF16,
-                     algo=qgemm.ALGO_TCGEN05)
-
-    for i in range(warmup):
-        step(i)
-    t_max, t_local = timed(step, steps, world)
-    res = {"M": M, "N": NT, "K": K, "n_local": NL,
-           "value": 2.0 * M * NT * K * steps / t_max / 1e12, "unit": "TOPS",
-           "ms_per_step": t_max / steps * 1e3, "scaling": "strong"}
-    if world > 1:
-        res["allgather"] = gather_output(st, out, rank, world, M, NL, (A, B, sA, sB, K))
-    return res
-
-
-def gather_output(st, out, rank, world, M, NL, gemm):
-    """All-gather of the bf16 output slabs through libqgemm's NCCL communicator,
-    then the [world][M][NL] -> [M][N] unshard kernel; timed separately.  Then the
-    whole sharded layer three ways: the GEMM, the gather and the unshard one after
-    the other on one stream; qgemm_w8a8_gemm_allgather_bf16, which gathers chunk i
-    of M rows on a second stream while the GEMM of chunk i+1 runs; and its window
-    form, where copy-engine copies write each chunk into the peers' outputs."""
+def gather_output(st, lo, rank, world, reps=5):
+    """The whole headline output on every rank, timed apart from the headline: the NCCL
+    all-gather of the bf16 output blocks and the [world][M][NL] -> [M][N] unshard kernel
+    (each alone), then the whole layer (GEMM + gather) three ways: one after the other
+    on one stream; qgemm_w8a8_gemm_allgather_bf16, which gathers chunk i of M rows on a
+    second stream while the GEMM of chunk i+1 runs; and its window form, where copy-engine
+    copies write each chunk into the peers' outputs.  Every form's output equals the
+    serial one, and rank 0 checks sampled full rows of it against the CPU oracle."""
     import ctypes
+    import numpy as np
     import torch
     import torch.distributed as dist
     import qgemm._lib as L
+    from oracle import oracle
     from qgemm import B_KN, BF16
     from qgemm import QuantizedGemmOps as qgemm_ops
+    A, B, sA, sB, out = lo["A"], lo["B"], lo["sA"], lo["sB"], lo["out"]
+    M, NL, K, N = lo["M"], lo["NL"], lo["K"], lo["N"]
+    rows = check_rows(M)
+    expect = None
+    if rank == 0:
+        Bf, sBf = (x.cpu().numpy() for x in weight_columns(0, N, K))
+        ridx = torch.as_tensor(rows, device="cuda")
+        _, expect = oracle.w8a8_gemm_rows(Bf, sBf, A[ridx].cpu().numpy(),
+                                          sA[ridx].cpu().numpy(), want_f32=False,
+                                          threads=host_cores())
+        del Bf, sBf
     uid = ctypes.create_string_buffer(128)
     if rank == 0:
         L.call("qgemm_comm_unique_id", uid)
@@ -777,9 +886,18 @@ def gather_output(st, out, rank, world, M, NL, gemm):
     uid = ctypes.create_string_buffer(obj[0], 128)
     comm = ctypes.c_void_p()
     L.call("qgemm_comm_init", st.dev.handle, uid, rank, world, ctypes.byref(comm))
+    ops = qgemm_ops(st)
+    res = {}
+
+    def oracle_ok(full):
+        if rank != 0:
+            return None
+        got = full[torch.as_tensor(rows, device="cuda")].contiguous().view(torch.int16)
+        return bool(np.array_equal(got.cpu().numpy().view(np.uint16), expect))
+
     try:
         gathered = torch.empty((world, M, NL), dtype=torch.bfloat16, device="cuda")
-        full = torch.empty((M, NL * world), dtype=torch.bfloat16, device="cuda")
+        full = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
 
         def gather(i):
             L.call("qgemm_comm_allgather_bf16", comm, st.handle, out.data_ptr(),
@@ -792,27 +910,26 @@ def gather_output(st, out, rank, world, M, NL, gemm):
         for i in range(2):
             gather(i)
             unshard(i)
-        reps = 5
         tg, _ = timed(gather, reps, world)
         tu, _ = timed(unshard, reps, world)
         recv = (world - 1) * M * NL * 2
-        res = {"ms": tg / reps * 1e3, "recv_GB_s_per_rank": recv / (tg / reps) / 1e9,
-               "unshard_ms": tu / reps * 1e3, "bytes_total": world * M * NL * 2}
-        A, B, sA, sB, K = gemm
-        ops = qgemm_ops(st)
+        res.update({"gather_ms": tg / reps * 1e3, "recv_GB_s_per_rank": recv / (tg / reps) / 1e9,
+                    "unshard_ms": tu / reps * 1e3, "bytes_total": world * M * NL * 2})
 
         def serial(i):
             ops.w8a8Gemm(A, B, sA, sB, out, M, NL, K, b_layout=B_KN, out_dtype=BF16)
             gather(i)
             unshard(i)
 
-        side = torch.cuda.Stream()
-        q_side = st.dev.wrap_stream(side.cuda_stream)
         for i in range(2):
             serial(i)
         ts, _ = timed(serial, reps, world)
-        res["serial_ms"] = ts / reps * 1e3
+        layers = {"serial": ts / reps * 1e3}
         ref = full.clone()
+        checks = {"serial": oracle_ok(full)}
+        equal = {}
+        side = torch.cuda.Stream()
+        q_side = st.dev.wrap_stream(side.cuda_stream)
         for R in (4096, 2048, 1024):
             wb = L.lib().qgemm_w8a8_allgather_work_bytes(world, R, NL)
             work = torch.empty(wb, dtype=torch.uint8, device="cuda")
@@ -826,105 +943,169 @@ def gather_output(st, out, rank, world, M, NL, gemm):
             for i in range(2):
                 piped(i)
             tp, _ = timed(piped, reps, world)
-            res[f"pipelined_ms_rows{R}"] = tp / reps * 1e3
-            res[f"pipelined_equal_rows{R}"] = bool(torch.equal(full, ref))
+            tag = f"nccl_pipelined_rows{R}"
+            layers[tag] = tp / reps * 1e3
+            equal[tag] = bool(torch.equal(full, ref))
+            checks[tag] = oracle_ok(full)
             del work
         # the window form: the copy engines write each finished chunk into the peers'
         # registered output buffers, in the final layout
         win = ctypes.c_void_p()
-        try:  # a refusal here is the same on every rank (the records are gathered first)
+        try:  # a refusal here is the same on every rank (registration agrees before it returns)
             L.call("qgemm_comm_window_register", comm, st.handle, full.data_ptr(),
                    full.numel() * 2, ctypes.byref(win))
         except L.QGemmError as e:
             res["window_error"] = str(e)
-            q_side.destroy()
-            return res
-        try:
-            # the peer copies on one stream (the default), then on one stream per peer
-            for R, ncp in ((4096, None), (2048, None), (1024, None), (4096, world - 1)):
-                def windowed(i):
-                    L.call("qgemm_w8a8_gemm_allgather_window_bf16", win, st.handle,
-                           q_side.handle, A.data_ptr(), B.data_ptr(), B_KN, sA.data_ptr(),
-                           sB.data_ptr(), M, NL, K, R)
+            win = None
+        if win is not None:
+            try:
+                # the peer copies on one stream (the default), then on one stream per peer
+                for R, ncp in ((4096, None), (2048, None), (1024, None), (4096, world - 1)):
+                    def windowed(i):
+                        L.call("qgemm_w8a8_gemm_allgather_window_bf16", win, st.handle,
+                               q_side.handle, A.data_ptr(), B.data_ptr(), B_KN, sA.data_ptr(),
+                               sB.data_ptr(), M, NL, K, R)
 
-                if ncp:
-                    os.environ["QGEMM_COPY_STREAMS"] = str(ncp)
-                full.zero_()
-                for i in range(2):
-                    windowed(i)
-                tw, _ = timed(windowed, reps, world)
-                os.environ.pop("QGEMM_COPY_STREAMS", None)
-                tag = f"rows{R}" + (f"_copy_streams{ncp}" if ncp else "")
-                res[f"window_ms_{tag}"] = tw / reps * 1e3
-                res[f"window_equal_{tag}"] = bool(torch.equal(full, ref))
-        finally:
-            torch.cuda.synchronize()
-            barrier(world)
-            L.call("qgemm_comm_window_release", win)
+                    if ncp:
+                        os.environ["QGEMM_COPY_STREAMS"] = str(ncp)
+                    full.zero_()
+                    for i in range(2):
+                        windowed(i)
+                    tw, _ = timed(windowed, reps, world)
+                    os.environ.pop("QGEMM_COPY_STREAMS", None)
+                    tag = f"window_rows{R}" + (f"_copy_streams{ncp}" if ncp else "")
+                    layers[tag] = tw / reps * 1e3
+                    equal[tag] = bool(torch.equal(full, ref))
+                    checks[tag] = oracle_ok(full)
+            finally:
+                torch.cuda.synchronize()
+                barrier(world)
+                L.call("qgemm_comm_window_release", win)
         q_side.destroy()
+        best = min(layers, key=layers.get)
+        res.update({"layer_ms": layers, "best_layer_form": best,
+                    "best_layer_ms": layers[best],
+                    "best_layer_TOPS": 2.0 * M * N * K / (layers[best] / 1e3) / 1e12,
+                    "equal_to_serial": equal,
+                    "oracle_rows_equal_rank0": checks, "oracle_rows": len(rows),
+                    "layer": "GEMM + all-gather: the whole [M, N] bf16 output on every rank"})
         return res
     finally:
         torch.cuda.synchronize()
         L.call("qgemm_comm_destroy", comm)
 
 
-def cpu_w8a8_sample(target_s: float = 10.0):
-    """The CPU restatement of w8a32Gemm (oracle, OpenMP over all host threads)
-    on a bounded sample of the 4096^3 workload: a row slice, or the whole GEMM
-    repeated, sized to about target_s seconds."""
-    import qgemm.synthetic as syn
+def cpu_legs(threads: int, w8a8_target_s: float = 5.0, single_target_s: float = 2.0,
+             w4_target_s: float = 1.5):
+    """The CPU restatement (oracle/, OpenMP) timed on bounded samples of the workloads:
+    the headline GEMM on a row slice with `threads` threads and with one (extrapolated to
+    the whole GEMM: the per-row work is the same for every row), and the W4A16 decode GEMV
+    at M = 1 (the grouped form of QuantizedGemmOps.scala:229-245) both ways."""
+    import numpy as np
     from oracle import oracle
-    M = N = K = 4096
-    A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=2, sa=(0.001, 0.01), sb=(0.0005, 0.005))
-    threads = oracle.max_threads()
-    t0 = time.perf_counter()
-    oracle.w8a8_gemm_rows(B, sB, A, sA, 0, threads, threads=threads, want_f32=False)
-    per_row = (time.perf_counter() - t0) / threads
-    rows = int(max(threads, min(M, target_s / max(per_row, 1e-9))))
-    rows = min(M, max(threads, rows // threads * threads))
-    reps = 1 if rows < M else max(1, int(round(target_s / (per_row * M))))
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        oracle.w8a8_gemm_rows(B, sB, A, sA, 0, rows, threads=threads, want_f32=False)
-    dt = time.perf_counter() - t0
-    what = (f"rows 0..{rows - 1} of" if rows < M else f"{reps} x the whole")
-    return {"value": 2.0 * rows * N * K * reps / dt / 1e12, "unit": "TOPS", "cores": threads,
-            "kind": "port", "seconds": dt,
-            "sample": f"{what} 4096^3 W8A8 GEMM (bf16 out), {threads} OpenMP threads"}
+    M, N, K = LARGE_M, LARGE_N, LARGE_K
+    rng = np.random.default_rng(2)
+    B = rng.integers(-127, 128, size=(K, N), dtype=np.int8)
+    sB = rng.uniform(0.001, 0.01, size=N).astype(np.float32)
+    x = rng.integers(-127, 128, size=(4 * threads + 64, K), dtype=np.int8)
+    sx = rng.uniform(0.001, 0.01, size=x.shape[0]).astype(np.float32)
+
+    def rows_rate(th, target):
+        # a slice of whole rounds of `th` rows, repeated to fill about `target` seconds
+        rows = max(th, x.shape[0] // th * th)
+        t0 = time.perf_counter()
+        oracle.w8a8_gemm_rows(B, sB, x[:rows], sx[:rows], want_f32=False, threads=th)
+        dt = time.perf_counter() - t0
+        reps = max(1, int(target / max(dt, 1e-9)))
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            oracle.w8a8_gemm_rows(B, sB, x[:rows], sx[:rows], want_f32=False, threads=th)
+        dt = time.perf_counter() - t0
+        return 2.0 * rows * N * K * reps / dt / 1e12, rows, reps, dt
+
+    v_mt, r_mt, n_mt, dt_mt = rows_rate(threads, w8a8_target_s)
+    v_1, r_1, n_1, dt_1 = rows_rate(1, single_target_s)
+    # W4A16 decode GEMV, M = 1, K = 4096, N = 14336, group 128
+    Nw, Kw, G = 14336, 4096, 128
+    import qgemm.synthetic as syn
+    xw, wq, sc = syn.w4a16_inputs(1, Nw, Kw, group=G, seed=3)
+    bytes_alg = Kw * Nw // 2 + (Kw // G) * Nw * 2 + Kw * 2 + Nw * 2
+
+    def w4_rate(th):
+        oracle.w4a16_grouped(wq, sc, 8, G, xw, threads=th)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < w4_target_s or n < 1:
+            oracle.w4a16_grouped(wq, sc, 8, G, xw, threads=th)
+            n += 1
+        dt = time.perf_counter() - t0
+        return bytes_alg * n / dt / 1e9, n
+
+    g_mt, c_mt = w4_rate(threads)
+    g_1, c_1 = w4_rate(1)
+    return {
+        "value": v_mt, "unit": "TOPS", "cores": threads, "kind": "port",
+        "sample": f"{n_mt} x rows 0..{r_mt - 1} of the M=16384 N=28672 K=8192 W8A8 GEMM "
+                  f"(bf16 out), {threads} OpenMP threads, extrapolated to the whole GEMM "
+                  f"at the same per-row rate ({dt_mt:.1f} s timed)",
+        "extrapolated_ms_per_gemm": 2.0 * M * N * K / (v_mt * 1e12) * 1e3,
+        "single_thread": {"value": v_1, "unit": "TOPS", "sample": f"{n_1} x {r_1} rows, "
+                          f"{dt_1:.1f} s timed", "extrapolated_s_per_gemm":
+                          2.0 * M * N * K / (v_1 * 1e12)},
+        "w4a16_decode_M1": {"openmp_GB_s": g_mt, "openmp_calls": c_mt,
+                            "single_thread_GB_s": g_1, "single_thread_calls": c_1,
+                            "bytes_per_call": bytes_alg,
+                            "what": "grouped W4A16 GEMV x bf16 [1, 4096], int4 [4096, 14336], "
+                                    "group 128, zero point 8"},
+        "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+    }
 
 
 def reference_arm(args):
+    """The reference's CPU path for the headline: the C restatement of
+    QuantizedGemmOps.w8a32Gemm (oracle/, the reference's JVM path being absent) on a row
+    slice of the same GEMM per step, all host threads, extrapolated to the whole GEMM.
+    Under torchrun only rank 0 runs it."""
+    import numpy as np
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    W, K = max(args.warmup, 0), max(args.steps, 1)
-    # size one step at ~2 s of CPU work so the whole run stays within minutes
-    cal = cpu_w8a8_sample(target_s=0.5)
-    rows_per_s = cal["value"] * 1e12 / (2.0 * 4096 * 4096)
-    rows = max(1, min(4096, int(rows_per_s * min(2.0, 120.0 / (W + K)))))
-    import qgemm.synthetic as syn
     from oracle import oracle
-    A, B, sA, sB = syn.w8a8_inputs(4096, 4096, 4096, seed=2, sa=(0.001, 0.01), sb=(0.0005, 0.005))
-    threads = oracle.max_threads()
-    for _ in range(W):
-        oracle.w8a8_gemm_rows(B, sB, A, sA, 0, rows, threads=threads, want_f32=False)
+    W, Ksteps = max(args.warmup, 0), max(args.steps, 1)
+    threads = host_cores()
+    M, N, K = LARGE_M, LARGE_N, LARGE_K
+    rng = np.random.default_rng(2)
+    B = rng.integers(-127, 128, size=(K, N), dtype=np.int8)
+    sB = rng.uniform(0.001, 0.01, size=N).astype(np.float32)
+    x = rng.integers(-127, 128, size=(32 * threads, K), dtype=np.int8)
+    sx = rng.uniform(0.001, 0.01, size=x.shape[0]).astype(np.float32)
+    # size one step at <= 2 s of CPU work, so the whole run stays within a few minutes
     t0 = time.perf_counter()
-    for _ in range(K):
-        oracle.w8a8_gemm_rows(B, sB, A, sA, 0, rows, threads=threads, want_f32=False)
+    oracle.w8a8_gemm_rows(B, sB, x[:threads], sx[:threads], want_f32=False, threads=threads)
+    per_round = time.perf_counter() - t0
+    budget = min(2.0, 100.0 / (W + Ksteps))
+    rounds = max(1, min(32, int(budget / max(per_round, 1e-9))))
+    rows = rounds * threads
+    for _ in range(W):
+        oracle.w8a8_gemm_rows(B, sB, x[:rows], sx[:rows], want_f32=False, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(Ksteps):
+        oracle.w8a8_gemm_rows(B, sB, x[:rows], sx[:rows], want_f32=False, threads=threads)
     dt = time.perf_counter() - t0
-    value = 2.0 * rows * 4096 * 4096 * K / dt / 1e12
+    value = 2.0 * rows * N * K * Ksteps / dt / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS",
-        "n_gpus": args.gpus, "steps": K, "warmup": W, "ms_per_step": dt / K * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic",
-        "config": {"workload": "w8a8_gemm M=K=4096 N=4096/GPU bf16 out (CPU restatement)",
-                   "M": 4096, "N": 4096, "K": 4096},
+        "n_gpus": args.gpus, "steps": Ksteps, "warmup": W, "ms_per_step": dt / Ksteps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic", "config": headline_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port",
-                         "sample": f"rows 0..{rows - 1} of the 4096^3 GEMM per step"},
+                         "sample": f"rows 0..{rows - 1} of the M=16384 N=28672 K=8192 GEMM per "
+                                   f"step, {threads} OpenMP threads, extrapolated to the whole "
+                                   f"GEMM at the same per-row rate",
+                         "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference's own path is Scala on the JVM, which is absent and computes only "
-                "element (0,0) per call; its C restatement (oracle/) is timed instead",
+        "note": "the reference's own path is Scala on the JVM, which is absent here and computes "
+                "only element (0,0) per call; its C restatement (oracle/) is timed instead",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -947,118 +1128,156 @@ def main():
     dev = qgemm.Device(local)
     st = dev.wrap_stream(torch.cuda.current_stream().cuda_stream)
     ops = qgemm.QuantizedGemmOps(st)
-    clocks = ClockSampler(local)
     K, W = max(1, args.steps), max(3, args.warmup)
+
+    def finish():
+        st.destroy()
+        dev.close()
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
 
     if args.only == "w4a16":
         log("w4a16 decode (only)")
         r = w4a16_profile(ops, K, W) if args.profile else w4a16_decode(ops, peaks)
         if rank == 0:
             print(json.dumps({"only": "w4a16", "w4a16_decode": r}), flush=True)
+        finish()
         return 0
     if args.only == "side":
         log("side kernels (only)")
         r = side_kernels(st, ops, K, W)
         if rank == 0:
             print(json.dumps({"only": "side", "side_kernels": r}), flush=True)
+        finish()
         return 0
     if args.only == "f32":
         log("fp32 facade (only)")
         r = f32_facade(st, peaks, K)
         if rank == 0:
             print(json.dumps({"only": "f32", "fp32_facade": r}), flush=True)
+        finish()
         return 0
     if args.only == "llama":
         log("llama stack (only)")
         r = llama_stack(ops, peaks)
         if rank == 0:
             print(json.dumps({"only": "llama", "llama2_7b_w4a16_stack": r}), flush=True)
+        finish()
         return 0
-    if args.only == "large":
-        log("w8a8 large (only)")
-        r = w8a8_large(ops, st, rank, world, K, W)
-        if rank == 0:
-            print(json.dumps({"only": "large", "w8a8_large": r}), flush=True)
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-        return 0
-    log("w8a8 headline")
-    hb = w8a8_headline(ops, st, rank, world, K, W, clocks,
-                       sustain=not (args.profile and args.only == "w8a8"))
     if args.only == "w8a8":
+        log("w8a8 4096^3 (only)")
+        if args.profile:
+            import qgemm as _q
+            M = N = Kd = 4096
+            g = torch.Generator(device="cuda")
+            g.manual_seed(1234)
+            A = rand_i8((M, Kd), g)
+            B = rand_i8((Kd, N), g)
+            sA = rand_u((M,), 0.001, 0.01, g)
+            sB = rand_u((N,), 0.0005, 0.005, g)
+            out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+            for _ in range(W + K):
+                ops.w8a8Gemm(A, B, sA, sB, out, M, N, Kd, b_layout=_q.B_KN, out_dtype=_q.BF16,
+                             algo=_q.ALGO_TCGEN05)
+            torch.cuda.synchronize()
+            r = {"launches": W + K}
+        else:
+            hb = w8a8_4096(ops, K, W, ClockSampler(local))
+            r = {"TOPS": hb["TOPS"], "us_per_launch": hb["per_launch_s"] * 1e6}
         if rank == 0:
-            print(json.dumps({"only": "w8a8", "TOPS": hb["value"],
-                              "us_per_launch": hb["per_launch_s"] * 1e6}), flush=True)
+            print(json.dumps({"only": "w8a8", **r}), flush=True)
+        finish()
         return 0
-    int8_peak = 2.0 * peaks["bf16_tflops"]
+
+    clocks_roof = ClockSampler(local)
+    clocks = ClockSampler(local)
+    int8_burst = 2.0 * peaks["bf16_tflops"]
     int8_sustained = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
-    achieved = hb["ops_per_launch"] / hb["per_launch_s"] / 1e12
-    # The timed steps follow one second of back-to-back launches (so that the clock
-    # sampler sees the timed region under load): the kernel runs at sustained clocks
-    # and is set against the sustained peak; the burst fraction is reported beside it.
-    roofline = {"bound": "tensor", "kernel": "w8a8_tcgen05_pair_kernel", "achieved": achieved,
-                "peak": int8_sustained, "unit": "TOPS", "frac": achieved / int8_sustained,
-                "traffic": NCU_TRAFFIC_W8A8_4096,
+
+    # ---- the roofline kernel: the same GEMM kernel at 4096^3, a burst on every rank ----
+    log("w8a8 4096^3 (roofline)")
+    hb = w8a8_4096(ops, K, W, clocks_roof)
+    achieved = hb["TOPS"]
+    roofline = {"bound": "tensor", "kernel": "w8a8_tcgen05_pair_kernel",
+                "shape": "M=N=K=4096 (the prefill-shaped W8A8 GEMM, one GPU), bf16 out, B [K,N]",
+                "achieved": achieved, "peak": int8_burst, "unit": "TOPS",
+                "frac": achieved / int8_burst, "traffic": NCU_TRAFFIC_W8A8_4096,
                 "algorithmic_ops_per_launch": hb["ops_per_launch"],
-                "algorithmic_bytes_per_launch": hb["M"] * hb["K"] + hb["K"] * hb["N"]
-                + 2 * hb["M"] * hb["N"] + 4 * (hb["M"] + hb["N"]),
-                "peak_basis": f"2 x bf16_tflops_sustained ({peak_src}: cuBLAS bf16 back to back "
-                              f"for seconds under the power cap): dense int8 runs at twice the "
-                              f"bf16 rate on B200; the timed steps follow 1 s of sustained load",
-                "burst_peak": int8_peak,
-                "frac_of_burst_peak": achieved / int8_peak}
-    libctx = library_int8_context(hb, K) if rank == 0 else None
-    pipe = w8a8_pipeline(ops, hb, max(10, min(K, 50)), peaks) if rank == 0 else None
+                "algorithmic_bytes_per_launch": 2 * 4096 * 4096 + 2 * 4096 * 4096 + 8 * 4096,
+                "us_per_launch": hb["per_launch_s"] * 1e6, "launches_timed": K,
+                "peak_basis": f"2 x bf16_tflops ({peak_src}: cuBLAS bf16, burst): dense int8 "
+                              f"runs at twice the bf16 rate on B200; the {K} timed launches "
+                              f"are a burst of {K * hb['per_launch_s'] * 1e3:.2f} ms",
+                "clocks": clocks_roof.summary()}
+    w8a8_4096_extra = {"TOPS": achieved}
+    if rank == 0 and world == 1:
+        w8a8_4096_extra["library_context"] = library_int8_context(hb, K)
+        w8a8_4096_extra["w8a8_pipeline_bf16_in"] = w8a8_pipeline(ops, hb, max(10, min(K, 50)),
+                                                                 peaks)
+    for k in ("A", "B", "sA", "sB"):
+        hb.pop(k)
+    torch.cuda.empty_cache()
+
+    # ---- the headline: the column-sharded GEMM, strong scaling ----
+    log("w8a8 column-sharded headline")
+    lo = large_operands(rank, world)
+    hl = headline_large(ops, lo, world, K, W, clocks)
+    rows = check_rows(LARGE_M)
+    parity_ok = all_ranks_true(oracle_rows_check(lo, lo["out"], rows, lo["n0"], lo["n1"],
+                                                 lo["B"].cpu().numpy(), lo["sB"].cpu().numpy()),
+                               world)
+    per_rank_tops = hl["ops_per_rank_launch"] * K / hl["t_local"] / 1e12
+    roofline_headline = {"kernel": "w8a8_tcgen05_pair_kernel",
+                         "shape": f"M={LARGE_M} N={lo['NL']} K={LARGE_K} per rank",
+                         "achieved_per_rank": per_rank_tops, "unit": "TOPS",
+                         "peak_sustained": int8_sustained,
+                         "frac_of_sustained": per_rank_tops / int8_sustained,
+                         "frac_of_burst": per_rank_tops / int8_burst,
+                         "basis": "rank 0's own launches; a step of this size runs long enough "
+                                  "to meet the power cap, so it is set against 2 x the sustained "
+                                  "bf16 rate too"}
     log("e2e")
-    e2e = w8a8_e2e(ops, st, hb, rank, world, max(10, min(K, 50)))
-    extra = {"library_context": libctx} if libctx else {}
-    if pipe:
-        extra["w8a8_pipeline_bf16_in"] = pipe
+    e2e = e2e_large(ops, st, lo, world, max(3, min(K, 10)))
+    extra = {"w8a8_4096": w8a8_4096_extra, "roofline_headline": roofline_headline,
+             "parity": {"oracle_rows_equal_all_ranks": parity_ok, "rows_per_rank": len(rows),
+                        "what": "bf16 outputs of sampled rows (first, second, last and 13 "
+                                "seeded) of every rank's block, bit for bit against the CPU "
+                                "oracle, after the timed region"}}
+    if world > 1:
+        log("all-gather forms")
+        extra["allgather"] = gather_output(st, lo, rank, world)
+    del lo
+    torch.cuda.empty_cache()
     if world == 1 and rank == 0:
         log("w4a16 decode")
         extra["w4a16_decode"] = w4a16_decode(ops, peaks)
         extra["w4a16_decode"]["peak_GB_s"] = peaks["hbm_gbs"]
         extra["w4a16_decode"]["peak_basis"] = f"hbm_gbs ({peak_src})"
         extra["w4a16_decode"]["traffic_M1"] = NCU_TRAFFIC_W4A16_M1
-    for k in ("A", "B", "sA", "sB"):
-        hb.pop(k)
-    torch.cuda.empty_cache()
-    if world == 1 and rank == 0:
+        torch.cuda.empty_cache()
         log("fp32 facade")
         extra["fp32_facade"] = f32_facade(st, peaks)
-    if world == 1 and rank == 0 and not args.no_llama:
-        log("llama stack")
-        extra["llama2_7b_w4a16_stack"] = llama_stack(ops, peaks)
-        torch.cuda.empty_cache()
-    if not args.no_large:
-        log("w8a8 large")
-        extra["w8a8_large"] = w8a8_large(ops, st, rank, world, 10, 3)
+        if not args.no_llama:
+            log("llama stack")
+            extra["llama2_7b_w4a16_stack"] = llama_stack(ops, peaks)
+            torch.cuda.empty_cache()
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
         log("cpu baseline")
-        cpu = cpu_w8a8_sample()
+        cpu = cpu_legs(host_cores())
     if rank == 0:
-        clk = clocks.summary()
         line = {
-            "metric": METRIC, "value": hb["value"], "unit": "TOPS", "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": hb["t_max"] / K * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "w8a8_gemm M=4096 K=4096, 4096 weight columns per GPU "
-                                   "(N=4096*n_gpus), per-token x per-channel fp32 scales, "
-                                   "bf16 out, B in the reference [K,N] layout",
-                       "M": 4096, "N_per_gpu": 4096, "K": 4096, "parallelism": f"col{world}",
-                       "l2": "8 rotating input sets (256 MB) > 126 MB L2"},
-            "roofline": roofline, "e2e": e2e, "gpu_launches": K, "clocks": clk,
+            "metric": METRIC, "value": hl["value"], "unit": "TOPS", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": hl["t_max"] / K * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": headline_config(world),
+            "roofline": roofline, "e2e": e2e, "gpu_launches": K, "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
         line.update(extra)
         print(json.dumps(line), flush=True)
-    st.destroy()
-    dev.close()
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    finish()
     return 0
 
 

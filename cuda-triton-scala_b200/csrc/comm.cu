@@ -207,6 +207,29 @@ qgemm_status qgemm_comm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, uint64_
   return QGEMM_OK;
 }
 
+// After a call has queued its first collective, its peers wait in that collective or
+// the next one for this rank.  A failure after that point aborts the communicator
+// (ncclCommAbort), so that NCCL tears down its side of the connections, and marks it
+// dead: every later call on it returns QGEMM_ERR_BAD_HANDLE.
+static qgemm_status abort_after(qgemm_comm_s* c, qgemm_status st) {
+  NcclApi& n = nccl();
+  if (c->comm && n.CommAbort) n.CommAbort(c->comm);
+  c->comm = nullptr;
+  return st;
+}
+
+// The argument checks of qgemm_w8a8_gemm for the chunks of a sharded call, made before
+// its first collective so that a bad argument fails on the host before any peer waits.
+static qgemm_status check_sharded_gemm(uint64_t A, uint64_t B, int b_layout, uint64_t sA,
+                                       uint64_t sB, int K) {
+  if (b_layout != QGEMM_B_KN && b_layout != QGEMM_B_NK)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad b_layout %d", b_layout);
+  if (!A || !B || !sA || !sB) return fail(QGEMM_ERR_INVALID_ARG, "null operand");
+  if (!aligned(sA, 4) || !aligned(sB, 4)) return fail(QGEMM_ERR_BAD_ALIGN, "sA / sB not 4-byte aligned");
+  if (K < 0) return fail(QGEMM_ERR_INVALID_ARG, "K %d < 0", K);
+  return QGEMM_OK;
+}
+
 // One rank's part of qgemm_comm_window_register, gathered over NCCL.
 struct WindowRecord {
   cudaIpcMemHandle_t handle;  // of the allocation that holds the buffer
@@ -297,17 +320,40 @@ qgemm_status qgemm_comm_window_register(qgemm_comm_t c, qgemm_stream_t s, uint64
   w->bytes = bytes;
   w->sync = dm + rec * world;
   w->peer.assign(world, 0);
-  for (int r = 0; r < world; ++r) {
+  cudaError_t open_err = cudaSuccess;
+  for (int r = 0; r < world && open_err == cudaSuccess; ++r) {
     if (r == c->rank) { w->peer[r] = buf; continue; }
     void* p = nullptr;
-    ce = cudaIpcOpenMemHandle(&p, all[r].handle, cudaIpcMemLazyEnablePeerAccess);
-    if (ce != cudaSuccess) {
-      qgemm_comm_window_release(w);
-      return cuda_fail(ce, "cudaIpcOpenMemHandle");
-    }
+    open_err = cudaIpcOpenMemHandle(&p, all[r].handle, cudaIpcMemLazyEnablePeerAccess);
+    if (open_err != cudaSuccess) break;
     w->opened.push_back(p);
     w->peer[r] = reinterpret_cast<uint64_t>(p) + all[r].offset;
   }
+  cudaGetLastError();
+  // Opening a peer's buffer can fail on one rank only (no peer mapping to one GPU), so
+  // every rank reports how its opens went and all of them reach the same verdict: a
+  // window on every rank, or the same error on every rank.
+  const uint16_t flag = open_err == cudaSuccess ? 0x3F80u : 0u;  // bf16 1.0 or 0
+  std::vector<uint16_t> flags(world, 0);
+  uint8_t* fl = static_cast<uint8_t*>(w->sync);
+  ce = cudaMemcpyAsync(fl + 2 * c->rank, &flag, 2, cudaMemcpyHostToDevice, s->stream);
+  if (ce != cudaSuccess) { qgemm_comm_window_release(w); return abort_after(c, cuda_fail(ce, "cudaMemcpyAsync")); }
+  st = qgemm_comm_allgather_bf16(c, s, reinterpret_cast<uint64_t>(fl + 2 * c->rank),
+                                 reinterpret_cast<uint64_t>(fl), 1);
+  if (st != QGEMM_OK) { qgemm_comm_window_release(w); return abort_after(c, st); }
+  ce = cudaMemcpyAsync(flags.data(), fl, 2 * world, cudaMemcpyDeviceToHost, s->stream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(s->stream);
+  if (ce != cudaSuccess) {
+    qgemm_comm_window_release(w);
+    return abort_after(c, cuda_fail(ce, "gathering the window open results"));
+  }
+  for (int r = 0; r < world; ++r)
+    if (flags[r] != 0x3F80u) {
+      qgemm_comm_window_release(w);
+      if (r == c->rank) return cuda_fail(open_err, "cudaIpcOpenMemHandle");
+      return fail(QGEMM_ERR_CUDA, "rank %d could not map a peer's buffer (CUDA IPC); no rank "
+                  "keeps the window", r);
+    }
   *out = w;
   return QGEMM_OK;
 }
@@ -354,6 +400,7 @@ qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_strea
     return fail(QGEMM_ERR_INVALID_ARG, "the window holds %zu bytes; [%d, %zu] bf16 needs %zu",
                 w->bytes, M, N, (size_t)M * N * 2);
   if (M == 0 || N_local == 0) return QGEMM_OK;
+  if ((st = check_sharded_gemm(A, B, b_layout, sA, sB, K)) != QGEMM_OK) return st;
   for (cudaEvent_t* e : {&c->ev_gemm[0], &c->ev_gemm[1], &c->ev_end, &c->ev_start, &c->ev_open})
     if (!*e) {
       cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
@@ -374,11 +421,12 @@ qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_strea
   cudaError_t ce = cudaEventRecord(c->ev_start, s->stream);
   if (ce == cudaSuccess) ce = cudaStreamWaitEvent(cs->stream, c->ev_start, 0);
   if (ce != cudaSuccess) return cuda_fail(ce, "ordering the copy stream after the caller's work");
-  if ((st = window_barrier(w, cs)) != QGEMM_OK) return st;
+  if ((st = window_barrier(w, cs)) != QGEMM_OK) return abort_after(c, st);
+  // from here on every failure aborts the communicator (abort_after)
   ce = cudaEventRecord(c->ev_open, cs->stream);
   for (int k = 0; k < ncp && ce == cudaSuccess; ++k)
     ce = cudaStreamWaitEvent(c->cp[k], c->ev_open, 0);
-  if (ce != cudaSuccess) return cuda_fail(ce, "ordering the copies after the barrier");
+  if (ce != cudaSuccess) return abort_after(c, cuda_fail(ce, "ordering the copies after the barrier"));
   const int R = chunk_rows < M ? chunk_rows : M;
   const size_t pitch = N * 2, width = (size_t)N_local * 2;
   for (int m0 = 0, i = 0; m0 < M; m0 += R, ++i) {
@@ -387,30 +435,30 @@ qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_strea
     st = qgemm_w8a8_gemm(s, A + (uint64_t)m0 * K, B, b_layout, sA + (uint64_t)m0 * 4, sB,
                          w->local + off, QGEMM_BF16, (int)N, rows, N_local, K, 0,
                          QGEMM_ALGO_AUTO);
-    if (st != QGEMM_OK) return st;
+    if (st != QGEMM_OK) return abort_after(c, st);
     cudaEvent_t ev = c->ev_gemm[i & 1];
     if ((ce = cudaEventRecord(ev, s->stream)) != cudaSuccess)
-      return cuda_fail(ce, "cudaEventRecord");
+      return abort_after(c, cuda_fail(ce, "cudaEventRecord"));
     for (int k = 0; k < ncp; ++k)
       if ((ce = cudaStreamWaitEvent(c->cp[k], ev, 0)) != cudaSuccess)
-        return cuda_fail(ce, "event between the GEMM and the copies");
+        return abort_after(c, cuda_fail(ce, "event between the GEMM and the copies"));
     for (int j = 1; j < world; ++j) {  // peers in rank order from this rank's right
       const int p = (rank + j) % world;
       ce = cudaMemcpy2DAsync(reinterpret_cast<void*>(w->peer[p] + off), pitch,
                              reinterpret_cast<const void*>(w->local + off), pitch, width, rows,
                              cudaMemcpyDeviceToDevice, c->cp[(j - 1) % ncp]);
-      if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemcpy2DAsync to a peer");
+      if (ce != cudaSuccess) return abort_after(c, cuda_fail(ce, "cudaMemcpy2DAsync to a peer"));
     }
   }
   for (int k = 0; k < ncp; ++k)
     if ((ce = cudaEventRecord(c->ev_cp[k], c->cp[k])) != cudaSuccess ||
         (ce = cudaStreamWaitEvent(cs->stream, c->ev_cp[k], 0)) != cudaSuccess)
-      return cuda_fail(ce, "joining the copy streams");
+      return abort_after(c, cuda_fail(ce, "joining the copy streams"));
   // every peer's columns have landed here once every rank has finished its copies
-  if ((st = window_barrier(w, cs)) != QGEMM_OK) return st;
+  if ((st = window_barrier(w, cs)) != QGEMM_OK) return abort_after(c, st);
   ce = cudaEventRecord(c->ev_end, cs->stream);
   if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s->stream, c->ev_end, 0);
-  if (ce != cudaSuccess) return cuda_fail(ce, "joining the copy stream");
+  if (ce != cudaSuccess) return abort_after(c, cuda_fail(ce, "joining the copy stream"));
   return QGEMM_OK;
 }
 
@@ -442,6 +490,8 @@ qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, qg
   if (!work || work_bytes < need)
     return fail(QGEMM_ERR_INVALID_ARG, "work buffer of %zu bytes; %zu needed", work_bytes, need);
   if (!aligned(work, 16)) return fail(QGEMM_ERR_BAD_ALIGN, "work must be 16-byte aligned");
+  if (!out) return fail(QGEMM_ERR_INVALID_ARG, "out is null");
+  if ((st = check_sharded_gemm(A, B, b_layout, sA, sB, K)) != QGEMM_OK) return st;
   for (cudaEvent_t* e : {&c->ev_gemm[0], &c->ev_gemm[1], &c->ev_done[0], &c->ev_done[1], &c->ev_end})
     if (!*e) {
       cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
@@ -450,6 +500,10 @@ qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, qg
   const size_t slot_bytes = (size_t)world * R * N_local * 2;
   const int N = N_local * world;
   const int nchunks = (M + R - 1) / R;
+  // Failures before the first gather is queued return on this rank alone (no peer waits
+  // yet); after it they abort the communicator (abort_after).
+  bool queued = false;
+  auto bail = [&](qgemm_status e) { return queued ? abort_after(c, e) : e; };
   for (int i = 0; i < nchunks; ++i) {
     const int b = i & 1, m0 = i * R, rows = (M - m0) < R ? (M - m0) : R;
     const uint64_t buf = work + (uint64_t)b * slot_bytes;  // [world][rows][N_local]
@@ -457,23 +511,24 @@ qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t c, qgemm_stream_t s, qg
     const uint64_t mine = buf + (uint64_t)rank * blk * 2;
     cudaError_t ce = cudaSuccess;
     if (i >= 2) ce = cudaStreamWaitEvent(s->stream, c->ev_done[b], 0);  // chunk i-2 let go of buf
-    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamWaitEvent");
+    if (ce != cudaSuccess) return bail(cuda_fail(ce, "cudaStreamWaitEvent"));
     st = qgemm_w8a8_gemm(s, A + (uint64_t)m0 * K, B, b_layout, sA + (uint64_t)m0 * 4, sB, mine,
                          QGEMM_BF16, N_local, rows, N_local, K, 0, QGEMM_ALGO_AUTO);
-    if (st != QGEMM_OK) return st;
+    if (st != QGEMM_OK) return bail(st);
     if ((ce = cudaEventRecord(c->ev_gemm[b], s->stream)) != cudaSuccess ||
         (ce = cudaStreamWaitEvent(cs->stream, c->ev_gemm[b], 0)) != cudaSuccess)
-      return cuda_fail(ce, "event between the GEMM and the gather");
+      return bail(cuda_fail(ce, "event between the GEMM and the gather"));
     st = qgemm_comm_allgather_bf16(c, cs, mine, buf, blk);  // in place
-    if (st != QGEMM_OK) return st;
+    queued = true;
+    if (st != QGEMM_OK) return bail(st);
     st = qgemm_unshard_columns_bf16(cs, buf, out + (uint64_t)m0 * N * 2, world, rows, N_local);
-    if (st != QGEMM_OK) return st;
+    if (st != QGEMM_OK) return bail(st);
     if ((ce = cudaEventRecord(c->ev_done[b], cs->stream)) != cudaSuccess)
-      return cuda_fail(ce, "cudaEventRecord");
+      return bail(cuda_fail(ce, "cudaEventRecord"));
   }
   cudaError_t ce = cudaEventRecord(c->ev_end, cs->stream);
   if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s->stream, c->ev_end, 0);
-  if (ce != cudaSuccess) return cuda_fail(ce, "joining the gather stream");
+  if (ce != cudaSuccess) return bail(cuda_fail(ce, "joining the gather stream"));
   return QGEMM_OK;
 }
 

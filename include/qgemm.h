@@ -468,7 +468,12 @@ QGEMM_API qgemm_status qgemm_unshard_columns_bf16(qgemm_stream_t s, uint64_t gat
  * aligned (two chunks of gather buffers).  s and cs must differ; when the call
  * returns, s is ordered after all of its work (cs too has finished it).  The events it
  * needs are made on the communicator's first call.  Every rank must make the same
- * calls in the same order. */
+ * calls in the same order, with the same M, N_local, K and chunk_rows: equal shards, so
+ * N a multiple of align * world in qgemm_shard_columns.  NCCL requires equal counts and
+ * a mismatch is not detected.  Argument errors are returned before the call queues its
+ * first collective, on the rank that made them; a failure after that point aborts the
+ * communicator (ncclCommAbort) and every later call on it returns
+ * QGEMM_ERR_BAD_HANDLE, so that no rank goes on as if the step had completed. */
 QGEMM_API size_t qgemm_w8a8_allgather_work_bytes(int world, int chunk_rows, int n_local);
 QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t comm, qgemm_stream_t s,
                                                       qgemm_stream_t cs, uint64_t A, uint64_t B,
@@ -482,7 +487,10 @@ QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_bf16(qgemm_comm_t comm, qgemm_s
  * 16-byte aligned.  Each rank maps the peers' buffers into its own address space (CUDA
  * IPC), so one process per GPU; one window per allocation at a time.  `s` carries the
  * exchange and is synchronised.  Release a window (a local call) after the work that
- * uses it has finished on every rank and before qgemm_comm_destroy. */
+ * uses it has finished on every rank and before qgemm_comm_destroy.  Every rank returns
+ * the same verdict: the buffers are checked on every rank and the results gathered
+ * before any rank maps its peers' buffers, and the mapping results are gathered again
+ * before any rank keeps the window. */
 QGEMM_API qgemm_status qgemm_comm_window_register(qgemm_comm_t comm, qgemm_stream_t s,
                                                   uint64_t buf, size_t bytes,
                                                   qgemm_window_t* out);
@@ -497,7 +505,9 @@ QGEMM_API qgemm_status qgemm_comm_window_release(qgemm_window_t w);
  * land in the final layout.  Two barriers on cs (one-element NCCL gathers) bracket
  * the copies: no rank writes into a peer's window before the peer has finished its
  * earlier work on s, and the call completes on s only when every peer's columns have
- * arrived.  Every rank must make the same calls in the same order. */
+ * arrived.  Every rank must make the same calls in the same order, with the same M,
+ * N_local, K and chunk_rows (equal shards); a mismatch is not detected (the window's
+ * size bounds every copy).  Errors behave as in qgemm_w8a8_gemm_allgather_bf16. */
 QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_stream_t s,
                                                              qgemm_stream_t cs, uint64_t A,
                                                              uint64_t B, int b_layout,

@@ -116,3 +116,52 @@ def test_dead_rank_surfaces_as_error():
         p.join(timeout=30)
         if p.is_alive():
             p.kill()
+
+
+def _failing_step_worker(rank, world, port, q):
+    """Two steps of the sharded layer's host loop (a collective per step).  Rank 1's
+    second step fails on the host before its collective (a stand-in for a failed launch)
+    and the rank stays alive without joining; rank 0 must get an error from its
+    collective within the process group's timeout, not wait for good."""
+    import datetime
+    import time
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=4))
+    t = torch.ones(8)
+    dist.all_reduce(t)  # step 1 completes on both ranks
+    if rank == 1:
+        try:
+            raise RuntimeError("launch failed")  # step 2 fails on the host
+        except RuntimeError as e:
+            q.put((rank, f"own error: {e}"))
+        time.sleep(12)  # alive, never joins the collective
+        os._exit(0)
+    t0 = time.time()
+    try:
+        dist.all_reduce(t)
+        q.put((rank, "no error", time.time() - t0))
+    except Exception as e:
+        q.put((rank, type(e).__name__, time.time() - t0))
+
+
+def test_rank_failing_between_steps_surfaces_as_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_step_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        item = q.get(timeout=120)
+        got[item[0]] = item[1:]
+    assert got[1][0].startswith("own error")
+    what, waited = got[0]
+    assert what != "no error" and waited < 60
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
