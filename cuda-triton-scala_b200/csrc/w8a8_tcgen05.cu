@@ -103,14 +103,6 @@ struct Params {
   int split_w, split_s;
   int32_t* part;   // [(tail tile * 2 + rank) * split_s + part][128 x 256 words, part_index]
   int* cnt;        // [tail tile * 2 + rank], zero between launches
-  // Stream-K tail (sk = 1; then split_s = 2): the first split_w tiles go round robin as
-  // whole tiles; the k-blocks of the remaining tiles, taken in order, are cut into one
-  // equal range per pair.  A range that ends inside a tile does that tile's first
-  // k-blocks first (part 0: its partial sums go to slot tt = next pair), then its whole
-  // tiles, then the last k-blocks of the tile it shares with the previous pair (part 1:
-  // adds the previous pair's partial, which was written long before, and stores the
-  // tile).  Slots and counters are indexed by the finishing pair: tt = pair * 2 + rank.
-  int sk;
   // int32 accumulator output: row pitch acc_ld (elements); when acc_c is set, c[m, n]
   // (row pitch acc_c_ld) is added to each sum before it is stored (int32, wrapping).
   int acc_ld;
@@ -124,48 +116,12 @@ struct Params {
   int hold_split;
 };
 
-// Work item i of pair `pair`: a whole tile, or one K part of a tail tile; `tt` is the
-// split slot of a part.  Returns false when the pair has no item i.
+// Work item i of pair `pair`: a whole tile, or one K part of a tail tile.  Returns
+// false when the pair has no item i.
 __device__ __forceinline__ bool pair_item(const Params& p, int pair, int npairs, int i,
-                                          int& tile, int& kb0, int& kb1, int& part, int& tt) {
+                                          int& tile, int& kb0, int& kb1, int& part) {
   const int T = p.num_m_blocks * p.num_n_blocks;
   const int rounds = p.split_w / npairs;  // split_w is a multiple of npairs when splitting
-  if (p.sk && i >= rounds) {
-    const int KB = p.num_k_blocks;
-    const long long U = (long long)(T - p.split_w) * KB;
-    const long long u0 = U * pair / npairs, u1 = U * (pair + 1) / npairs;
-    int idx = i - rounds;
-    const int head = (int)(u1 % KB);  // the range ends inside tile u1 / KB
-    if (head != 0) {
-      if (idx == 0) {
-        tile = p.split_w + (int)(u1 / KB);
-        kb0 = 0;
-        kb1 = head;
-        part = 0;
-        tt = pair + 1;
-        return true;
-      }
-      --idx;
-    }
-    const long long w0 = (u0 + KB - 1) / KB, w1 = u1 / KB;  // whole tiles [w0, w1)
-    if (idx < w1 - w0) {
-      tile = p.split_w + (int)(w0 + idx);
-      kb0 = 0;
-      kb1 = KB;
-      part = -1;
-      return true;
-    }
-    idx -= (int)(w1 - w0);
-    if (idx == 0 && u0 % KB != 0) {  // the range starts inside tile u0 / KB
-      tile = p.split_w + (int)(u0 / KB);
-      kb0 = (int)(u0 % KB);
-      kb1 = KB;
-      part = 1;
-      tt = pair;
-      return true;
-    }
-    return false;
-  }
   if (p.split_s <= 1 || i < rounds) {
     tile = pair + i * npairs;
     if (tile >= (p.split_s <= 1 ? T : p.split_w)) return false;
@@ -177,7 +133,6 @@ __device__ __forceinline__ bool pair_item(const Params& p, int pair, int npairs,
   if (i > rounds || pair >= (T - p.split_w) * p.split_s) return false;
   tile = p.split_w + pair / p.split_s;
   part = pair % p.split_s;
-  tt = tile - p.split_w;
   kb0 = (int)((long long)p.num_k_blocks * part / p.split_s);
   kb1 = (int)((long long)p.num_k_blocks * (part + 1) / p.split_s);
   return true;
@@ -750,9 +705,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      int tile, kb0, kb1, part, tt_base;
-      for (int item = 0; ok && pair_item(p, pair_id, npairs, item, tile, kb0, kb1, part, tt_base);
-           ++item) {
+      int tile, kb0, kb1, part;
+      for (int item = 0; ok && pair_item(p, pair_id, npairs, item, tile, kb0, kb1, part); ++item) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -797,8 +751,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       bool issued_any = false;
-      int tile, kb0, kb1, part, tt_base;
-      for (; ok && pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part, tt_base); ++it) {
+      int tile, kb0, kb1, part;
+      for (; ok && pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part); ++it) {
         const int a = it & 1;
         const uint32_t aphase = (uint32_t)((it >> 1) & 1);
         if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag, p.wait_ns)) {
@@ -853,8 +807,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     volatile int* last_flag = abort_flag + 1;
     const int rl = q * 32 + lane;  // row of this CTA's half-tile
     int it = 0;
-    int tile, kb0, kb1, part, tt_base = 0;
-    for (; pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part, tt_base); ++it) {
+    int tile, kb0, kb1, part;
+    for (; pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part); ++it) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int a = it & 1;
@@ -876,11 +830,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       // others have counted in, adds their partials to its own accumulator in TMEM and
       // stores the tile; it neither writes nor re-reads a partial of its own.
       const size_t slot_ints = (size_t)128 * 256;
-      const int tt = tt_base * 2 + (int)rank;
-      // stream-K keeps one slot per split tile (its one writing part)
-      const size_t slot0 = p.sk ? (size_t)tt : (size_t)tt * p.split_s;
+      const int tt = (tile - p.split_w) * 2 + (int)rank;
       if (part < p.split_s - 1) {
-        int4* mine = reinterpret_cast<int4*>(p.part + (slot0 + part) * slot_ints);
+        int4* mine = reinterpret_cast<int4*>(p.part + ((size_t)tt * p.split_s + part) * slot_ints);
 #pragma unroll 1
         for (int c = 0; c < 256 / 32; ++c) {
           uint32_t r[32];
@@ -906,9 +858,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       if (elected) {
         // bounded wait for the other parts' count-ins.  They run on lower-numbered pairs
-        // (pair = tail tile * split_s + part; with stream-K the previous pair, as the first
-        // item of its tail), which are dispatched before this one, and wait on nothing: a
-        // resident final part never waits on a part that cannot run.
+        // (pair = tail tile * split_s + part), which are dispatched before this one, and
+        // wait on nothing: a resident final part never waits on a part that cannot run.
         bool got = false;
         const unsigned long long t0 = ptx::globaltimer();
         for (;;) {
@@ -923,7 +874,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const bool ready = ok && *last_flag != 0;
       epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM + (int)rank * 128,
                     nb * BN, stg_base, elected, chunk_seq, ready,
-                    p.part + slot0 * slot_ints, p.split_s - 1, slot_ints, true);
+                    p.part + (size_t)tt * p.split_s * slot_ints, p.split_s - 1, slot_ints, true);
       ptx::tc_fence_before();
       ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
       if (elected) p.cnt[tt] = 0;
@@ -1000,7 +951,6 @@ struct TcPlan {
   int grid;
   int num_tiles;
   int split_w, split_s;   // as in Params; split_s = 1: no split
-  int sk;                 // stream-K tail (Params::sk)
   size_t cnt_bytes;       // counter block at the start of the scratch
   size_t part_bytes;      // partial tiles after it (0: no split)
 };
@@ -1020,7 +970,6 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, b
   t.num_tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
   t.split_w = t.num_tiles;
   t.split_s = 1;
-  t.sk = 0;
   // The counter block has one fixed size on a device (counters for up to
   // 2 * max_pairs half-tiles; rest < max_pairs) and is counted in every plan, so that
   // callers which carve their own buffers out of the stream's scratch never place them
@@ -1058,19 +1007,6 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, b
   // adding the others' partials in TMEM (4096^3: 2295 against 2511; 4096x4096x2048:
   // 1494 against 1825).
   const int rounds = t.num_tiles / pairs, rest = t.num_tiles - rounds * pairs;
-  // Stream-K tail: when the last round would leave more than 3 % of the pair-rounds
-  // idle and more than a quarter of the pairs busy, the last rounds (one full round and
-  // the leftover tiles, so that every pair's range covers at least one whole tile's
-  // k-blocks) are cut into equal k-block ranges, one per pair.  The whole-tile rounds
-  // before them keep the raster order that makes concurrent tiles share A and B in L2.
-  if (rounds >= 1 && rest * 4 > pairs && num_k_blocks >= 2 &&
-      (double)t.num_tiles / ((double)(rounds + 1) * pairs) < 0.97) {
-    t.sk = 1;
-    t.split_w = (rounds - 1) * pairs;
-    t.split_s = 2;
-    t.part_bytes = (size_t)pairs * 2 * 128 * 256 * sizeof(int32_t);
-    return t;
-  }
   int parts = (rest > 0 && rest * 4 <= pairs) ? 4 : 1;
   while (parts > 1 && num_k_blocks / parts < 2) --parts;
   if (parts < 4) parts = 1;
@@ -1173,7 +1109,6 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   }
   p.split_w = t.num_tiles;
   p.split_s = 1;
-  p.sk = 0;
   p.part = nullptr;
   p.cnt = nullptr;
   if (t.split_s > 1) {
@@ -1191,7 +1126,6 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
     if (ws) {
       p.split_w = t.split_w;
       p.split_s = t.split_s;
-      p.sk = t.sk;
       p.cnt = static_cast<int*>(ws);
       p.part = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + t.cnt_bytes);
     }
