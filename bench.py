@@ -73,9 +73,11 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-llama", action="store_true", help="skip the Llama-shaped W4A16 stack")
-    p.add_argument("--only", choices=["all", "w8a8", "w4a16", "llama", "f32", "side"],
+    p.add_argument("--only", choices=["all", "w8a8", "large", "w4a16", "llama", "f32", "side"],
                    default="all",
                    help="run one workload alone (for profiling); prints its own JSON line")
+    p.add_argument("--as-world", type=int, default=1,
+                   help="with --only large: run rank 0's shard of a W-GPU job on this GPU")
     p.add_argument("--profile", action="store_true",
                    help="with --only w8a8|w4a16: warmup + steps plain launches and nothing "
                         "else (no clock warm-up, no graphs), for ncu captures")
@@ -1163,6 +1165,26 @@ def main():
         r = llama_stack(ops, peaks)
         if rank == 0:
             print(json.dumps({"only": "llama", "llama2_7b_w4a16_stack": r}), flush=True)
+        finish()
+        return 0
+    if args.only == "large":
+        W_as = max(1, args.as_world)
+        log(f"column-sharded headline GEMM, rank 0 of {W_as} (only)")
+        lo = large_operands(0, W_as)
+        if args.profile:
+            for i in range(W + K):
+                ops.w8a8Gemm(lo["A"], lo["B"], lo["sA"], lo["sB"], lo["out"], lo["M"], lo["NL"],
+                             lo["K"], b_layout=qgemm.B_KN, out_dtype=qgemm.BF16,
+                             algo=qgemm.ALGO_TCGEN05)
+            torch.cuda.synchronize()
+            r = {"launches": W + K, "shape": [lo["M"], lo["NL"], lo["K"]]}
+        else:
+            hl = headline_large(ops, lo, 1, K, W, ClockSampler(local))
+            r = {"shape": [lo["M"], lo["NL"], lo["K"]],
+                 "TOPS_this_gpu": hl["ops_per_rank_launch"] * K / hl["t_local"] / 1e12,
+                 "ms_per_launch": hl["t_local"] / K * 1e3}
+        if rank == 0:
+            print(json.dumps({"only": "large", **r}), flush=True)
         finish()
         return 0
     if args.only == "w8a8":
