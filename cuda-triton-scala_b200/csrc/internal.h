@@ -177,13 +177,20 @@ bool w4a16_frag_supported(const qgemm_device_s* d, uint64_t x, uint64_t wf, uint
 qgemm_status launch_w4a16_frag(qgemm_stream_s* s, const void* x, const void* wf, const void* sc,
                                int zp, int G, void* y, int M, int N, int K);
 size_t w4_frag_bytes(int K, int N);
+// The K-split cluster kernel on the same fragment-ordered weights (w4a16_frag_cluster.cu):
+// up to 32 activation rows per pass, K up to 16384; needs N % 16 == 0.
+bool w4a16_frag_cluster_fits(int N, int K);
+qgemm_status launch_w4a16_frag_cluster(qgemm_stream_s* s, const void* x, const void* wf,
+                                       const void* sc, int zp, int G, void* y, int M, int N,
+                                       int K);
 qgemm_status launch_prepack_w4_frag(qgemm_stream_s* s, const uint32_t* src, uint32_t* dst, int K,
                                     int N);
-size_t w4a16_prefill_workspace_bytes(int K, int N);
+// terms: bf16 values per expanded weight (2: exact hi + lo, 1: bf16((q - zp) * s))
+size_t w4a16_prefill_workspace_bytes(int K, int N, int terms);
 // frag: wt is in the fragment order of qgemm_prepack_w4_frag instead of 64-column tiles
 qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
                                   const void* scales, int zp, int G, void* y, int M, int N,
-                                  int K, void* ws, size_t ws_bytes, bool frag);
+                                  int K, void* ws, size_t ws_bytes, bool frag, int terms);
 qgemm_status launch_w4a16_grouped(qgemm_stream_s* s, const void* x, const uint32_t* wq,
                                   const void* scales, int zp, int group, void* y, int M,
                                   int N, int K);

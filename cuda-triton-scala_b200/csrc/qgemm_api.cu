@@ -550,13 +550,23 @@ qgemm_status qgemm_w4a16_grouped_gemm_frag(qgemm_stream_t s, uint64_t x, uint64_
 qgemm_status qgemm_w4a16_prefill_workspace_bytes(int K, int N, size_t* bytes) {
   if (!bytes) return fail(QGEMM_ERR_INVALID_ARG, "bytes is null");
   if (K < 0 || N < 0) return fail(QGEMM_ERR_INVALID_ARG, "negative size K=%d N=%d", K, N);
-  *bytes = w4a16_prefill_workspace_bytes(K, N);
+  *bytes = w4a16_prefill_workspace_bytes(K, N, 2);
+  return QGEMM_OK;
+}
+
+qgemm_status qgemm_w4a16_prefill_workspace_bytes_ex(int K, int N, int flags, size_t* bytes) {
+  if (!bytes) return fail(QGEMM_ERR_INVALID_ARG, "bytes is null");
+  if (K < 0 || N < 0) return fail(QGEMM_ERR_INVALID_ARG, "negative size K=%d N=%d", K, N);
+  if (flags & ~(QGEMM_PREFILL_FRAG | QGEMM_PREFILL_ONE_TERM))
+    return fail(QGEMM_ERR_INVALID_ARG, "unknown prefill flags 0x%x", flags);
+  *bytes = w4a16_prefill_workspace_bytes(K, N, (flags & QGEMM_PREFILL_ONE_TERM) ? 1 : 2);
   return QGEMM_OK;
 }
 
 static qgemm_status prefill_entry(qgemm_stream_t s, uint64_t x, uint64_t wt, uint64_t scales,
                                   int zero_point, int group_size, uint64_t y, int M, int N,
-                                  int K, uint64_t workspace, size_t workspace_bytes, bool frag) {
+                                  int K, uint64_t workspace, size_t workspace_bytes, bool frag,
+                                  int terms) {
   QG_TRY(enter(s));
   QG_TRY(check_dims(M, N, K));
   if (group_size <= 0) return fail(QGEMM_ERR_INVALID_ARG, "group_size %d <= 0", group_size);
@@ -582,7 +592,7 @@ static qgemm_status prefill_entry(qgemm_stream_t s, uint64_t x, uint64_t wt, uin
                               reinterpret_cast<const uint8_t*>(wt),
                               reinterpret_cast<const void*>(scales), zero_point, group_size,
                               reinterpret_cast<void*>(y), M, N, K,
-                              reinterpret_cast<void*>(workspace), workspace_bytes, frag);
+                              reinterpret_cast<void*>(workspace), workspace_bytes, frag, terms);
 }
 
 qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint64_t wt,
@@ -590,7 +600,7 @@ qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint
                                               uint64_t y, int M, int N, int K, uint64_t workspace,
                                               size_t workspace_bytes) {
   return prefill_entry(s, x, wt, scales, zero_point, group_size, y, M, N, K, workspace,
-                       workspace_bytes, false);
+                       workspace_bytes, false, 2);
 }
 
 qgemm_status qgemm_w4a16_grouped_gemm_prefill_frag(qgemm_stream_t s, uint64_t x, uint64_t wf,
@@ -599,7 +609,19 @@ qgemm_status qgemm_w4a16_grouped_gemm_prefill_frag(qgemm_stream_t s, uint64_t x,
                                                    int K, uint64_t workspace,
                                                    size_t workspace_bytes) {
   return prefill_entry(s, x, wf, scales, zero_point, group_size, y, M, N, K, workspace,
-                       workspace_bytes, true);
+                       workspace_bytes, true, 2);
+}
+
+qgemm_status qgemm_w4a16_grouped_gemm_prefill_ex(qgemm_stream_t s, uint64_t x, uint64_t w,
+                                                 uint64_t scales, int zero_point, int group_size,
+                                                 uint64_t y, int M, int N, int K,
+                                                 uint64_t workspace, size_t workspace_bytes,
+                                                 int flags) {
+  if (flags & ~(QGEMM_PREFILL_FRAG | QGEMM_PREFILL_ONE_TERM))
+    return fail(QGEMM_ERR_INVALID_ARG, "unknown prefill flags 0x%x", flags);
+  return prefill_entry(s, x, w, scales, zero_point, group_size, y, M, N, K, workspace,
+                       workspace_bytes, (flags & QGEMM_PREFILL_FRAG) != 0,
+                       (flags & QGEMM_PREFILL_ONE_TERM) ? 1 : 2);
 }
 
 qgemm_status qgemm_gemm_bf16_nk(qgemm_stream_t s, uint64_t A, uint64_t B, uint64_t out, int ldc,

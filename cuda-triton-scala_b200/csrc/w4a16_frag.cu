@@ -591,7 +591,8 @@ bool w4a16_frag_supported(const qgemm_device_s* d, uint64_t x, uint64_t wf, uint
   if (K % 16 != 0) return no("K must be a multiple of 16");
   if (!(G == 32 || G == 64 || G % 128 == 0)) return no("group_size must be 32, 64 or a multiple of 128");
   if (N % 8 != 0) return no("N must be a multiple of 8");
-  if (w4f::kbw_for(K) == 0) return no("K must be at most 8192");
+  if (w4f::kbw_for(K) == 0 && !w4a16_frag_cluster_fits(N, K))
+    return no("K must be at most 8192, or at most 16384 with N a multiple of 16");
   if (!aligned(x, 16) || !aligned(wf, 16) || !aligned(sc, 16))
     return no("x, weights and scales must be 16-byte aligned");
   (void)M;
@@ -620,6 +621,10 @@ qgemm_status launch_w4a16_frag(qgemm_stream_s* s, const void* x, const void* wf,
     while (want > 1 && smem_of(want) > d->smem_optin) --want;
     return want;
   };
+  // 17 to 32 rows a pass, or K past the register-resident kernels' limit: the K-split
+  // cluster kernel (w4a16_frag_cluster.cu) reads the weights once per 32 rows
+  if (w4a16_frag_cluster_fits(N, K) && (M > 16 || kbw == 0 || (M > MP && kbw > 2)))
+    return launch_w4a16_frag_cluster(s, x, wf, sc, zp, G, y, M, N, K);
   if (M > MP && N % 16 == 0 && kbw <= 2) {
     // more than 4 rows: 16-row passes on column pairs (weights read once per 16 rows)
     const int NP = N / 16;

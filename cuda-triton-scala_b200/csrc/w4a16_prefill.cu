@@ -10,13 +10,19 @@
 // activations by it, and the next slab follows.
 //
 // Exactness: w = (q - zp) * s has up to 12 significant bits (a 4-bit integer times an
-// 8-bit bf16 significand), more than bf16 holds.  Each weight is therefore written as
-// two bf16 values, hi = bf16(w) and lo = w - hi (exact: at most 4 bits remain), in two
-// K-blocks of the same slab row, and the GEMM reads the activations twice along K:
-//     y = x * hi^T + x * lo^T,  with exact products and fp32 sums,
-// so the only roundings are those of the fp32 accumulation and of the bf16 output,
-// as on the decode path.  This doubles the tensor work; the expansion itself costs
-// 4.5 bytes of HBM traffic per weight against 4 * M multiply-adds.
+// 8-bit bf16 significand), more than bf16 holds.  Two expansions:
+//   * exact (two terms, the default): each weight is written as two bf16 values,
+//     hi = bf16(w) and lo = w - hi (exact: at most 4 bits remain), in two K-blocks of
+//     the same slab row, and the GEMM reads the activations twice along K:
+//         y = x * hi^T + x * lo^T,  with exact products and fp32 sums,
+//     so the only roundings are those of the fp32 accumulation and of the bf16 output,
+//     as on the decode path.  This doubles the tensor work.
+//   * one term: the slab holds hi = bf16(w) alone (round to nearest even, relative
+//     error at most 2^-9 per weight) and the GEMM runs once over K: the algorithmic
+//     tensor work, half the workspace, and a relative output error of about 2^-9 / 2
+//     on average against the exact sum.
+// The expansion costs 2.5 (one term) or 4.5 bytes of HBM traffic per weight against
+// 4 * M multiply-adds.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -31,10 +37,11 @@ constexpr int KR = 128;   // weight rows per CTA
 constexpr int PAD = 8;    // bf16 padding per transposed row (keeps rows 16-byte aligned)
 
 // One CTA: one 64-column tile x 128 rows of the tiled weights -> rows n of the slab,
-// dst[n - n0][k] = hi and dst[n - n0][Kp + k] = lo (bf16, row pitch 2 * Kp, Kp = K
-// rounded up to 64, zeros in between).  Thread t dequantises half a row (32 columns,
-// one 16-byte load) into two transposed shared tiles; then each warp writes eight
-// slab rows, 256 bytes of hi and 256 bytes of lo each.
+// dst[n - n0][k] = hi and, with TERMS = 2, dst[n - n0][Kp + k] = lo (bf16, row pitch
+// TERMS * Kp, Kp = K rounded up to 64, zeros in between).  Thread t dequantises half a
+// row (32 columns, one 16-byte load) into the transposed shared tiles; then each warp
+// writes eight slab rows, 256 bytes of each term.
+template <int TERMS>
 __global__ void __launch_bounds__(256) dequant_slab_kernel(
     const uint8_t* __restrict__ wt, const __nv_bfloat16* __restrict__ scales, int zp, int G,
     __nv_bfloat16* __restrict__ dst, int K, int Kp, int N, int n0, int ncols) {
@@ -60,7 +67,7 @@ __global__ void __launch_bounds__(256) dequant_slab_kernel(
         }
         const __nv_bfloat16 hi = __float2bfloat16_rn(v);
         tr[0][c][r] = hi;
-        tr[1][c][r] = __float2bfloat16_rn(v - __bfloat162float(hi));  // exact
+        if (TERMS == 2) tr[1][c][r] = __float2bfloat16_rn(v - __bfloat162float(hi));  // exact
       }
     }
   }
@@ -72,8 +79,8 @@ __global__ void __launch_bounds__(256) dequant_slab_kernel(
   for (int i = 0; i < TW / 8; ++i) {
     const int c = warp * (TW / 8) + i;
     const int n = tile * TW + c - n0;       // slab row
-    if (n >= ncols || k0 + kk >= Kp) continue;  // Kp % 64 == 0: whole 16-byte pieces
-    __nv_bfloat16* drow = dst + (size_t)n * 2 * Kp + (size_t)h * Kp + k0 + kk;
+    if (h >= TERMS || n >= ncols || k0 + kk >= Kp) continue;  // Kp % 64 == 0: whole pieces
+    __nv_bfloat16* drow = dst + (size_t)n * TERMS * Kp + (size_t)h * Kp + k0 + kk;
     if (k0 + kk + 8 <= K) {
       *reinterpret_cast<uint4*>(drow) = *reinterpret_cast<const uint4*>(&tr[h][c][kk]);
     } else {  // the tail of K and the zero padding up to Kp
@@ -89,6 +96,7 @@ __global__ void __launch_bounds__(256) dequant_slab_kernel(
 // 4i).  One CTA: 8 consecutive column groups (64 columns) x one 128-row block; thread
 // 32u + lane loads that lane's 16 bytes of unit u and places its 32 weights in the
 // transposed shared tiles; the write-out is the one above.
+template <int TERMS>
 __global__ void __launch_bounds__(256) dequant_slab_frag_kernel(
     const uint4* __restrict__ wf, const __nv_bfloat16* __restrict__ scales, int zp, int G,
     __nv_bfloat16* __restrict__ dst, int K, int Kp, int N, int NKB, int n0, int ncols) {
@@ -119,7 +127,7 @@ __global__ void __launch_bounds__(256) dequant_slab_frag_kernel(
       if (n < N && k0 + r < K) v = ((float)((wv[s] >> (4 * i)) & 0xFu) - fzp) * sc;  // exact
       const __nv_bfloat16 hi = __float2bfloat16_rn(v);
       tr[0][c][r] = hi;
-      tr[1][c][r] = __float2bfloat16_rn(v - __bfloat162float(hi));  // exact
+      if (TERMS == 2) tr[1][c][r] = __float2bfloat16_rn(v - __bfloat162float(hi));  // exact
     }
   }
   __syncthreads();
@@ -130,8 +138,8 @@ __global__ void __launch_bounds__(256) dequant_slab_frag_kernel(
   for (int i = 0; i < TW / 8; ++i) {
     const int cc = warp * (TW / 8) + i;
     const int nn = col0 + cc - n0;          // slab row
-    if (nn >= ncols || k0 + kk >= Kp) continue;  // Kp % 64 == 0: whole 16-byte pieces
-    __nv_bfloat16* drow = dst + (size_t)nn * 2 * Kp + (size_t)h * Kp + k0 + kk;
+    if (h >= TERMS || nn >= ncols || k0 + kk >= Kp) continue;  // Kp % 64 == 0: whole pieces
+    __nv_bfloat16* drow = dst + (size_t)nn * TERMS * Kp + (size_t)h * Kp + k0 + kk;
     if (k0 + kk + 8 <= K) {
       *reinterpret_cast<uint4*>(drow) = *reinterpret_cast<const uint4*>(&tr[h][cc][kk]);
     } else {  // the tail of K and the zero padding up to Kp
@@ -145,19 +153,20 @@ __global__ void __launch_bounds__(256) dequant_slab_frag_kernel(
 
 static size_t padded_k(int K) { return ((size_t)K + 63) / 64 * 64; }
 
-size_t w4a16_prefill_workspace_bytes(int K, int N) {
+size_t w4a16_prefill_workspace_bytes(int K, int N, int terms) {
   const size_t ncols = ((size_t)N + 255) / 256 * 256;
-  return ncols * padded_k(K) * 4;  // hi and lo per weight
+  return ncols * padded_k(K) * 2 * (size_t)terms;  // bf16 terms per weight
 }
 
 qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
                                   const void* scales, int zp, int G, void* y, int M, int N,
-                                  int K, void* ws, size_t ws_bytes, bool frag) {
+                                  int K, void* ws, size_t ws_bytes, bool frag, int terms) {
   using namespace w4p;
+  if (terms != 1 && terms != 2) return fail(QGEMM_ERR_INVALID_ARG, "terms %d", terms);
   // slab width: as many columns as the workspace holds, a multiple of 256 (so that
   // every slab but the last fills whole 256-column GEMM tiles)
   const size_t Kp = padded_k(K);
-  const size_t row_bytes = Kp * 4;  // hi and lo
+  const size_t row_bytes = Kp * 2 * (size_t)terms;
   size_t cols = ws_bytes / row_bytes;
   cols = cols / 256 * 256;
   if (cols == 0) {
@@ -170,18 +179,34 @@ qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_
   for (size_t n0 = 0; n0 < (size_t)N; n0 += cols) {
     const int ncols = (int)(((size_t)N - n0) < cols ? ((size_t)N - n0) : cols);
     dim3 grid2((ncols + TW - 1) / TW, (unsigned)((Kp + KR - 1) / KR));
-    if (frag)  // Kp rounds K up to 64, the layout to 128: the grid's blocks are the layout's
-      dequant_slab_frag_kernel<<<grid2, 256, 0, s->stream>>>(
-          reinterpret_cast<const uint4*>(wt), static_cast<const __nv_bfloat16*>(scales), zp, G,
-          slab, K, (int)Kp, N, (K + KR - 1) / KR, (int)n0, ncols);
+    const uint4* wf = reinterpret_cast<const uint4*>(wt);
+    const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(scales);
+    const int nkb = (K + KR - 1) / KR;
+    // frag: Kp rounds K up to 64, the layout to 128: the grid's blocks are the layout's
+    if (frag && terms == 2)
+      dequant_slab_frag_kernel<2><<<grid2, 256, 0, s->stream>>>(wf, sc, zp, G, slab, K, (int)Kp,
+                                                                  N, nkb, (int)n0, ncols);
+    else if (frag)
+      dequant_slab_frag_kernel<1><<<grid2, 256, 0, s->stream>>>(wf, sc, zp, G, slab, K, (int)Kp,
+                                                                  N, nkb, (int)n0, ncols);
+    else if (terms == 2)
+      dequant_slab_kernel<2><<<grid2, 256, 0, s->stream>>>(wt, sc, zp, G, slab, K, (int)Kp, N,
+                                                             (int)n0, ncols);
     else
-      dequant_slab_kernel<<<grid2, 256, 0, s->stream>>>(
-          wt, static_cast<const __nv_bfloat16*>(scales), zp, G, slab, K, (int)Kp, N, (int)n0,
-          ncols);
+      dequant_slab_kernel<1><<<grid2, 256, 0, s->stream>>>(wt, sc, zp, G, slab, K, (int)Kp, N,
+                                                             (int)n0, ncols);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "dequant_slab launch");
-    const qgemm_status st = launch_bf16_gemm_nk(
-        s, x, slab, static_cast<__nv_bfloat16*>(y) + n0, N, M, ncols, K, 2);
+    // y[:, n0 .. n0+ncols) = x * slab^T over one segment (hi) or two (hi, then lo)
+    TcArgs a;
+    a.kind = KIND_BF16;
+    a.A = x; a.B = slab;
+    a.M = M; a.N = ncols; a.K = 2 * K;
+    a.nseg = terms;
+    a.b_seg = terms == 2 ? 0x2u : 0u;
+    a.b_pitch = row_bytes;
+    a.out = static_cast<__nv_bfloat16*>(y) + n0; a.out_dtype = QGEMM_BF16; a.ldc = N;
+    const qgemm_status st = launch_tc_gemm(s, a);
     if (st != QGEMM_OK) return st;
   }
   return QGEMM_OK;

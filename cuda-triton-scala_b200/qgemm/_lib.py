@@ -32,6 +32,8 @@ B_NK = 1
 ALGO_AUTO = 0
 ALGO_TCGEN05 = 1
 ALGO_SIMT = 2
+PREFILL_FRAG = 1
+PREFILL_ONE_TERM = 2
 
 BLOB_VERSION = 1
 BLOB_W4_TILED = 1
@@ -104,6 +106,9 @@ SIGNATURES = {
     "qgemm_w4a16_prefill_workspace_bytes": (_S, [_I, _I, ctypes.POINTER(_SZ)]),
     "qgemm_w4a16_grouped_gemm_prefill": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I, _I,
                                                _U64, _SZ]),
+    "qgemm_w4a16_prefill_workspace_bytes_ex": (_S, [_I, _I, _I, ctypes.POINTER(_SZ)]),
+    "qgemm_w4a16_grouped_gemm_prefill_ex": (_S, [_P, _U64, _U64, _U64, _I, _I, _U64, _I, _I,
+                                                 _I, _U64, _SZ, _I]),
     "qgemm_gemm_bf16_nk": (_S, [_P, _U64, _U64, _U64, _I, _I, _I, _I]),
     "qgemm_quantize_per_token": (_S, [_P, _U64, _I, _U64, _U64, _I, _I]),
     "qgemm_gemm_f32": (_S, [_P, _U64, _U64, _U64, _U64, _I, _I, _I, ctypes.c_float,

@@ -97,28 +97,46 @@ class QuantizedGemmOps:
                zero_point, group_size, L.addr(y), M, N, K)
 
     @staticmethod
-    def w4PrefillWorkspaceBytes(K: int, N: int) -> int:
+    def w4PrefillWorkspaceBytes(K: int, N: int, *, one_term: bool = False) -> int:
+        """Workspace that holds all of N in one slab: two bf16 terms per weight (exact),
+        or one with one_term."""
         n = ctypes.c_size_t(0)
-        L.call("qgemm_w4a16_prefill_workspace_bytes", K, N, ctypes.byref(n))
+        if one_term:
+            L.call("qgemm_w4a16_prefill_workspace_bytes_ex", K, N, L.PREFILL_ONE_TERM,
+                   ctypes.byref(n))
+        else:
+            L.call("qgemm_w4a16_prefill_workspace_bytes", K, N, ctypes.byref(n))
         return n.value
 
     def w4a16GemmGroupedPrefill(self, x, wt, scales, y, M: int, N: int, K: int, workspace,
                                 workspace_bytes: int, *, zero_point: int = 8,
-                                group_size: int = 128):
+                                group_size: int = 128, one_term: bool = False):
         """Group-wise W4A16 for prefill-sized M on prepackW4Tiled weights: bf16 slabs
-        expanded in `workspace`, then the tensor-core bf16 GEMM."""
-        L.call("qgemm_w4a16_grouped_gemm_prefill", self._h, L.addr(x), L.addr(wt),
-               L.addr(scales), zero_point, group_size, L.addr(y), M, N, K, L.addr(workspace),
-               workspace_bytes)
+        expanded in `workspace`, then the tensor-core bf16 GEMM.  Each weight is
+        expanded exactly (hi + lo), or with one_term to bf16((q - zp) * s) alone (half
+        the tensor work; relative weight error <= 2^-9)."""
+        if one_term:
+            L.call("qgemm_w4a16_grouped_gemm_prefill_ex", self._h, L.addr(x), L.addr(wt),
+                   L.addr(scales), zero_point, group_size, L.addr(y), M, N, K,
+                   L.addr(workspace), workspace_bytes, L.PREFILL_ONE_TERM)
+        else:
+            L.call("qgemm_w4a16_grouped_gemm_prefill", self._h, L.addr(x), L.addr(wt),
+                   L.addr(scales), zero_point, group_size, L.addr(y), M, N, K,
+                   L.addr(workspace), workspace_bytes)
 
     def w4a16GemmGroupedPrefillFrag(self, x, wf, scales, y, M: int, N: int, K: int, workspace,
                                     workspace_bytes: int, *, zero_point: int = 8,
-                                    group_size: int = 128):
+                                    group_size: int = 128, one_term: bool = False):
         """The prefill GEMM on prepackW4Frag weights (one weight copy for prefill and
-        decode)."""
-        L.call("qgemm_w4a16_grouped_gemm_prefill_frag", self._h, L.addr(x), L.addr(wf),
-               L.addr(scales), zero_point, group_size, L.addr(y), M, N, K, L.addr(workspace),
-               workspace_bytes)
+        decode); one_term as in w4a16GemmGroupedPrefill."""
+        if one_term:
+            L.call("qgemm_w4a16_grouped_gemm_prefill_ex", self._h, L.addr(x), L.addr(wf),
+                   L.addr(scales), zero_point, group_size, L.addr(y), M, N, K,
+                   L.addr(workspace), workspace_bytes, L.PREFILL_FRAG | L.PREFILL_ONE_TERM)
+        else:
+            L.call("qgemm_w4a16_grouped_gemm_prefill_frag", self._h, L.addr(x), L.addr(wf),
+                   L.addr(scales), zero_point, group_size, L.addr(y), M, N, K,
+                   L.addr(workspace), workspace_bytes)
 
     def gemmBf16NK(self, A, B, out, M: int, N: int, K: int, *, ldc: int | None = None):
         """out[M, ldc] bf16 = A[M,K] (bf16) x B[N,K]^T (bf16), fp32 sums."""

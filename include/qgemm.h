@@ -290,13 +290,14 @@ QGEMM_API qgemm_status qgemm_prepack_w4_frag(qgemm_stream_t s, uint64_t wq, uint
 
 /* Group-wise W4A16 GEMM for prefill-sized M (the same arithmetic as
  * qgemm_w4a16_grouped_gemm on the same prepacked weights `wt`): the weights are
- * expanded slab by slab into the caller's workspace as bf16 (q - zero_point) *
- * scale, rounded once, and multiplied on the tensor cores with fp32 sums.  Any M;
- * meant for M in the hundreds and above, where the expansion is a few percent of
- * the call.  workspace: 16-byte aligned, at least 512 * K bytes (one 256-column
- * slab); qgemm_w4a16_prefill_workspace_bytes gives the size that holds all of N in
- * one slab.  Requires sm_100, K % 8 == 0, K % group_size == 0, N % 8 == 0 and
- * 16-byte aligned x, wt, scales, y.  Deterministic. */
+ * expanded slab by slab into the caller's workspace, each (q - zero_point) * scale
+ * as two bf16 values hi + lo that sum to it exactly, and multiplied on the tensor
+ * cores with fp32 sums (twice the algorithmic tensor work; the products are exact).
+ * Any M; meant for M in the hundreds and above, where the expansion is a few percent
+ * of the call.  workspace: 16-byte aligned, at least 1024 * Kp bytes (one 256-column
+ * slab; Kp = K rounded up to a multiple of 64); qgemm_w4a16_prefill_workspace_bytes
+ * gives the size that holds all of N in one slab.  Requires sm_100, K % 8 == 0,
+ * K % group_size == 0, N % 8 == 0 and 16-byte aligned x, wt, y.  Deterministic. */
 QGEMM_API qgemm_status qgemm_w4a16_prefill_workspace_bytes(int K, int N, size_t* bytes);
 QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_prefill(qgemm_stream_t s, uint64_t x, uint64_t wt,
                                                         uint64_t scales, int zero_point,
@@ -313,6 +314,26 @@ QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_prefill_frag(qgemm_stream_t s, u
                                                              uint64_t y, int M, int N, int K,
                                                              uint64_t workspace,
                                                              size_t workspace_bytes);
+/* Both prefill forms behind one call, with flags:
+ *   QGEMM_PREFILL_FRAG      w is in the fragment order of qgemm_prepack_w4_frag (else
+ *                           the 64-column tiles of qgemm_prepack_w4_tiled);
+ *   QGEMM_PREFILL_ONE_TERM  each weight is expanded to one bf16 value, bf16((q - zp) *
+ *                           scale) rounded to nearest even, instead of the exact pair:
+ *                           the algorithmic tensor work and half the workspace
+ *                           (512 * Kp bytes a 256-column slab); each product then
+ *                           carries the weight's rounding (relative error <= 2^-9).
+ * qgemm_w4a16_prefill_workspace_bytes_ex gives the full-N workspace for the flags.
+ * Unknown flag bits are QGEMM_ERR_INVALID_ARG. */
+#define QGEMM_PREFILL_FRAG 1
+#define QGEMM_PREFILL_ONE_TERM 2
+QGEMM_API qgemm_status qgemm_w4a16_prefill_workspace_bytes_ex(int K, int N, int flags,
+                                                              size_t* bytes);
+QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_prefill_ex(qgemm_stream_t s, uint64_t x,
+                                                           uint64_t w, uint64_t scales,
+                                                           int zero_point, int group_size,
+                                                           uint64_t y, int M, int N, int K,
+                                                           uint64_t workspace,
+                                                           size_t workspace_bytes, int flags);
 
 /* bf16 GEMM on the tcgen05 kernels (no counterpart among the reference's quantized
  * operators; it is the multiply of the W4A16 prefill path):

@@ -128,3 +128,22 @@ def test_bridge_argument_errors_without_gpu():
     # qBits of dynamicQuantize has a default (QuantizedGemmOps.scala:127): only the handle fails
     assert launch("dynamicQuantize", 3, [4, 4], ["K", "N"]) == -1
     assert "stream" in L.last_error()
+
+
+def test_prefill_workspace_sizes_without_gpu():
+    """Host-only sizing: the one-term workspace is half the exact one; unknown flags are
+    refused."""
+    import qgemm
+    import qgemm._lib as L
+    ops = qgemm.QuantizedGemmOps
+    for K, N in ((4096, 22016), (11008, 4096), (1056, 520)):
+        kp = (K + 63) // 64 * 64
+        ncols = (N + 255) // 256 * 256
+        assert ops.w4PrefillWorkspaceBytes(K, N) == ncols * kp * 4
+        assert ops.w4PrefillWorkspaceBytes(K, N, one_term=True) == ncols * kp * 2
+    n = ctypes.c_size_t(0)
+    assert L.lib().qgemm_w4a16_prefill_workspace_bytes_ex(64, 64, 4, ctypes.byref(n)) == \
+        L.ERR_INVALID_ARG
+    assert L.lib().qgemm_w4a16_prefill_workspace_bytes_ex(64, 64, L.PREFILL_FRAG,
+                                                          ctypes.byref(n)) == L.OK
+    assert n.value == 256 * 64 * 4

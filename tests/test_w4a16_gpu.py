@@ -123,6 +123,18 @@ def test_prepack_w4_frag_layout(gpu, K, N):
     (33, 2048, 2048, 128, 8),    # passes of 16, 16 and 1 rows
     (2, 131072, 512, 128, 8),    # wide N: the columns go out in several chunks
     (16, 65536, 1024, 64, 8),    # wide N on column pairs: several chunks
+    # 17 to 32 rows a pass, or K past 8192: the K-split cluster kernel
+    (32, 12288, 4096, 128, 8),   # Llama-2-7B qkv, one 32-row pass
+    (32, 4096, 11008, 128, 8),   # Llama-2-7B down projection, K > 8192
+    (1, 4096, 11008, 128, 8),    # one row, K > 8192 (8-row tile)
+    (24, 22016, 4096, 128, 8),   # 24 of 32 rows, 1376 pairs
+    (17, 1008, 2048, 64, 3),     # 17 rows, G = 64, 63 pairs
+    (32, 4112, 4128, 32, 8),     # G = 32, K not a multiple of 128, 257 pairs
+    (40, 2048, 16384, 256, 15),  # K = 16384 (the limit), G = 256, passes of 32 and 8
+    (9, 48, 9984, 128, 8),       # three pairs, K > 8192
+    (64, 512, 1024, 128, 0),     # two full 32-row passes
+    (16, 1024, 6144, 128, 8),    # 16 rows, K past the 16-row kernel's 4096
+    (32, 131072, 512, 128, 8),   # wide N: the pairs go out in several launches
 ])
 def test_grouped_frag_path(gpu, oracle, M, N, K, G, zp):
     x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M * 5 + N + K + G)
@@ -132,7 +144,7 @@ def test_grouped_frag_path(gpu, oracle, M, N, K, G, zp):
     assert err <= TOL_BF16, err
 
 
-@pytest.mark.parametrize("M,N", [(4, 2048), (16, 2048)])
+@pytest.mark.parametrize("M,N", [(4, 2048), (16, 2048), (32, 2048)])
 def test_frag_activation_magnitudes(gpu, oracle, M, N):
     """Rows of very different magnitude (bf16 values from 1e-30 to 1e30, and an all-zero
     row): the frag kernels' fp16 arithmetic scales activations by powers of two, so the
@@ -140,7 +152,7 @@ def test_frag_activation_magnitudes(gpu, oracle, M, N):
     K, G = 2048, 128
     x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=83)
     xf = syn.bf16_to_float(x).astype(np.float32)
-    mags = np.array([1.0, 1e30, 1e-30, 0.0, 3e4, 1e-5, 7e12, 2.0] * 2, np.float32)[:M]
+    mags = np.array([1.0, 1e30, 1e-30, 0.0, 3e4, 1e-5, 7e12, 2.0] * 4, np.float32)[:M]
     xf = xf * mags[:, None]
     xf[M - 1, : K // 2] *= 1e6  # one row whose first half is much larger than its second
     xb = syn.bf16_bits(xf)
@@ -149,6 +161,16 @@ def test_frag_activation_magnitudes(gpu, oracle, M, N):
     got = syn.bf16_to_float(y).astype(np.float64)
     for m in range(M):  # per row: the floor of rel_err scales with the row
         assert rel_err(got[m], ref[m]) <= TOL_BF16, (m, mags[m])
+
+
+def test_frag_cluster_deterministic(gpu):
+    """The cluster kernel adds the K slices' partial sums in rank order: repeat runs are
+    bit-identical."""
+    M, N, K, G = 32, 4096, 11008, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=66)
+    a = frag(gpu, x, wq, sc, M, N, K, G)
+    b = frag(gpu, x, wq, sc, M, N, K, G)
+    np.testing.assert_array_equal(a, b)
 
 
 def test_frag_deterministic_and_matches_tiled(gpu):
@@ -161,17 +183,18 @@ def test_frag_deterministic_and_matches_tiled(gpu):
     assert rel_err(syn.bf16_to_float(a).astype(np.float64), c) <= TOL_BF16
 
 
-@pytest.mark.parametrize("K,G", [(480, 48), (8320, 128)])
-def test_frag_rejects_unsupported_shapes(gpu, K, G):
-    """Group 48 (not 32, 64 or a multiple of 128) and K > 8192 are refused."""
+@pytest.mark.parametrize("K,G,N", [(480, 48, 64), (8320, 128, 72), (16512, 128, 64)])
+def test_frag_rejects_unsupported_shapes(gpu, K, G, N):
+    """Group 48 (not 32, 64 or a multiple of 128), K > 8192 with N not a multiple of 16,
+    and K > 16384 are refused."""
     import qgemm
     dev, st, ops = gpu
-    x, wq, sc = syn.w4a16_inputs(1, 64, K, group=G, seed=65)
-    wf = Out(dev, st, ops.w4FragBytes(K, 64))
-    ops.prepackW4Frag(dev_array(gpu, wq), wf, K, 64)
-    y = Out(dev, st, 64 * 2)
+    x, wq, sc = syn.w4a16_inputs(1, N, K, group=G, seed=65)
+    wf = Out(dev, st, ops.w4FragBytes(K, N))
+    ops.prepackW4Frag(dev_array(gpu, wq), wf, K, N)
+    y = Out(dev, st, N * 2)
     with pytest.raises(qgemm.QGemmError) as e:
-        ops.w4a16GemmGroupedFrag(dev_array(gpu, x), wf, dev_array(gpu, sc), y, 1, 64, K,
+        ops.w4a16GemmGroupedFrag(dev_array(gpu, x), wf, dev_array(gpu, sc), y, 1, N, K,
                                  group_size=G)
     assert e.value.status == qgemm._lib.ERR_UNSUPPORTED
     st.sync()
