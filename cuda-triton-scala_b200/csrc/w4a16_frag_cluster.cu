@@ -16,10 +16,15 @@
 //   * A CTA keeps its slice's activations (8 NB rows) in shared memory in fragment
 //     order: the B registers of one (block, step, n tile) are one 16-byte load per lane
 //     from 512 contiguous bytes, free of bank conflicts.
-//   * Each of the 8 consumer warps owns up to PMAX = 4 of the CTA's column pairs over
-//     the whole slice and keeps their fp32 sums in registers, so no partial sum crosses
-//     warps; every B fragment it loads feeds 2 * PMAX MMAs (at 32 rows: 32 MMAs per
-//     step per 4 loads).  The weights are read from HBM once for all 32 rows.
+//   * Each of the 8 warps owns NP (1 to 4, a template parameter) of the CTA's 8 NP
+//     column pairs over the whole slice and keeps their fp32 sums in registers, so no
+//     partial sum crosses warps; every B fragment it loads feeds 2 NP MMAs per 8-row
+//     tile.  Every warp has the same work (a warp with more pairs than the others would
+//     set the pace, the loop being latency-bound at a few pairs a warp), and NP is known
+//     to the compiler (the loop has no branches: 10.4 cycles per MMA per sub-partition
+//     at NP = 3 against 13.3 with a run-time pair count, measured in isolation).  The
+//     last cluster's pairs past N read zeros (TMA fills past the tensor) and are not
+//     stored.  The weights are read from HBM once for all 32 rows.
 //   * The slice streams one 128-row block of all the CTA's column groups per ring
 //     stage: one 3-D TMA tile (512 bytes x 1 block x 2 * pairs).  There is no producer
 //     warp (a ninth warp would put three warps on one sub-partition and cap registers at
@@ -51,9 +56,9 @@ namespace qg {
 namespace w4c {
 
 constexpr int KB = 128;          // rows per block
-constexpr int NCW = 8;           // consumer warps
+constexpr int NCW = 8;           // warps
 constexpr int THREADS = 32 * NCW;
-constexpr int PMAX = 4;          // column pairs per consumer warp, at most
+constexpr int PMAX = 4;          // column pairs per warp, at most
 constexpr int MAX_S = 8;         // K slices (cluster size), at most
 constexpr int MAX_STAGES = 8;
 constexpr int NBLK_MAX = 16;     // 128-row blocks per slice, at most
@@ -64,8 +69,7 @@ struct Params {
   int NKB, S;
   int nblk_max, npc_max, nsr_max;  // shared-memory layout sizes (the same in every CTA)
   int stages;
-  int pair0;                       // first column pair of this launch
-  int pbase, prem;                 // cluster x owns pbase + (x < prem) column pairs
+  int pair0, pair1;                // column pairs [pair0, pair1) of this launch
   int y_vec;                       // y rows are 8-byte aligned
   unsigned long long wait_ns;
   const __nv_bfloat16* x;
@@ -131,9 +135,9 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int s) {
   return s == 0 ? v.x : s == 1 ? v.y : s == 2 ? v.z : v.w;
 }
 
-// NB: 8-row activation tiles (1, 2 or 4); GS: 32-row steps per scale group (1, 2 or 4:
-// group 32, 64 or a multiple of 128).
-template <int NB, int GS>
+// NB: 8-row activation tiles (1, 2 or 4); NP: column pairs per warp; GS: 32-row steps
+// per scale group (1, 2 or 4: group 32, 64 or a multiple of 128).
+template <int NB, int NP, int GS>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_frag_cluster_kernel(const __grid_constant__ CUtensorMap tmW, const Params p) {
   constexpr int NQ = 4 / GS;  // scale groups per block
@@ -143,9 +147,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int g = lane >> 2, t = lane & 3;
   const int S = p.S;
   const int rank = (int)ptx::cluster_ctarank();  // K slice
-  const int cx = blockIdx.x;                     // run of column pairs
-  const int p0 = cx * p.pbase + (cx < p.prem ? cx : p.prem);
-  const int npc = p.pbase + (cx < p.prem ? 1 : 0);
+  constexpr int npc = NCW * NP;                  // column pairs of this CTA
+  const int p0 = p.pair0 + blockIdx.x * npc;      // its first pair
+  const int preal = (p.pair1 - p0) < npc ? (p.pair1 - p0) : npc;  // pairs inside the launch
   const int kb0 = (int)((long long)rank * p.NKB / S);
   const int kb1 = (int)((long long)(rank + 1) * p.NKB / S);
   const int nblk = kb1 - kb0;
@@ -166,7 +170,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t stage_bytes = (uint32_t)p.npc_max * 1024u;  // 2 npc_max units of 512 B
   const int STAGES = p.stages;
   const uint32_t ring0 = ptx::smem_u32(smem + L.ring);
-  const int gz = 2 * (p.pair0 + p0);  // first column group of the cluster's run
+  const int gz = 2 * p0;              // first column group of the cluster's run
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -180,25 +184,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     ptx::prefetch_tmap(&tmW);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    // the first stages (weights never depend on the previous kernel: before the wait);
-    // the other threads start the activation and scale copies meanwhile
-    for (int j = 0; j < STAGES && j < nblk; ++j) {
+  // the first stages, one per warp (lane 0 of warp j issues stage j: a TMA issue holds
+  // its thread for some 150 ns, and the warps' fills below wait for the slowest warp);
+  // weights never depend on the previous kernel, so this precedes the launch wait
+  for (int j = warp; j < STAGES && j < nblk; j += NCW) {
+    if (lane == 0) {
       ptx::mbar_arrive_expect_tx(full_bar(j), stage_bytes);
       ptx::tma_load_3d(ring0 + j * stage_bytes, &tmW, full_bar(j), 0, kb0 + j, gz);
       laps[j] = 1;
     }
   }
 
-  float acc[PMAX][NB][4];
+  float acc[NP][NB][4];
 #pragma unroll
-  for (int i = 0; i < PMAX; ++i)
+  for (int i = 0; i < NP; ++i)
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[i][nb][e] = 0.f;
-  const int pw0 = warp * npc / NCW;
-  const int np = (warp + 1) * npc / NCW - pw0;  // pairs of this warp (<= PMAX)
+  const int pw0 = warp * NP;  // this warp's first pair within the CTA
 
   {
     // ---------------- consumers (all warps) ----------------
@@ -208,13 +212,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     {
       const int klast = (kb1 * KB < p.K ? kb1 * KB : p.K) - 1;
       const int nsr = klast / p.G - gr0 + 1;
-      const int c8 = npc * 2;  // 8-column pieces per row
-      const __nv_bfloat16* sbase = p.s + (size_t)(p.pair0 + p0) * 16;
+      constexpr int c8 = npc * 2;  // 8-column pieces per row (zeros past the launch)
+      const int c8real = preal * 2;
+      const __nv_bfloat16* sbase = p.s + (size_t)p0 * 16;
       const uint32_t sc0 = ptx::smem_u32(scs);
       for (int i = ctid; i < nsr * c8; i += 32 * NCW) {
         const int r = i / c8, c = i - r * c8;
+        const bool in = c < c8real;
         ptx::cp_async_16(sc0 + (uint32_t)((r * ncs + 8 * c) * 2),
-                         sbase + (size_t)(gr0 + r) * p.N + 8 * c, 16u);
+                         in ? sbase + (size_t)(gr0 + r) * p.N + 8 * c : p.s, in ? 16u : 0u);
       }
     }
     // activations may be written by the previous kernel in the stream
@@ -273,16 +279,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // this warp's units of the stage: groups 2(pw0+i) and 2(pw0+i)+1, 16 bytes a lane
       const uint4* rw = ring + (size_t)st * (stage_bytes / 16) + lane;
-      uint4 wa[PMAX], wb[PMAX];
+      uint4 wa[NP], wb[NP];
 #pragma unroll
-      for (int i = 0; i < PMAX; ++i) {
-        if (i < np) {
-          wa[i] = rw[(2 * (pw0 + i)) * 32];
-          wb[i] = rw[(2 * (pw0 + i) + 1) * 32];
-        } else {
-          wa[i] = make_uint4(0u, 0u, 0u, 0u);
-          wb[i] = wa[i];
-        }
+      for (int i = 0; i < NP; ++i) {
+        wa[i] = rw[(2 * (pw0 + i)) * 32];
+        wb[i] = rw[(2 * (pw0 + i) + 1) * 32];
       }
       __syncwarp();
       if (lane == 0) {
@@ -303,47 +304,43 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb)
           z[nb] = *reinterpret_cast<const float2*>(sx + (j * NQ + q) * 32 + 8 * nb + 2 * t);
-        float d[PMAX][NB][4];
+        float d[NP][NB][4];
 #pragma unroll
         for (int s = q * GS; s < q * GS + GS; ++s) {
           uint4 b[NB];
 #pragma unroll
           for (int nb = 0; nb < NB; ++nb) b[nb] = xs[((j * 4 + s) * NB + nb) * 32 + lane];
           // first k half of every pair, then the second: an MMA and the next one on the
-          // same accumulator are np * NB MMAs apart
+          // same accumulator are NP * NB MMAs apart
 #pragma unroll
-          for (int i = 0; i < PMAX; ++i) {
-            if (i < np) {
-              const uint32_t w0 = word_of(wa[i], s), w1 = word_of(wb[i], s);
-              const uint32_t l0 = and_or(w0, MASK, BIAS), l1 = and_or(w1, MASK, BIAS);
-              const uint32_t l2 = and_or(w0 >> 8, MASK, BIAS), l3 = and_or(w1 >> 8, MASK, BIAS);
+          for (int i = 0; i < NP; ++i) {
+            const uint32_t w0 = word_of(wa[i], s), w1 = word_of(wb[i], s);
+            const uint32_t l0 = and_or(w0, MASK, BIAS), l1 = and_or(w1, MASK, BIAS);
+            const uint32_t l2 = and_or(w0 >> 8, MASK, BIAS), l3 = and_or(w1 >> 8, MASK, BIAS);
 #pragma unroll
-              for (int nb = 0; nb < NB; ++nb) {
-                if (s == q * GS)
-                  mma_bf16_init(d[i][nb], l0, l1, l2, l3, b[nb].x, b[nb].y, z[nb].x, z[nb].y);
-                else
-                  mma_bf16(d[i][nb], l0, l1, l2, l3, b[nb].x, b[nb].y);
-              }
+            for (int nb = 0; nb < NB; ++nb) {
+              if (s == q * GS)
+                mma_bf16_init(d[i][nb], l0, l1, l2, l3, b[nb].x, b[nb].y, z[nb].x, z[nb].y);
+              else
+                mma_bf16(d[i][nb], l0, l1, l2, l3, b[nb].x, b[nb].y);
             }
           }
 #pragma unroll
-          for (int i = 0; i < PMAX; ++i) {
-            if (i < np) {
-              const uint32_t w0 = word_of(wa[i], s), w1 = word_of(wb[i], s);
-              const uint32_t h0 = and_or(w0 >> 4, MASK, BIAS), h1 = and_or(w1 >> 4, MASK, BIAS);
-              const uint32_t h2 = and_or(w0 >> 12, MASK, BIAS), h3 = and_or(w1 >> 12, MASK, BIAS);
+          for (int i = 0; i < NP; ++i) {
+            const uint32_t w0 = word_of(wa[i], s), w1 = word_of(wb[i], s);
+            const uint32_t h0 = and_or(w0 >> 4, MASK, BIAS), h1 = and_or(w1 >> 4, MASK, BIAS);
+            const uint32_t h2 = and_or(w0 >> 12, MASK, BIAS), h3 = and_or(w1 >> 12, MASK, BIAS);
 #pragma unroll
-              for (int nb = 0; nb < NB; ++nb)
-                mma_bf16(d[i][nb], h0, h1, h2, h3, b[nb].z, b[nb].w);
-            }
+            for (int nb = 0; nb < NB; ++nb)
+              mma_bf16(d[i][nb], h0, h1, h2, h3, b[nb].z, b[nb].w);
           }
         }
         // a scale group wholly past K has no scale row (its sums are zero): skipped
         const int k0g = (kb0 + j) * KB + q * GS * 32;
         const int lr = k0g / p.G - gr0;
 #pragma unroll
-        for (int i = 0; i < PMAX; ++i) {
-          if (i < np && k0g < p.K) {
+        for (int i = 0; i < NP; ++i) {
+          if (k0g < p.K) {
             const uint16_t* sr = scs + (size_t)lr * ncs + 16 * (pw0 + i) + g;
             const float s0 = bf16_bits_to_f32(sr[0]), s1 = bf16_bits_to_f32(sr[8]);
 #pragma unroll
@@ -373,23 +370,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (ok) {
     // D rows g / g+8 are columns 16p+g / 16p+8+g; D columns 2t, 2t+1 are rows 8nb+2t(+1)
 #pragma unroll
-    for (int i = 0; i < PMAX; ++i) {
-      if (i < np) {
+    for (int i = 0; i < NP; ++i) {
 #pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-          float* r0 = red + (size_t)(8 * nb + 2 * t) * rs + 16 * (pw0 + i) + g;
-          r0[0] = acc[i][nb][0];
-          r0[rs] = acc[i][nb][1];
-          r0[8] = acc[i][nb][2];
-          r0[rs + 8] = acc[i][nb][3];
-        }
+      for (int nb = 0; nb < NB; ++nb) {
+        float* r0 = red + (size_t)(8 * nb + 2 * t) * rs + 16 * (pw0 + i) + g;
+        r0[0] = acc[i][nb][0];
+        r0[rs] = acc[i][nb][1];
+        r0[8] = acc[i][nb][2];
+        r0[rs + 8] = acc[i][nb][3];
       }
     }
   }
   ptx::cluster_sync_all();
   // CTA `rank` finishes pairs [rank*chunk, (rank+1)*chunk) of the cluster's run
   const int chunk = (npc + S - 1) / S;
-  const int q0 = rank * chunk, q1 = (q0 + chunk < npc ? q0 + chunk : npc);
+  const int q0 = rank * chunk, q1 = (q0 + chunk < preal ? q0 + chunk : preal);
   if (ok && q1 > q0) {
     const int rows = p.M < MR ? p.M : MR;
     const int nc4 = (q1 - q0) * 4;  // float4 pieces per row
@@ -407,7 +402,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int r = 1; r < MAX_S; ++r)
         if (r < S) { v.x += u[r].x; v.y += u[r].y; v.z += u[r].z; v.w += u[r].w; }
-      __nv_bfloat16* yo = p.y + (size_t)m * p.N + (size_t)(p.pair0 + p0) * 16 + c;
+      __nv_bfloat16* yo = p.y + (size_t)m * p.N + (size_t)p0 * 16 + c;
       const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
       if (p.y_vec) {
         uint2 o;
@@ -457,32 +452,43 @@ static bool map_weights(CUtensorMap* m, const void* wf, int NKB, int NG, int gro
 
 using Kern = void (*)(const CUtensorMap, const Params);
 
-template <int NB>
-static Kern kernel_for(int gs) {
-  return gs == 1 ? w4a16_frag_cluster_kernel<NB, 1>
-       : gs == 2 ? w4a16_frag_cluster_kernel<NB, 2>
-                 : w4a16_frag_cluster_kernel<NB, 4>;
+template <int NB, int NP>
+static Kern kernel_for_gs(int gs) {
+  return gs == 1 ? w4a16_frag_cluster_kernel<NB, NP, 1>
+       : gs == 2 ? w4a16_frag_cluster_kernel<NB, NP, 2>
+                 : w4a16_frag_cluster_kernel<NB, NP, 4>;
 }
-static Kern kernel_for(int nb, int gs) {
-  return nb == 1 ? kernel_for<1>(gs) : nb == 2 ? kernel_for<2>(gs) : kernel_for<4>(gs);
+template <int NB>
+static Kern kernel_for_np(int np, int gs) {
+  return np == 1 ? kernel_for_gs<NB, 1>(gs)
+       : np == 2 ? kernel_for_gs<NB, 2>(gs)
+       : np == 3 ? kernel_for_gs<NB, 3>(gs)
+                 : kernel_for_gs<NB, 4>(gs);
+}
+static Kern kernel_for(int nb, int np, int gs) {
+  return nb == 1 ? kernel_for_np<1>(np, gs) : nb == 2 ? kernel_for_np<2>(np, gs)
+                                                      : kernel_for_np<4>(np, gs);
 }
 
 static std::mutex g_mu;
-static std::map<std::tuple<int, int, int>, bool> g_attr;     // (device, nb, gs) -> set
-static std::map<std::tuple<int, int>, int> g_clusters;        // (device, S) -> clusters
+static std::map<std::tuple<int, int, int, int>, bool> g_attr;  // (device, nb, np, gs) -> set
+static std::map<std::tuple<int, int>, int> g_clusters;          // (device, S) -> clusters
 
-static qgemm_status set_attr(qgemm_device_s* d, int nb, int gs) {
+static qgemm_status set_attr(qgemm_device_s* d, int nb, int np, int gs) {
   std::lock_guard<std::mutex> lk(g_mu);
-  auto key = std::make_tuple(d->ordinal, nb, gs);
+  auto key = std::make_tuple(d->ordinal, nb, np, gs);
   if (g_attr.count(key)) return QGEMM_OK;
-  cudaError_t e = cudaFuncSetAttribute(kernel_for(nb, gs), cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(kernel_for(nb, np, gs),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)d->smem_optin);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4a16_frag_cluster)");
   g_attr[key] = true;
   return QGEMM_OK;
 }
 
-// Clusters of S CTAs (one CTA per SM, the largest shared-memory request) that run at once.
+// Clusters of S CTAs (one CTA per SM, the largest shared-memory request) that run at
+// once: fewer than SMs / S, since a cluster must sit inside one GPU processing cluster
+// (measured on B200: 148, 74, 45, 33, 26, 22, 15, 15 for S = 1 .. 8).
 static int max_clusters(qgemm_device_s* d, int S) {
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -490,7 +496,7 @@ static int max_clusters(qgemm_device_s* d, int S) {
     if (it != g_clusters.end()) return it->second;
   }
   int n = 0;
-  if (set_attr(d, MAX_NB, 4) == QGEMM_OK) {
+  if (set_attr(d, MAX_NB, PMAX, 4) == QGEMM_OK) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, S, 1);
     cfg.blockDim = dim3(THREADS, 1, 1);
@@ -502,63 +508,59 @@ static int max_clusters(qgemm_device_s* d, int S) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, kernel_for(MAX_NB, 4), &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, kernel_for(MAX_NB, PMAX, 4), &cfg) != cudaSuccess) {
       (void)cudaGetLastError();
       n = 0;
     }
   }
-  if (n <= 0) n = d->sm_count / S;  // the query failed: assume every SM takes one CTA
+  if (n <= 0) n = d->sm_count / (S * 2);  // the query failed: a conservative guess
+  if (n < 1) n = 1;
   std::lock_guard<std::mutex> lk(g_mu);
   g_clusters[std::make_tuple(d->ordinal, S)] = n;
   return n;
 }
 
-// pairs on the busiest sub-partition (warps w and w+4 share one) for npc pairs a CTA
-static int busiest(int npc) {
-  int b = 0;
-  for (int k = 0; k < 4; ++k) {
-    int n = 0;
-    for (int w = k; w < NCW; w += 4) n += (w + 1) * npc / NCW - w * npc / NCW;
-    b = n > b ? n : b;
-  }
-  return b;
-}
-
 struct Plan {
-  int S = 0, X = 0, nblk_max = 0, npc_max = 0, nsr_max = 0, stages = 0;
+  int np = 0, S = 0, X = 0, nblk_max = 0, nsr_max = 0, stages = 0;
   size_t smem = 0;
 };
 
-// The slice count S and cluster count X for NP column pairs: every cluster resident at
-// once, at most NCW * PMAX pairs a CTA, least MMA work on the busiest sub-partition
-// (plus a charge for the cross-CTA sum and the activation fill).
-static bool plan_for(qgemm_device_s* d, int NP, int nkb, int G, int nb, Plan* out) {
+// Cycles per MMA per sub-partition of the main loop at NP pairs a warp (two warps a
+// sub-partition, 32 rows, measured on B200 with the loop alone in shared memory).
+static double loop_cycles_per_mma(int np) {
+  return np == 1 ? 13.0 : np == 2 ? 10.9 : np == 3 ? 10.4 : 9.9;
+}
+
+// The pairs per warp NP and the slice count S for NPT column pairs: every cluster
+// resident at once, the least modelled time (MMA issue on a sub-partition over the
+// slice, plus the fixed cost of the prologue, and of the cross-CTA sum when S > 1).
+static bool plan_for(qgemm_device_s* d, int NPT, int nkb, int G, int nb, Plan* out) {
   const int nq = G == 32 ? 4 : G == 64 ? 2 : 1;
   double best = 1e30;
-  for (int S = 1; S <= MAX_S && S <= nkb; ++S) {
-    const int nblk = (nkb + S - 1) / S;
-    if (nblk > NBLK_MAX) continue;
-    const int maxc = max_clusters(d, S);
-    if (maxc <= 0) continue;
-    int X = NP < maxc ? NP : maxc;
-    int npc = (NP + X - 1) / X;
-    if (npc > NCW * PMAX) continue;
-    X = (NP + npc - 1) / npc;  // the fewest clusters at that width
-    Plan c;
-    c.S = S; c.X = X; c.nblk_max = nblk; c.npc_max = npc;
-    c.nsr_max = (nblk * KB + G - 1) / G + 1;
-    const Smem base = smem_layout(nb, nq, nblk, npc, c.nsr_max, 0);
-    const size_t fixed = base.total;
-    const size_t per = (size_t)npc * 1024;
-    if (fixed + 2 * per > d->smem_optin) continue;
-    int stages = (int)((d->smem_optin - fixed) / per);
-    stages = stages > MAX_STAGES ? MAX_STAGES : stages;
-    stages = stages > nblk ? (nblk > 2 ? nblk : 2) : stages;
-    c.stages = stages;
-    c.smem = smem_layout(nb, nq, nblk, npc, c.nsr_max, stages).total;
-    if (c.smem > d->smem_optin) continue;
-    const double cost = busiest(npc) * (nblk + (S > 1 ? 0.5 : 0.0)) + 0.25 * nblk * nb;
-    if (cost < best) { best = cost; *out = c; }
+  for (int np = 1; np <= PMAX; ++np) {
+    const int npc = NCW * np;
+    const int X = (NPT + npc - 1) / npc;
+    for (int S = 1; S <= MAX_S && S <= nkb; ++S) {
+      const int nblk = (nkb + S - 1) / S;
+      if (nblk > NBLK_MAX) continue;
+      if (X > max_clusters(d, S)) continue;
+      Plan c;
+      c.np = np; c.S = S; c.X = X; c.nblk_max = nblk;
+      c.nsr_max = (nblk * KB + G - 1) / G + 1;
+      const size_t fixed = smem_layout(nb, nq, nblk, npc, c.nsr_max, 0).total;
+      const size_t per = (size_t)npc * 1024;
+      if (fixed + 2 * per > d->smem_optin) continue;
+      int stages = (int)((d->smem_optin - fixed) / per);
+      stages = stages > MAX_STAGES ? MAX_STAGES : stages;
+      stages = stages > nblk ? (nblk > 2 ? nblk : 2) : stages;
+      c.stages = stages;
+      c.smem = smem_layout(nb, nq, nblk, npc, c.nsr_max, stages).total;
+      if (c.smem > d->smem_optin) continue;
+      // two warps a sub-partition, NP pairs, 4 steps x 2 halves x NB MMAs a block
+      const double mma = 2.0 * np * nblk * 8 * nb * loop_cycles_per_mma(np);
+      const double cost = mma + 3000.0 + (S > 1 ? 1500.0 : 0.0);
+      if (cost < best) { best = cost; *out = c; }
+    }
   }
   return best < 1e29;
 }
@@ -578,9 +580,9 @@ qgemm_status launch_w4a16_frag_cluster(qgemm_stream_s* s, const void* x, const v
   if (!w4a16_frag_cluster_fits(N, K))
     return fail(QGEMM_ERR_UNSUPPORTED, "cluster frag path: N %% 16 != 0 or K > %d", NBLK_MAX * MAX_S * KB);
   const int nkb = (K + KB - 1) / KB;
-  const int NP = N / 16;
+  const int NPT = N / 16;
   const int gs = G == 32 ? 1 : G == 64 ? 2 : 4;
-  CUtensorMap tm;  // one box = one block of the widest cluster's column groups
+  CUtensorMap tm;  // one box = one block of one CTA's 2 * 8 NP column groups
   Params p;
   p.N = N; p.K = K; p.G = G; p.zp = zp;
   p.NKB = nkb;
@@ -591,31 +593,30 @@ qgemm_status launch_w4a16_frag_cluster(qgemm_stream_s* s, const void* x, const v
   for (int m0 = 0; m0 < M; m0 += 8 * MAX_NB) {
     const int rows = (M - m0) < 8 * MAX_NB ? (M - m0) : 8 * MAX_NB;
     const int nb = rows <= 8 ? 1 : rows <= 16 ? 2 : 4;
-    const qgemm_status as = set_attr(d, nb, gs);
-    if (as != QGEMM_OK) return as;
     p.M = rows;
     p.x = static_cast<const __nv_bfloat16*>(x) + (size_t)m0 * K;
     p.y = static_cast<__nv_bfloat16*>(y) + (size_t)m0 * N;
     // column chunks: one unless N is wider than every resident cluster can take
     int pc0 = 0;
-    while (pc0 < NP) {
-      int npc_chunk = NP - pc0;
+    while (pc0 < NPT) {
+      int nchunk = NPT - pc0;
       Plan pl;
-      while (!plan_for(d, npc_chunk, nkb, G, nb, &pl)) {
-        if (npc_chunk <= 1)
+      while (!plan_for(d, nchunk, nkb, G, nb, &pl)) {
+        if (nchunk <= 1)
           return fail(QGEMM_ERR_UNSUPPORTED, "no cluster layout fits K=%d in shared memory", K);
-        npc_chunk = (npc_chunk + 1) / 2;
+        nchunk = (nchunk + 1) / 2;
       }
-      if (!map_weights(&tm, wf, nkb, N / 8, 2 * pl.npc_max))
+      const qgemm_status as = set_attr(d, nb, pl.np, gs);
+      if (as != QGEMM_OK) return as;
+      if (!map_weights(&tm, wf, nkb, N / 8, 2 * NCW * pl.np))
         return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for the frag weights");
       p.S = pl.S;
       p.nblk_max = pl.nblk_max;
-      p.npc_max = pl.npc_max;
+      p.npc_max = NCW * pl.np;
       p.nsr_max = pl.nsr_max;
       p.stages = pl.stages;
       p.pair0 = pc0;
-      p.pbase = npc_chunk / pl.X;
-      p.prem = npc_chunk % pl.X;
+      p.pair1 = pc0 + nchunk;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(pl.X, pl.S, 1);
       cfg.blockDim = dim3(THREADS, 1, 1);
@@ -630,9 +631,9 @@ qgemm_status launch_w4a16_frag_cluster(qgemm_stream_s* s, const void* x, const v
       attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 2;
-      cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_for(nb, gs), tm, p);
+      cudaError_t e = cudaLaunchKernelEx(&cfg, kernel_for(nb, pl.np, gs), tm, p);
       if (e != cudaSuccess) return cuda_fail(e, "w4a16_frag_cluster_kernel launch");
-      pc0 += npc_chunk;
+      pc0 += nchunk;
     }
   }
   return QGEMM_OK;
