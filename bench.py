@@ -468,7 +468,8 @@ def library_int8_context(hb, steps):
 
 def w4a16_profile(ops, steps, warmup):
     """The decode GEMV as warmup + steps plain launches each (no graph), for ncu: M = 1
-    on the 64-column-tile kernel, then M = 1 and M = 16 on the fragment order."""
+    on the 64-column-tile kernel, then M = 1, 16 and 32 on the fragment order (M = 32 on
+    the K-split cluster kernel)."""
     import torch
     N, K, G, R = 14336, 4096, 128, 8
     gen = torch.Generator(device="cuda")
@@ -499,8 +500,13 @@ def w4a16_profile(ops, steps, warmup):
     for i in range(warmup + steps):
         ops.w4a16GemmGroupedFrag(x16, wf[i % R], sc[i % R], y16, 16, N, K, zero_point=8,
                                  group_size=G)
+    x32 = torch.randn((32, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y32 = torch.empty((32, N), dtype=torch.bfloat16, device="cuda")
+    for i in range(warmup + steps):
+        ops.w4a16GemmGroupedFrag(x32, wf[i % R], sc[i % R], y32, 32, N, K, zero_point=8,
+                                 group_size=G)
     torch.cuda.synchronize()
-    return {"launches": warmup + steps, "M": [1, 16], "N": N, "K": K}
+    return {"launches": warmup + steps, "M": [1, 16, 32], "N": N, "K": K}
 
 
 def w4a16_decode(ops, peaks):
@@ -811,7 +817,9 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
                     "frac_of_bf16_sustained_peak": flops / t / 1e12 / sustained,
                     "tensor_work_factor": 1 if one_term else 2,
                     "note": ("one term: each int4 weight is expanded to bf16((q - zp) * s), "
-                             "relative weight error <= 2^-9, output within 1e-2 of the oracle"
+                             "relative weight error <= 2^-9; forward error <= 2^-8 of "
+                             "sum |x w| (tested), not within the elementwise 1e-2 gate for "
+                             "outputs far below the output scale"
                              if one_term else
                              "exact weights: each int4 weight is expanded to two bf16 terms "
                              "(hi + lo), so the tensor cores do twice the algorithmic work")}

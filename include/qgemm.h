@@ -268,11 +268,13 @@ QGEMM_API qgemm_status qgemm_prepack_w4_tiled(qgemm_stream_t s, uint64_t wq, uin
 
 /* The same group-wise W4A16 on weights repacked once by qgemm_prepack_w4_frag
  * (fragment order: each SM streams an equal, contiguous share of the columns; the
- * fast decode path).  M <= 4 reads 8-column groups; larger M, when N % 16 == 0 and
- * K <= 4096, reads 16-column pairs in passes of 16 rows (otherwise passes of 4
- * rows).  Requires sm_100, K % 16 == 0, K <= 8192, group_size 32, 64 or a multiple
- * of 128, N % 8 == 0 and 16-byte aligned x, wf and scales; otherwise
- * QGEMM_ERR_UNSUPPORTED.  Deterministic. */
+ * fast decode path).  M <= 4 reads 8-column groups; up to 16 rows with N % 16 == 0
+ * and K <= 4096 read 16-column pairs; more rows, or K past 4096 (past 8192 at
+ * M <= 4), with N % 16 == 0 run a K-split kernel over thread-block clusters in passes
+ * of 32 rows, each weight read once a pass; other shapes run passes of 4 rows.
+ * Requires sm_100, K % 16 == 0, K <= 16384 when N % 16 == 0 and K <= 8192
+ * otherwise, group_size 32, 64 or a multiple of 128, N % 8 == 0 and 16-byte aligned
+ * x, wf and scales; otherwise QGEMM_ERR_UNSUPPORTED.  Deterministic. */
 QGEMM_API qgemm_status qgemm_w4a16_grouped_gemm_frag(qgemm_stream_t s, uint64_t x, uint64_t wf,
                                                      uint64_t scales, int zero_point,
                                                      int group_size, uint64_t y, int M, int N,
