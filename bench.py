@@ -751,7 +751,7 @@ LLAMA_LINEARS = (("qkv", 4096, 12288), ("o", 4096, 4096), ("gate_up", 4096, 2201
                  ("down", 11008, 4096))
 
 
-def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
+def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=50):
     """Quantized linear stack of a Llama-2-7B-shaped decoder: `layers` x {qkv
     4096->12288, o 4096->4096, gate+up 4096->22016, down 11008->4096}, random-init
     int4 group-128 weights (zero point 8, bf16 scales ~U[0.005, 0.02]), bf16
@@ -852,16 +852,18 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=20):
     for _ in range(2):
         g.replay()
     torch.cuda.synchronize()
-    e0.record()
-    for _ in range(decode_steps):
-        g.replay()
-    e1.record()
-    torch.cuda.synchronize()
+    # the legacy-MMA-bound decode follows the SM clock: record it beside the time
+    with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clk:
+        e0.record()
+        for _ in range(decode_steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
     t = e0.elapsed_time(e1) / 1e3 / decode_steps
     bytes_step = weights_bytes + sum(M * K * 2 + M * N * 2 for _, K, N, _, _, _ in W)
     res["decode"] = {"M": M, "ms_per_step": t * 1e3, "GB_s": bytes_step / t / 1e9,
                      "frac_of_hbm": bytes_step / t / 1e9 / peaks["hbm_gbs"],
-                     "bytes_per_step": bytes_step}
+                     "bytes_per_step": bytes_step, "clocks": clk.summary()}
     del g
     q.destroy()
     return res
