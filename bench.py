@@ -876,7 +876,9 @@ def gather_output(st, lo, rank, world, reps=5):
     on one stream; qgemm_w8a8_gemm_allgather_bf16, which gathers chunk i of M rows on a
     second stream while the GEMM of chunk i+1 runs; and its window form, where copy-engine
     copies write each chunk into the peers' outputs.  Every form's output equals the
-    serial one, and rank 0 checks sampled full rows of it against the CPU oracle."""
+    serial one, and rank 0 checks sampled full rows of it against the CPU oracle.  The
+    fused form is one GEMM whose epilogue stores each output chunk into every rank's
+    registered output (TMA stores over NVLink)."""
     import ctypes
     import numpy as np
     import torch
@@ -995,6 +997,25 @@ def gather_output(st, lo, rank, world, reps=5):
                     layers[tag] = tw / reps * 1e3
                     equal[tag] = bool(torch.equal(full, ref))
                     checks[tag] = oracle_ok(full)
+
+                # the fused form: the GEMM's epilogue stores into every rank's window
+                def fused(i):
+                    L.call("qgemm_w8a8_gemm_allgather_fused_bf16", win, st.handle,
+                           A.data_ptr(), B.data_ptr(), B_KN, sA.data_ptr(), sB.data_ptr(),
+                           M, NL, K)
+
+                try:  # a refusal comes before any collective, the same on every rank
+                    full.zero_()
+                    for i in range(2):
+                        fused(i)
+                    tf, _ = timed(fused, reps, world)
+                    layers["fused"] = tf / reps * 1e3
+                    equal["fused"] = bool(torch.equal(full, ref))
+                    checks["fused"] = oracle_ok(full)
+                    res["fused_egress_GB_s_per_rank"] = \
+                        (world - 1) * M * NL * 2 / (tf / reps) / 1e9
+                except L.QGemmError as e:
+                    res["fused_error"] = str(e)
             finally:
                 torch.cuda.synchronize()
                 barrier(world)

@@ -462,6 +462,58 @@ qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, qgemm_strea
   return QGEMM_OK;
 }
 
+// The GEMM and the all-gather as one kernel: the epilogue stores each output chunk into
+// this rank's columns of its own window and, by TMA stores over NVLink from the same
+// staging buffer, into the same columns of every peer's window.  The transfer of a
+// tile overlaps the MMAs of the next (two TMEM accumulators), so the layer takes the
+// longer of the GEMM and this rank's egress (N_local * M * 2 bytes to each of world-1
+// peers) instead of their sum.
+qgemm_status qgemm_w8a8_gemm_allgather_fused_bf16(qgemm_window_t w, qgemm_stream_t s, uint64_t A,
+                                                  uint64_t B, int b_layout, uint64_t sA,
+                                                  uint64_t sB, int M, int N_local, int K) {
+  if (!w || !w->comm || !w->comm->comm) return fail(QGEMM_ERR_BAD_HANDLE, "null window");
+  qgemm_comm_s* c = w->comm;
+  qgemm_status st = enter(s);
+  if (st != QGEMM_OK) return st;
+  if (s->dev != c->dev)
+    return fail(QGEMM_ERR_INVALID_ARG, "stream and communicator are on different devices");
+  if (M < 0 || N_local < 0 || K < 0)
+    return fail(QGEMM_ERR_INVALID_ARG, "bad sizes M=%d N_local=%d K=%d", M, N_local, K);
+  const int world = c->world, rank = c->rank;
+  if (world - 1 > 7)
+    return fail(QGEMM_ERR_UNSUPPORTED, "the fused form stores to at most 7 peers (world %d)", world);
+  const size_t N = (size_t)N_local * world;
+  if ((size_t)M * N * 2 > w->bytes)
+    return fail(QGEMM_ERR_INVALID_ARG, "the window holds %zu bytes; [%d, %zu] bf16 needs %zu",
+                w->bytes, M, N, (size_t)M * N * 2);
+  if (M == 0 || N_local == 0) return QGEMM_OK;
+  if ((st = check_sharded_gemm(A, B, b_layout, sA, sB, K)) != QGEMM_OK) return st;
+  // every check that depends on the shape, before the first collective: the same
+  // verdict on every rank
+  const size_t off = (size_t)rank * N_local * 2;  // this rank's columns, row 0
+  const char* why = nullptr;
+  if (K == 0 || N_local % 8 != 0 ||
+      !w8a8_tcgen05_supported(c->dev, A, B, b_layout == QGEMM_B_KN, w->local + off, QGEMM_BF16,
+                              (int)N, M, N_local, K, &why))
+    return fail(QGEMM_ERR_UNSUPPORTED, "the fused form needs the tcgen05 GEMM with the TMA-store "
+                "epilogue (K > 0, N_local %% 8 == 0)%s%s", why ? ": " : "", why ? why : "");
+  uint64_t peers[7] = {};
+  int np = 0;
+  for (int j = 1; j < world; ++j) peers[np++] = w->peer[(rank + j) % world] + off;
+  // every rank is done with its earlier uses of its window before a peer writes into it
+  if ((st = window_barrier(w, s)) != QGEMM_OK) return abort_after(c, st);
+  st = launch_w8a8_tcgen05_peers(s, reinterpret_cast<const void*>(A),
+                                 reinterpret_cast<const void*>(B), b_layout == QGEMM_B_KN,
+                                 reinterpret_cast<const float*>(sA),
+                                 reinterpret_cast<const float*>(sB),
+                                 reinterpret_cast<void*>(w->local + off), (int)N, M, N_local, K,
+                                 peers, np);
+  if (st != QGEMM_OK) return abort_after(c, st);
+  // every peer's columns have landed here once every rank's GEMM has finished
+  if ((st = window_barrier(w, s)) != QGEMM_OK) return abort_after(c, st);
+  return QGEMM_OK;
+}
+
 size_t qgemm_w8a8_allgather_work_bytes(int world, int chunk_rows, int n_local) {
   if (world < 1 || chunk_rows < 1 || n_local < 1) return 0;
   return (size_t)2 * world * chunk_rows * n_local * 2;

@@ -93,6 +93,10 @@ struct TcArgs {
   void* out = nullptr;
   int out_dtype = QGEMM_F32;
   int ldc = 0;
+  // The same output block in up to 7 peers' windows (same M, N, ldc): each output
+  // chunk is also TMA-stored there (the fused sharded GEMM + all-gather).
+  const void* peer_out[7] = {};
+  int npeer = 0;
   // bf16 / tf32 kinds: v = acc; v = alpha * v (ep_alpha); v += bias[n] (bias);
   // v += beta * out[m, n] (ep_beta, fp32 out), each step rounded on its own.
   float alpha = 1.f, beta = 0.f;
@@ -108,6 +112,13 @@ struct TcArgs {
   size_t scratch_bytes = 0;
 };
 qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a);
+// The W8A8 tcgen05 GEMM with bf16 output whose epilogue also TMA-stores every output
+// chunk into npeer (<= 7) peers' copies of the output block (same ldc): the fused
+// sharded GEMM + all-gather.
+qgemm_status launch_w8a8_tcgen05_peers(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
+                                       const float* sA, const float* sB, void* out, int ldc,
+                                       int M, int N, int K, const uint64_t* peer_out,
+                                       int npeer);
 // Scratch bytes a launch of this shape uses for its last-wave split: the counter block
 // (always counted) and the partial tiles.
 size_t tc_gemm_scratch_bytes(const qgemm_device_s* d, int M, int N, int num_k_blocks,

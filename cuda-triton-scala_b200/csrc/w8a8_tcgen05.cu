@@ -64,8 +64,18 @@ static_assert(STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024 <= SMEM_BYTES,
               "shared memory budget");
 constexpr int GROUP_M = 16;                         // tile raster: 16 m-blocks per group
 
+// The output windows of the other ranks of a column-sharded GEMM (the fused GEMM +
+// all-gather): every output chunk the epilogue stores into this GPU's output is also
+// stored, by the same TMA engine from the same staging buffer, into each peer's window
+// over NVLink (plain TMA stores, no multicast).  npeer = 0 in every other use.
+constexpr int MAX_PEERS = 7;
+struct PeerMaps {
+  CUtensorMap m[MAX_PEERS];
+};
+
 struct Params {
   int M, N, K, ldc;
+  int npeer;       // peer output windows in PeerMaps (0: none)
   int out_dtype;   // QGEMM_F32 / QGEMM_BF16
   int b_kn;        // 1: B is [K,N] (MN-major operand); 0: B is [N,K]
   int num_m_blocks, num_n_blocks, num_k_blocks, num_tiles;
@@ -326,7 +336,7 @@ __device__ __forceinline__ void sum_parts(const int32_t* parts, int nparts, size
 }
 
 __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tmO,
-                                              uint32_t tmem_base, uint32_t acc_col, int q,
+                                              const PeerMaps* pm, uint32_t tmem_base, uint32_t acc_col, int q,
                                               int lane, int row0, int n0, uint32_t stg,
                                               bool elected, int& chunk_seq, bool ok,
                                               const int32_t* parts = nullptr, int nparts = 0,
@@ -420,6 +430,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
     ptx::named_bar_sync(1, 128);
     if (elected && !skip && row0 < p.M && n0 + ch * cwe < p.N) {  // blocks past the edge: nothing to store
       ptx::tma_store_2d(tmO, buf, n0 + ch * cwe, row0);
+      for (int i = 0; i < p.npeer; ++i) ptx::tma_store_2d(&pm->m[i], buf, n0 + ch * cwe, row0);
       ptx::bulk_commit_group();
     }
   }
@@ -431,7 +442,8 @@ template <int KIND>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmO, const Params p) {
+                        const __grid_constant__ CUtensorMap tmO,
+                        const __grid_constant__ PeerMaps pm, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: required by the 128-byte swizzle pattern of TMA and UMMA.
   const uint32_t raw_base = ptx::smem_u32(smem_raw);
@@ -600,7 +612,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is .sync.aligned
       if (!ok && lane == 0 && !*abort_flag) report(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag);
       ptx::tc_fence_after();
-      epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM, nb * BN, stg_base,
+      epilogue_tile(p, &tmO, &pm, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM, nb * BN, stg_base,
                     elected, chunk_seq, ok);
       ptx::tc_fence_before();
       ptx::mbar_arrive(tempty_bar(a));
@@ -645,7 +657,8 @@ template <int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
-                             const __grid_constant__ CUtensorMap tmO, const Params p) {
+                             const __grid_constant__ CUtensorMap tmO,
+                             const __grid_constant__ PeerMaps pm, const Params p) {
   constexpr int BM = pair::BM, BN = pair::BN, STAGES = pair::STAGES;
   constexpr int A_BYTES = pair::A_BYTES, B_BYTES = pair::B_BYTES, STAGE_BYTES = pair::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
@@ -819,8 +832,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         report_pair(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag, rank);
       ptx::tc_fence_after();
       if (part < 0) {
-        epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM + (int)rank * 128,
-                      nb * BN, stg_base, elected, chunk_seq, ok);
+        epilogue_tile(p, &tmO, &pm, tmem_base, (uint32_t)(a * BN), q, lane,
+                      mb * BM + (int)rank * 128, nb * BN, stg_base, elected, chunk_seq, ok);
         ptx::tc_fence_before();
         ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
         continue;
@@ -872,8 +885,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       ptx::named_bar_sync(1, 128);
       const bool ready = ok && *last_flag != 0;
-      epilogue_tile(p, &tmO, tmem_base, (uint32_t)(a * BN), q, lane, mb * BM + (int)rank * 128,
-                    nb * BN, stg_base, elected, chunk_seq, ready,
+      epilogue_tile(p, &tmO, &pm, tmem_base, (uint32_t)(a * BN), q, lane,
+                    mb * BM + (int)rank * 128, nb * BN, stg_base, elected, chunk_seq, ready,
                     p.part + (size_t)tt * p.split_s * slot_ints, p.split_s - 1, slot_ints, true);
       ptx::tc_fence_before();
       ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
@@ -1092,8 +1105,36 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
       p.tma_store = 1;
   }
+  // peer output windows (fused sharded GEMM + all-gather): the same map on each peer's
+  // address; TMA stores only
+  PeerMaps pm;
+  memset(&pm, 0, sizeof(pm));
+  p.npeer = 0;
+  if (a.npeer > 0) {
+    if (a.npeer > MAX_PEERS)
+      return fail(QGEMM_ERR_UNSUPPORTED, "%d peer windows (at most %d)", a.npeer, MAX_PEERS);
+    if (!p.tma_store)
+      return fail(QGEMM_ERR_UNSUPPORTED, "peer windows need the TMA-store epilogue: 16-byte "
+                  "aligned output and rows a multiple of 16 bytes");
+    EncodeTiledFn enc = get_encode_fn();
+    for (int i = 0; i < a.npeer; ++i) {
+      cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+      cuuint64_t strides[1] = {(cuuint64_t)a.ldc * esize};
+      cuuint32_t box[2] = {(cuuint32_t)(128 / esize), 128};
+      cuuint32_t estr[2] = {1, 1};
+      if (!aligned((uint64_t)a.peer_out[i], 16) || !enc ||
+          enc(&pm.m[i], a.out_dtype == QGEMM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+              2, const_cast<void*>(a.peer_out[i]), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for peer window %d", i);
+    }
+    p.npeer = a.npeer;
+  }
 
-  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params);
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const PeerMaps,
+                        const Params);
   static const Kern kerns[2][3] = {
       {w8a8_tcgen05_kernel<KIND_I8>, w8a8_tcgen05_kernel<KIND_BF16>, w8a8_tcgen05_kernel<KIND_TF32>},
       {w8a8_tcgen05_pair_kernel<KIND_I8>, w8a8_tcgen05_pair_kernel<KIND_BF16>,
@@ -1140,7 +1181,7 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, pm, p);
   if (e != cudaSuccess) return cuda_fail(e, "w8a8_tcgen05 launch");
   return QGEMM_OK;
 }
@@ -1160,6 +1201,17 @@ qgemm_status launch_w8a8_tcgen05(qgemm_stream_s* s, const void* A, const void* B
                                  const float* sA, const float* sB, void* out, int out_dtype,
                                  int ldc, int M, int N, int K, int32_t* acc) {
   return launch_tc_gemm(s, w8a8_args(A, B, b_kn, sA, sB, out, out_dtype, ldc, M, N, K, acc));
+}
+
+qgemm_status launch_w8a8_tcgen05_peers(qgemm_stream_s* s, const void* A, const void* B, int b_kn,
+                                       const float* sA, const float* sB, void* out, int ldc,
+                                       int M, int N, int K, const uint64_t* peer_out,
+                                       int npeer) {
+  TcArgs a = w8a8_args(A, B, b_kn, sA, sB, out, QGEMM_BF16, ldc, M, N, K, nullptr);
+  if (npeer < 0 || npeer > 7) return fail(QGEMM_ERR_INVALID_ARG, "npeer %d", npeer);
+  for (int i = 0; i < npeer; ++i) a.peer_out[i] = reinterpret_cast<const void*>(peer_out[i]);
+  a.npeer = npeer;
+  return launch_tc_gemm(s, a);
 }
 
 // With a_repeat = 2, each row of B holds 2 blocks of ceil(2K / 128) * 128 bytes (zero past

@@ -141,6 +141,8 @@ SIGNATURES = {
     "qgemm_comm_window_release": (_S, [_P]),
     "qgemm_w8a8_gemm_allgather_window_bf16": (_S, [_P, _P, _P, _U64, _U64, _I, _U64, _U64, _I,
                                                    _I, _I, _I]),
+    "qgemm_w8a8_gemm_allgather_fused_bf16": (_S, [_P, _P, _U64, _U64, _I, _U64, _U64, _I, _I,
+                                                  _I]),
 }
 
 _lib = None

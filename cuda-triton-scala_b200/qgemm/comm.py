@@ -111,6 +111,15 @@ class OutputWindow:
                L.addr(A), L.addr(B), b_layout, L.addr(sA), L.addr(sB), M, n_local, K,
                chunk_rows)
 
+    def w8a8GemmAllGatherFused(self, s, A, B, sA, sB, M: int, n_local: int, K: int,
+                               b_layout: int = B_KN) -> None:
+        """The GEMM and the gather as one kernel: its epilogue stores each output chunk
+        into every rank's window (TMA stores over NVLink)."""
+        if not self.handle:
+            raise L.QGemmError(L.ERR_BAD_HANDLE, "OutputWindow", "released window")
+        L.call("qgemm_w8a8_gemm_allgather_fused_bf16", self.handle, s.handle, L.addr(A),
+               L.addr(B), b_layout, L.addr(sA), L.addr(sB), M, n_local, K)
+
     def release(self) -> None:
         """Local; call once every rank has finished with the window."""
         if self.handle:

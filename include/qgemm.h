@@ -538,6 +538,26 @@ QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, q
                                                              int N_local, int K,
                                                              int chunk_rows);
 
+/* The sharded GEMM and the all-gather as one kernel, into a registered window
+ * ([M, N_local * world] bf16 on every rank): the GEMM's epilogue stores each output
+ * chunk into this rank's columns of its own window and, with TMA stores over NVLink
+ * from the same staging buffer (no multicast), into the same columns of every peer's
+ * window.  A tile's transfer overlaps the next tile's MMAs, so the layer takes the
+ * longer of the GEMM and this rank's egress instead of their sum; there is no gather
+ * buffer, no copy stream and no unshard pass.  Two one-element NCCL gathers on s
+ * bracket the GEMM: no rank writes into a peer's window before the peer has finished
+ * its earlier work on s, and the call completes on s only when every rank's columns
+ * have arrived.  Requires sm_100, world <= 8, K > 0 with K % 16 == 0, N_local % 8 == 0
+ * and the tcgen05 GEMM's alignments; otherwise QGEMM_ERR_UNSUPPORTED on every rank,
+ * before any collective.  Every rank must make the same calls in the same order, with
+ * the same M, N_local and K.  Errors after the first gather abort the communicator,
+ * as in qgemm_w8a8_gemm_allgather_bf16. */
+QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_fused_bf16(qgemm_window_t w, qgemm_stream_t s,
+                                                            uint64_t A, uint64_t B,
+                                                            int b_layout, uint64_t sA,
+                                                            uint64_t sB, int M, int N_local,
+                                                            int K);
+
 #ifdef __cplusplus
 }
 #endif

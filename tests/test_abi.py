@@ -147,3 +147,9 @@ def test_prefill_workspace_sizes_without_gpu():
     assert L.lib().qgemm_w4a16_prefill_workspace_bytes_ex(64, 64, L.PREFILL_FRAG,
                                                           ctypes.byref(n)) == L.OK
     assert n.value == 256 * 64 * 4
+
+
+def test_fused_gather_rejects_a_null_window_without_gpu():
+    import qgemm._lib as L
+    assert L.lib().qgemm_w8a8_gemm_allgather_fused_bf16(None, None, 16, 16, 0, 16, 16, 64, 64,
+                                                         64) == L.ERR_BAD_HANDLE

@@ -3,9 +3,10 @@
 qgemm_w8a8_gemm_allgather_bf16 runs each rank's GEMM slice chunk by chunk of M and
 all-gathers every chunk over NCCL while the next chunk's GEMM runs (NCCLOps.scala:302-320
 is the reference's all-gather); qgemm_w8a8_gemm_allgather_window_bf16 instead copies each
-chunk into the peers' registered output windows.  Every rank must end with the whole
-[M, N] output, bit for bit the unsharded product from the oracle.  Skipped with fewer
-than two GPUs.
+chunk into the peers' registered output windows; qgemm_w8a8_gemm_allgather_fused_bf16
+stores each output chunk into every rank's window from the GEMM's own epilogue (TMA
+stores over NVLink).  Every rank must end with the whole [M, N] output, bit for bit the
+unsharded product from the oracle.  Skipped with fewer than two GPUs.
 """
 import os
 import sys
@@ -68,15 +69,37 @@ def _rank_main(rank, world, q_id, q_out):
                 ys.append(win_buf.to_numpy(s, np.uint16, (M, N)))
             s.sync()
             cs.sync()
+            # the fused form, twice, each time into a window filled with 0xFFFF first; a
+            # shard of N % 16 == 8 columns has no tcgen05 GEMM on [K,N] weights, and
+            # every rank refuses it before any collective
+            if (n1 - n0) % 16 == 0:
+                for _ in range(2):
+                    s.memset(win_buf.address, 0xFF, M * N * 2)
+                    L.call("qgemm_w8a8_gemm_allgather_fused_bf16", win, s.handle, args[0],
+                           args[1], qgemm.B_KN, args[2], args[3], M, n1 - n0, K)
+                    ys.append(win_buf.to_numpy(s, np.uint16, (M, N)))
+            else:
+                assert L.try_call("qgemm_w8a8_gemm_allgather_fused_bf16", win, s.handle,
+                                  args[0], args[1], qgemm.B_KN, args[2], args[3], M, n1 - n0,
+                                  K) == L.ERR_UNSUPPORTED
+            s.sync()
             L.call("qgemm_comm_window_release", win)
-            results.append((y, ys[0], ys[1]))
+            results.append((y, *ys))
         # refusals, made identically on every rank before any collective
         M, N, K, R = CASES[0]
         st1 = L.try_call("qgemm_w8a8_gemm_allgather_bf16", comm, s.handle, s.handle, 16, 16,
                          qgemm.B_KN, 16, 16, 16, M, N // world, K, R, 256, 1 << 20)
         st2 = L.try_call("qgemm_w8a8_gemm_allgather_bf16", comm, s.handle, cs.handle, 16, 16,
                          qgemm.B_KN, 16, 16, 16, M, N // world, K, R, 256, 64)
-        errors = [st1, st2]
+        # K % 16 != 0: no tcgen05 GEMM, so the fused form refuses before any collective
+        win_buf = qgemm.Buffer(dev, M * N * 2)
+        win = ctypes.c_void_p()
+        L.call("qgemm_comm_window_register", comm, s.handle, win_buf.address, M * N * 2,
+               ctypes.byref(win))
+        st3 = L.try_call("qgemm_w8a8_gemm_allgather_fused_bf16", win, s.handle, 16, 16,
+                         qgemm.B_KN, 16, 16, M, N // world, 8)
+        L.call("qgemm_comm_window_release", win)
+        errors = [st1, st2, st3]
         q_out.put((rank, results, errors))
     except Exception as e:  # report instead of leaving the parent waiting
         q_out.put((rank, None, repr(e)))
@@ -111,9 +134,9 @@ def test_pipelined_gemm_allgather_matches_full(oracle):
         for (M, N, K, _), ys in zip(CASES, results):
             A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K)
             yo, _ = oracle.w8a32_gemm(B, sB, A, sA)
-            for y in ys:  # gather buffers, then the window (twice)
+            for y in ys:  # gather buffers, the window (twice), the fused form (twice)
                 np.testing.assert_array_equal(y, oracle.bf16_rne(yo))
-        assert errors == [L.ERR_INVALID_ARG, L.ERR_INVALID_ARG]
+        assert errors == [L.ERR_INVALID_ARG, L.ERR_INVALID_ARG, L.ERR_UNSUPPORTED]
     for p in procs:
         assert p.exitcode == 0
 
@@ -156,8 +179,11 @@ def _rank_main_facade(rank, world, q_id, q_out):
         win.w8a8GemmAllGather(s, cs, *bufs, M, n1 - n0, K, R)
         yw = win_buf.to_numpy(s, np.uint16, (M, N))
         cs.sync()
+        s.memset(win_buf.address, 0xFF, M * N * 2)
+        win.w8a8GemmAllGatherFused(s, *bufs, M, n1 - n0, K)
+        yf = win_buf.to_numpy(s, np.uint16, (M, N))
         win.release()
-        q_out.put((rank, [(y, yw)], []))
+        q_out.put((rank, [(y, yw, yf)], []))
     except Exception as e:
         q_out.put((rank, None, repr(e)))
     finally:
