@@ -548,8 +548,8 @@ QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_window_bf16(qgemm_window_t w, q
  * bracket the GEMM: no rank writes into a peer's window before the peer has finished
  * its earlier work on s, and the call completes on s only when every rank's columns
  * have arrived.  Requires sm_100, world <= 8, K > 0 with K % 16 == 0, N_local % 8 == 0
- * and the tcgen05 GEMM's alignments; otherwise QGEMM_ERR_UNSUPPORTED on every rank,
- * before any collective.  Every rank must make the same calls in the same order, with
+ * (% 16 with B in [K,N]) and 16-byte aligned A and B; otherwise QGEMM_ERR_UNSUPPORTED,
+ * before any collective (the same verdict on every rank when the shapes agree).  Every rank must make the same calls in the same order, with
  * the same M, N_local and K.  Errors after the first gather abort the communicator,
  * as in qgemm_w8a8_gemm_allgather_bf16. */
 QGEMM_API qgemm_status qgemm_w8a8_gemm_allgather_fused_bf16(qgemm_window_t w, qgemm_stream_t s,
