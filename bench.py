@@ -699,8 +699,8 @@ def f32_facade(st, peaks, steps=10):
 def side_kernels(st, ops, steps, warmup):
     """The facade's smaller kernels on their own, each `warmup` + `steps` launches:
     fp32 gemv A [16384, 16384], per-token quantisation of x [4096, 4096] bf16, the
-    CUDA-core fp32 GEMM at 64 x 4096 x 4096 (the cases profiles/ cite), and w8a16Gemm
-    at 1 x 14336 x 4096."""
+    CUDA-core fp32 GEMM at 64 x 4096 x 4096 (small cases, each one launch that an ncu
+    capture can hold), and w8a16Gemm at 1 x 14336 x 4096."""
     import torch
     import qgemm
     m = qgemm.MatrixOps(st)

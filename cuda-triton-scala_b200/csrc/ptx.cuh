@@ -362,6 +362,19 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// The same with any swizzle mode (bits 61-63): SWZ_128B, or SWZ_64B for 64-byte rows.
+constexpr uint32_t SWZ_128B = 2, SWZ_64B = 4;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint32_t swizzle) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(swizzle & 7u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::i8: s8 x s8 -> s32, M x N tile.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (2u << 4)                        // D format: s32

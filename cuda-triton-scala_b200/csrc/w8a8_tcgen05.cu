@@ -124,13 +124,34 @@ struct Params {
   // Test hook: the final K part of a split tile waits for one count-in more than the
   // other parts make, so that its bounded wait runs out (the timeout path).
   int hold_split;
+  // Column-half tail of the CTA-pair kernel (halves = 1, split_s = 1): the first half_w
+  // tiles are done whole, one per pair per round; each remaining tile is done as two
+  // 256 x 128 items (columns [0,128) and [128,256) of the tile, M=256 N=128 MMAs, B
+  // from the half-width map) on different pairs in the round after them.
+  int halves, half_w;
 };
 
 // Work item i of pair `pair`: a whole tile, or one K part of a tail tile.  Returns
 // false when the pair has no item i.
+// half: -1 for a whole tile or a K part, else which column half of the tile.
 __device__ __forceinline__ bool pair_item(const Params& p, int pair, int npairs, int i,
-                                          int& tile, int& kb0, int& kb1, int& part) {
+                                          int& tile, int& kb0, int& kb1, int& part, int& half) {
   const int T = p.num_m_blocks * p.num_n_blocks;
+  half = -1;
+  if (p.halves) {
+    const int rounds = p.half_w / npairs;  // half_w is a multiple of npairs
+    kb0 = 0;
+    kb1 = p.num_k_blocks;
+    part = -1;
+    if (i < rounds) {
+      tile = pair + i * npairs;
+      return true;
+    }
+    if (i > rounds || pair >= 2 * (T - p.half_w)) return false;
+    tile = p.half_w + pair / 2;
+    half = pair & 1;
+    return true;
+  }
   const int rounds = p.split_w / npairs;  // split_w is a multiple of npairs when splitting
   if (p.split_s <= 1 || i < rounds) {
     tile = pair + i * npairs;
@@ -294,8 +315,8 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int n0, fl
 }
 
 
-// Epilogue of one accumulator: this CTA's 128 rows (row0..row0+127) x 256 columns
-// (n0..n0+255) held in TMEM columns [acc_col, acc_col+256).  Warp q reads TMEM lanes
+// Epilogue of one accumulator: this CTA's 128 rows (row0..row0+127) x ncols (256, or
+// 128 for a column half) columns (n0..) held in TMEM columns [acc_col, acc_col+ncols).  Warp q reads TMEM lanes
 // 32q..32q+31 (one output row per thread), dequantises, and writes 128-byte row pieces
 // into the swizzled staging buffer; one elected thread then stores each 128-row x
 // 128-byte block with a TMA bulk tensor store (clipped at the tensor edges).  `chunk_seq`
@@ -340,14 +361,15 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
                                               int lane, int row0, int n0, uint32_t stg,
                                               bool elected, int& chunk_seq, bool ok,
                                               const int32_t* parts = nullptr, int nparts = 0,
-                                              size_t part_stride = 0, bool add_tmem = false) {
+                                              size_t part_stride = 0, bool add_tmem = false,
+                                              int ncols = 256) {
   const int row = row0 + q * 32 + lane;
   const int rl = q * 32 + lane;  // row within the staging block
   const float sa = (!p.fp_acc && !p.no_out && row < p.M) ? __ldg(p.sA + row) : 0.f;
   const bool skip = p.skip_flag != nullptr && *reinterpret_cast<const volatile int*>(p.skip_flag) != 0;
   if (!p.tma_store) {
 #pragma unroll 1
-    for (int c = 0; c < 256 / 32; ++c) {
+    for (int c = 0; c < ncols / 32; ++c) {
       uint32_t r[32];
       __syncwarp();
       if (!ok) return;
@@ -363,7 +385,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
   const bool bf16 = p.out_dtype == QGEMM_BF16;
   const int cwe = bf16 ? 64 : 32;  // columns per 128-byte staging row
 #pragma unroll 1
-  for (int ch = 0; ch < 256 / cwe; ++ch, ++chunk_seq) {
+  for (int ch = 0; ch < ncols / cwe; ++ch, ++chunk_seq) {
     const uint32_t buf = stg + (uint32_t)(chunk_seq & 1) * (128 * 128);
     // the store issued two chunks ago (same buffer) must have finished reading it
     if (elected) ptx::bulk_wait_group_read<1>();
@@ -442,6 +464,7 @@ template <int KIND>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmBh,
                         const __grid_constant__ CUtensorMap tmO,
                         const __grid_constant__ PeerMaps pm, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -657,6 +680,7 @@ template <int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     w8a8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmBh,
                              const __grid_constant__ CUtensorMap tmO,
                              const __grid_constant__ PeerMaps pm, const Params p) {
   constexpr int BM = pair::BM, BN = pair::BN, STAGES = pair::STAGES;
@@ -700,6 +724,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     ptx::grid_launch_dependents();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
+    if (p.halves) ptx::prefetch_tmap(&tmBh);
   }
   if (warp == 1) {
     ptx::tmem_alloc_pair(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)), TMEM_COLS);
@@ -718,10 +743,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      int tile, kb0, kb1, part;
-      for (int item = 0; ok && pair_item(p, pair_id, npairs, item, tile, kb0, kb1, part); ++item) {
+      int tile, kb0, kb1, part, half;
+      for (int item = 0; ok && pair_item(p, pair_id, npairs, item, tile, kb0, kb1, part, half); ++item) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
+        // B per CTA: 128 columns of the tile, or 64 columns of one column half (the
+        // half-width map: [K,N] boxes 64 columns x 128 k-rows with the 64-byte swizzle,
+        // [N,K] boxes 128 k-bytes x 64 rows)
+        const bool hf = half >= 0;
+        const void* bmap = hf ? (const void*)&tmBh : (const void*)&tmB;
+        const int bcol = nb * BN + (hf ? half * 128 + (int)rank * 64 : (int)rank * 128);
+        const uint32_t tx = hf ? 2u * (A_BYTES + B_BYTES / 2) : 2u * STAGE_BYTES;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_ns)) {
             if (!*abort_flag) report_pair(p.err, DEVERR_TIMEOUT_PRODUCER, abort_flag, rank);
@@ -733,12 +765,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t fb = ptx::map_to_rank(full_bar(stage), 0);
           int akb, bkb;
           seg_blocks(p, kb, akb, bkb);
-          if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+          if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), tx);
           ptx::tma_load_2d_pair(sa, &tmA, fb, akb * BK, mb * BM + (int)rank * 128);
           if (p.b_kn)
-            ptx::tma_load_2d_pair(sb, &tmB, fb, nb * BN + (int)rank * 128, kb * BK);
+            ptx::tma_load_2d_pair(sb, bmap, fb, bcol, kb * BK);
           else
-            ptx::tma_load_2d_pair(sb, &tmB, fb, bkb * BK, nb * BN + (int)rank * 128);
+            ptx::tma_load_2d_pair(sb, bmap, fb, bkb * BK, bcol);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -756,16 +788,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA) ----------------
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = KIND == KIND_BF16   ? ptx::idesc_bf16(BM, BN)
-                             : KIND == KIND_TF32 ? ptx::idesc_tf32(BM, BN)
-                                                 : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc_w = KIND == KIND_BF16   ? ptx::idesc_bf16(BM, BN)
+                               : KIND == KIND_TF32 ? ptx::idesc_tf32(BM, BN)
+                                                   : ptx::idesc_i8(BM, BN, false, p.b_kn != 0);
+      const uint32_t idesc_h = KIND == KIND_BF16   ? ptx::idesc_bf16(BM, BN / 2)
+                               : KIND == KIND_TF32 ? ptx::idesc_tf32(BM, BN / 2)
+                                                   : ptx::idesc_i8(BM, BN / 2, false, p.b_kn != 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       bool issued_any = false;
-      int tile, kb0, kb1, part;
-      for (; ok && pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part); ++it) {
+      int tile, kb0, kb1, part, half;
+      for (; ok && pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part, half); ++it) {
+        // B operand of this item.  [K,N] (MN-major): one 128-column swizzle row per CTA
+        // (128-byte swizzle, k-row groups 1024 bytes apart), or for a column half one
+        // 64-column row (64-byte swizzle, groups 512 bytes apart); the leading offset
+        // is the B region's size, which no read reaches with a single MN atom.  [N,K]
+        // (K-major): 128 or 64 rows of 128 k-bytes, the same descriptor.
+        const bool hf = half >= 0;
+        const uint32_t idesc = hf ? idesc_h : idesc_w;
+        const uint32_t b_row = p.b_kn ? (hf ? 64u : 128u) : 1u;  // bytes per k of B
+        const uint32_t b_lbo = p.b_kn ? (uint32_t)B_BYTES : 16u;
+        const uint32_t b_sbo = p.b_kn ? 8u * b_row : 1024u;
+        const uint32_t b_swz = (p.b_kn && hf) ? ptx::SWZ_64B : ptx::SWZ_128B;
         const int a = it & 1;
         const uint32_t aphase = (uint32_t)((it >> 1) & 1);
         if (!ptx::mbar_wait(tempty_bar(a), aphase ^ 1u, abort_flag, p.wait_ns)) {
@@ -787,9 +833,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             const uint64_t adesc = ptx::smem_desc_sw128(sa + kk * UMMA_K, 16, 1024);
-            // B per CTA: 128 columns = one 128-byte swizzle row in either layout.
-            const uint64_t bdesc = p.b_kn ? ptx::smem_desc_sw128(sb + kk * UMMA_K * 128, B_BYTES, 1024)
-                                          : ptx::smem_desc_sw128(sb + kk * UMMA_K, 16, 1024);
+            const uint64_t bdesc = ptx::smem_desc(sb + kk * UMMA_K * b_row, b_lbo, b_sbo, b_swz);
             const uint32_t accum = (kb != kb0 || kk != 0) ? 1u : 0u;
             if constexpr (KIND == KIND_BF16)
               ptx::umma_bf16_pair(d_tmem, adesc, bdesc, idesc, accum);
@@ -820,8 +864,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     volatile int* last_flag = abort_flag + 1;
     const int rl = q * 32 + lane;  // row of this CTA's half-tile
     int it = 0;
-    int tile, kb0, kb1, part;
-    for (; pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part); ++it) {
+    int tile, kb0, kb1, part, half;
+    for (; pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part, half); ++it) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int a = it & 1;
@@ -833,7 +877,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       ptx::tc_fence_after();
       if (part < 0) {
         epilogue_tile(p, &tmO, &pm, tmem_base, (uint32_t)(a * BN), q, lane,
-                      mb * BM + (int)rank * 128, nb * BN, stg_base, elected, chunk_seq, ok);
+                      mb * BM + (int)rank * 128, nb * BN + (half > 0 ? BN / 2 : 0), stg_base,
+                      elected, chunk_seq, ok, nullptr, 0, 0, false, half >= 0 ? BN / 2 : BN);
         ptx::tc_fence_before();
         ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
         continue;
@@ -928,7 +973,8 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 static bool make_map_u8(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
-                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -936,7 +982,7 @@ static bool make_map_u8(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -964,6 +1010,7 @@ struct TcPlan {
   int grid;
   int num_tiles;
   int split_w, split_s;   // as in Params; split_s = 1: no split
+  int halves, half_w;     // as in Params; halves = 0: whole tiles only
   size_t cnt_bytes;       // counter block at the start of the scratch
   size_t part_bytes;      // partial tiles after it (0: no split)
 };
@@ -983,6 +1030,8 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, b
   t.num_tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
   t.split_w = t.num_tiles;
   t.split_s = 1;
+  t.halves = 0;
+  t.half_w = t.num_tiles;
   // The counter block has one fixed size on a device (counters for up to
   // 2 * max_pairs half-tiles; rest < max_pairs) and is counted in every plan, so that
   // callers which carve their own buffers out of the stream's scratch never place them
@@ -1011,6 +1060,13 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, b
       return t;
     }
   }
+  if (t.num_tiles < max_pairs && 2 * t.num_tiles <= max_pairs) {
+    // fewer tiles than half the pairs: every tile as two column halves, one per pair
+    t.halves = 1;
+    t.half_w = 0;
+    t.grid = 4 * t.num_tiles;
+    return t;
+  }
   const int pairs = t.num_tiles < max_pairs ? t.num_tiles : max_pairs;
   t.grid = 2 * pairs;
   // Last-wave split: when the final round would leave at least three quarters of the
@@ -1027,6 +1083,12 @@ static TcPlan tc_plan(const qgemm_device_s* d, int M, int N, int num_k_blocks, b
     t.split_w = rounds * pairs;
     t.split_s = parts;
     t.part_bytes = (size_t)rest * 2 * parts * 128 * 256 * sizeof(int32_t);
+  } else if (rounds >= 1 && rest > 0 && 2 * rest <= pairs) {
+    // Column-half tail: the leftover tiles as 256 x 128 halves on twice as many pairs,
+    // so the last round takes about half as long (4096^3: 34 leftover tiles on 74
+    // pairs become 68 halves).  No scratch.
+    t.halves = 1;
+    t.half_w = rounds * pairs;
   }
   return t;
 }
@@ -1059,6 +1121,15 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   bool okb = a.b_kn ? make_map_u8(&tmB, a.B, (uint64_t)N, (uint64_t)K, kn_pitch, 128, BK)
                     : make_map_u8(&tmB, a.B, b_pitch, (uint64_t)N, b_pitch, BK, nk_rows);
   if (!okb) return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for B");
+  // half-width B boxes for the column-half items of the pair kernel
+  CUtensorMap tmBh;
+  memset(&tmBh, 0, sizeof(tmBh));
+  if (use_pair && t.halves) {
+    okb = a.b_kn ? make_map_u8(&tmBh, a.B, (uint64_t)N, (uint64_t)K, kn_pitch, 64, BK,
+                               CU_TENSOR_MAP_SWIZZLE_64B)
+                 : make_map_u8(&tmBh, a.B, b_pitch, (uint64_t)N, b_pitch, BK, 64);
+    if (!okb) return fail(QGEMM_ERR_CUDA, "cuTensorMapEncodeTiled failed for the B half map");
+  }
 
   Params p;
   p.M = M; p.N = N; p.K = K; p.ldc = a.ldc;
@@ -1133,8 +1204,8 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
     p.npeer = a.npeer;
   }
 
-  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const PeerMaps,
-                        const Params);
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                        const PeerMaps, const Params);
   static const Kern kerns[2][3] = {
       {w8a8_tcgen05_kernel<KIND_I8>, w8a8_tcgen05_kernel<KIND_BF16>, w8a8_tcgen05_kernel<KIND_TF32>},
       {w8a8_tcgen05_pair_kernel<KIND_I8>, w8a8_tcgen05_pair_kernel<KIND_BF16>,
@@ -1150,6 +1221,8 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   }
   p.split_w = t.num_tiles;
   p.split_s = 1;
+  p.halves = t.halves;
+  p.half_w = t.half_w;
   p.part = nullptr;
   p.cnt = nullptr;
   if (t.split_s > 1) {
@@ -1181,7 +1254,7 @@ qgemm_status launch_tc_gemm(qgemm_stream_s* s, const TcArgs& a) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, pm, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmBh, tmO, pm, p);
   if (e != cudaSuccess) return cuda_fail(e, "w8a8_tcgen05 launch");
   return QGEMM_OK;
 }

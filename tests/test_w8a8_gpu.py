@@ -85,13 +85,16 @@ def test_tcgen05_cta_pair_shapes(gpu, oracle, M, N, K, layout):
     (3840, 1280, 1024, qgemm.B_KN, qgemm.BF16, None),   # 75 pair tiles: one tile in 4 K parts
     (3840, 1536, 1024, qgemm.B_NK, qgemm.BF16, None),   # 90 tiles: 16 leftover tiles in 4 parts
     (3840, 1280, 1024, qgemm.B_KN, qgemm.F32, 1281),    # parts summed on the plain-store path
-    (4096, 4096, 512, qgemm.B_NK, qgemm.BF16, None),    # 256 tiles: last round left whole
+    (4096, 4096, 512, qgemm.B_NK, qgemm.BF16, None),    # 256 tiles: 34 leftover as 68 column halves
     (2048, 6144, 1024, qgemm.B_KN, qgemm.F32, 6150),    # 192 tiles: last round left whole
+    (3840, 4224, 512, qgemm.B_KN, qgemm.BF16, None),    # 255 tiles: 33 leftover as halves, the
+    (3840, 4224, 640, qgemm.B_NK, qgemm.F32, 4230),     # last tile column's second half past N
 ])
 def test_tcgen05_last_wave_split(gpu, oracle, M, N, K, layout, out_dtype, ldc):
-    """The last-wave split (tail tiles cut along K over idle CTA pairs, int32 partials
-    summed by the last part) gives the same bits as the CUDA-core kernel, and the
-    sampled rows equal the oracle; run twice to check that the counters reset."""
+    """The last-wave forms (tail tiles cut along K over idle CTA pairs, int32 partials
+    summed by the last part; or done as 256 x 128 column halves) give the same bits as
+    the CUDA-core kernel, and the sampled rows equal the oracle; run twice to check
+    that the counters reset."""
     A, B, sA, sB = syn.w8a8_inputs(M, N, K, seed=M + N + K + 5)
     y1, a1 = run(gpu, A, B, sA, sB, layout=layout, out_dtype=out_dtype, ldc=ldc,
                  algo=qgemm.ALGO_TCGEN05)

@@ -25,7 +25,7 @@ def gemm(gpu, fn, A, B, sA, sB, M, N, K, layout):
 @pytest.mark.parametrize("M,N,K,layout", [
     (3840, 1280, 1024, qgemm.B_KN),   # 75 pair tiles: the leftover tile is split in 4
     (3840, 1536, 1024, qgemm.B_NK),   # 90 pair tiles: 16 leftover tiles split in 4
-    (4096, 4096, 512, qgemm.B_KN),    # no split
+    (4096, 4096, 512, qgemm.B_KN),    # no split (34 leftover tiles as column halves)
     (200, 512, 256, qgemm.B_NK),      # 1-CTA tiles
 ])
 def test_static_scratch_matches_default_twice(gpu, M, N, K, layout):
