@@ -756,7 +756,8 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=50):
     4096->12288, o 4096->4096, gate+up 4096->22016, down 11008->4096}, random-init
     int4 group-128 weights (zero point 8, bf16 scales ~U[0.005, 0.02]), bf16
     activations ~N(0,1).  Prefill: batch x seq = 32 x 512 = 16384 rows through the
-    prefill path, with the exact two-term weight expansion and with the one-term one;
+    prefill path, with the exact expansion (q - zp in the slab, the group scales applied
+    in fp32 to each group's partial sums) and with the one-term one;
     decode: 32 rows through the decode kernel (one CUDA graph per step).  One step =
     every linear of every layer once.  Each weight is stored once, in the fragment order
     (qgemm_prepack_w4_frag); prefill and decode read that copy."""
@@ -815,14 +816,15 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=50):
         res[key] = {"M": M, "ms_per_step": t * 1e3, "TFLOPs": flops / t / 1e12,
                     "algorithmic_flop_per_step": flops,
                     "frac_of_bf16_sustained_peak": flops / t / 1e12 / sustained,
-                    "tensor_work_factor": 1 if one_term else 2,
+                    "tensor_work_factor": 1,
                     "note": ("one term: each int4 weight is expanded to bf16((q - zp) * s), "
                              "relative weight error <= 2^-9; forward error <= 2^-8 of "
                              "sum |x w| (tested), not within the elementwise 1e-2 gate for "
                              "outputs far below the output scale"
                              if one_term else
-                             "exact weights: each int4 weight is expanded to two bf16 terms "
-                             "(hi + lo), so the tensor cores do twice the algorithmic work")}
+                             "exact: q - zp (exact in bf16) in the slab, the group-128 "
+                             "scales applied in fp32 to each group's tensor-core partial "
+                             "sums by the epilogue warps (one pass over K)")}
     del xs, ys, ws
     torch.cuda.empty_cache()
 

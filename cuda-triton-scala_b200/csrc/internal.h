@@ -198,6 +198,15 @@ qgemm_status launch_prepack_w4_frag(qgemm_stream_s* s, const uint32_t* src, uint
                                     int N);
 // terms: bf16 values per expanded weight (2: exact hi + lo, 1: bf16((q - zp) * s))
 size_t w4a16_prefill_workspace_bytes(int K, int N, int terms);
+// The group-scaled multiply of the prefill path (w4a16_prefill_gs.cu): y[M, ldc] (bf16) =
+// sum_g s[g, n] * (x[:, group g] * slab[n, group g]^T), the slab holding q - zp as bf16
+// [N rows, slab_pitch bytes], scales bf16 with row pitch ld_s (elements).  Needs
+// w4a16_gs_supported (sm_100, G % 64 == 0, 16-byte aligned scales), K % 8 == 0,
+// N % 8 == 0, ldc % 8 == 0 and 16-byte aligned x, slab, y.
+bool w4a16_gs_supported(const qgemm_device_s* d, int G, uint64_t scales);
+qgemm_status launch_w4a16_gs_gemm(qgemm_stream_s* s, const void* x, const void* slab,
+                                  size_t slab_pitch, const void* scales, long long ld_s, int G,
+                                  void* y, int ldc, int M, int N, int K);
 // frag: wt is in the fragment order of qgemm_prepack_w4_frag instead of 64-column tiles
 qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_t* wt,
                                   const void* scales, int zp, int G, void* y, int M, int N,

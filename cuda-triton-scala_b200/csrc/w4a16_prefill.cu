@@ -21,8 +21,12 @@
 //     error at most 2^-9 per weight) and the GEMM runs once over K: the algorithmic
 //     tensor work, half the workspace, and a relative output error of about 2^-9 / 2
 //     on average against the exact sum.
-// The expansion costs 2.5 (one term) or 4.5 bytes of HBM traffic per weight against
-// 4 * M multiply-adds.
+//   * integer (the exact form when group_size % 64 == 0): the slab holds q - zp as bf16
+//     (exact), and the group-scaled multiply (w4a16_prefill_gs.cu) applies s[g, n] in
+//     fp32 to each group's tensor-core partial sums: exact products and fp32 sums with
+//     one pass over K, and no rounding of the scaled weight.
+// The expansion costs 2.5 (one term, integer) or 4.5 bytes of HBM traffic per weight
+// against 4 * M multiply-adds.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -36,15 +40,24 @@ constexpr int TWB = 32;   // bytes of a tile row
 constexpr int KR = 128;   // weight rows per CTA
 constexpr int PAD = 8;    // bf16 padding per transposed row (keeps rows 16-byte aligned)
 
+// MODE: 0 = q - zp (exact, no scale), 1 = bf16((q - zp) * s), 2 = hi + lo.
+template <int MODE> struct SlabMode {
+  static constexpr int TERMS = MODE == 2 ? 2 : 1;  // bf16 values per weight in the slab
+};
+__device__ __forceinline__ float slab_value(int mode, float q, float zp, float sc) {
+  return mode == 0 ? q - zp : (q - zp) * sc;  // exact in fp32
+}
+
 // One CTA: one 64-column tile x 128 rows of the tiled weights -> rows n of the slab,
-// dst[n - n0][k] = hi and, with TERMS = 2, dst[n - n0][Kp + k] = lo (bf16, row pitch
-// TERMS * Kp, Kp = K rounded up to 64, zeros in between).  Thread t dequantises half a
-// row (32 columns, one 16-byte load) into the transposed shared tiles; then each warp
-// writes eight slab rows, 256 bytes of each term.
-template <int TERMS>
+// dst[n - n0][k] = hi (or q - zp) and, with MODE = 2, dst[n - n0][Kp + k] = lo (bf16,
+// row pitch TERMS * Kp, Kp = K rounded up to 64, zeros in between).  Thread t
+// dequantises half a row (32 columns, one 16-byte load) into the transposed shared
+// tiles; then each warp writes eight slab rows, 256 bytes of each term.
+template <int MODE>
 __global__ void __launch_bounds__(256) dequant_slab_kernel(
     const uint8_t* __restrict__ wt, const __nv_bfloat16* __restrict__ scales, int zp, int G,
     __nv_bfloat16* __restrict__ dst, int K, int Kp, int N, int n0, int ncols) {
+  constexpr int TERMS = SlabMode<MODE>::TERMS;
   __shared__ __align__(16) __nv_bfloat16 tr[2][TW][KR + PAD];  // 34.8 KB
   const int tile = n0 / TW + blockIdx.x;
   const int k0 = blockIdx.y * KR;
@@ -63,7 +76,7 @@ __global__ void __launch_bounds__(256) dequant_slab_kernel(
         float v = 0.f;
         if (tile * TW + c < N) {
           const float q = (float)((wv[j] >> (4 * e)) & 0xFu);
-          v = (q - fzp) * __bfloat162float(srow[8 * j + e]);  // exact in fp32
+          v = slab_value(MODE, q, fzp, MODE == 0 ? 1.f : __bfloat162float(srow[8 * j + e]));
         }
         const __nv_bfloat16 hi = __float2bfloat16_rn(v);
         tr[0][c][r] = hi;
@@ -96,10 +109,11 @@ __global__ void __launch_bounds__(256) dequant_slab_kernel(
 // 4i).  One CTA: 8 consecutive column groups (64 columns) x one 128-row block; thread
 // 32u + lane loads that lane's 16 bytes of unit u and places its 32 weights in the
 // transposed shared tiles; the write-out is the one above.
-template <int TERMS>
+template <int MODE>
 __global__ void __launch_bounds__(256) dequant_slab_frag_kernel(
     const uint4* __restrict__ wf, const __nv_bfloat16* __restrict__ scales, int zp, int G,
     __nv_bfloat16* __restrict__ dst, int K, int Kp, int N, int NKB, int n0, int ncols) {
+  constexpr int TERMS = SlabMode<MODE>::TERMS;
   __shared__ __align__(16) __nv_bfloat16 tr[2][TW][KR + PAD];  // 34.8 KB
   const int col0 = n0 + blockIdx.x * TW;  // first column of this CTA (a multiple of 8)
   const int kb = blockIdx.y, k0 = kb * KR;
@@ -118,13 +132,14 @@ __global__ void __launch_bounds__(256) dequant_slab_frag_kernel(
   for (int s = 0; s < 4; ++s) {
     const int rb = 32 * s + 8 * t;        // this lane's 8 rows of step s: rb .. rb+7
     const int grow = (k0 + rb) / G;       // one scale group (G >= 32 and G | 32s)
-    const float sc = (n < N && k0 + rb < K && grow < srows)
+    const float sc = MODE == 0 ? 1.f
+                     : (n < N && k0 + rb < K && grow < srows)
                          ? __bfloat162float(scales[(size_t)grow * N + n]) : 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = rb + off[i];
       float v = 0.f;
-      if (n < N && k0 + r < K) v = ((float)((wv[s] >> (4 * i)) & 0xFu) - fzp) * sc;  // exact
+      if (n < N && k0 + r < K) v = slab_value(MODE, (float)((wv[s] >> (4 * i)) & 0xFu), fzp, sc);
       const __nv_bfloat16 hi = __float2bfloat16_rn(v);
       tr[0][c][r] = hi;
       if (TERMS == 2) tr[1][c][r] = __float2bfloat16_rn(v - __bfloat162float(hi));  // exact
@@ -163,10 +178,15 @@ qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_
                                   int K, void* ws, size_t ws_bytes, bool frag, int terms) {
   using namespace w4p;
   if (terms != 1 && terms != 2) return fail(QGEMM_ERR_INVALID_ARG, "terms %d", terms);
+  // The exact form: integer slab + group-scaled multiply where the group size and the
+  // scales' alignment allow it, hi + lo otherwise.
+  const bool gs = terms == 2 && w4a16_gs_supported(s->dev, G, (uint64_t)scales);
+  const int mode = gs ? 0 : terms;
+  const int slab_terms = mode == 2 ? 2 : 1;
   // slab width: as many columns as the workspace holds, a multiple of 256 (so that
   // every slab but the last fills whole 256-column GEMM tiles)
   const size_t Kp = padded_k(K);
-  const size_t row_bytes = Kp * 2 * (size_t)terms;
+  const size_t row_bytes = Kp * 2 * (size_t)slab_terms;
   size_t cols = ws_bytes / row_bytes;
   cols = cols / 256 * 256;
   if (cols == 0) {
@@ -183,27 +203,44 @@ qgemm_status launch_w4a16_prefill(qgemm_stream_s* s, const void* x, const uint8_
     const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(scales);
     const int nkb = (K + KR - 1) / KR;
     // frag: Kp rounds K up to 64, the layout to 128: the grid's blocks are the layout's
-    if (frag && terms == 2)
-      dequant_slab_frag_kernel<2><<<grid2, 256, 0, s->stream>>>(wf, sc, zp, G, slab, K, (int)Kp,
-                                                                  N, nkb, (int)n0, ncols);
-    else if (frag)
-      dequant_slab_frag_kernel<1><<<grid2, 256, 0, s->stream>>>(wf, sc, zp, G, slab, K, (int)Kp,
-                                                                  N, nkb, (int)n0, ncols);
-    else if (terms == 2)
-      dequant_slab_kernel<2><<<grid2, 256, 0, s->stream>>>(wt, sc, zp, G, slab, K, (int)Kp, N,
-                                                             (int)n0, ncols);
-    else
-      dequant_slab_kernel<1><<<grid2, 256, 0, s->stream>>>(wt, sc, zp, G, slab, K, (int)Kp, N,
-                                                             (int)n0, ncols);
+    if (frag) {
+      if (mode == 0)
+        dequant_slab_frag_kernel<0><<<grid2, 256, 0, s->stream>>>(wf, sc, zp, G, slab, K,
+                                                                    (int)Kp, N, nkb, (int)n0, ncols);
+      else if (mode == 1)
+        dequant_slab_frag_kernel<1><<<grid2, 256, 0, s->stream>>>(wf, sc, zp, G, slab, K,
+                                                                    (int)Kp, N, nkb, (int)n0, ncols);
+      else
+        dequant_slab_frag_kernel<2><<<grid2, 256, 0, s->stream>>>(wf, sc, zp, G, slab, K,
+                                                                    (int)Kp, N, nkb, (int)n0, ncols);
+    } else {
+      if (mode == 0)
+        dequant_slab_kernel<0><<<grid2, 256, 0, s->stream>>>(wt, sc, zp, G, slab, K, (int)Kp, N,
+                                                               (int)n0, ncols);
+      else if (mode == 1)
+        dequant_slab_kernel<1><<<grid2, 256, 0, s->stream>>>(wt, sc, zp, G, slab, K, (int)Kp, N,
+                                                               (int)n0, ncols);
+      else
+        dequant_slab_kernel<2><<<grid2, 256, 0, s->stream>>>(wt, sc, zp, G, slab, K, (int)Kp, N,
+                                                               (int)n0, ncols);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "dequant_slab launch");
+    if (gs) {
+      // y[:, n0 .. n0+ncols) = sum_g s[g, n] * (x * slab^T over group g)
+      const qgemm_status st = launch_w4a16_gs_gemm(s, x, slab, row_bytes, sc + n0, (long long)N,
+                                                   G, static_cast<__nv_bfloat16*>(y) + n0, N, M,
+                                                   ncols, K);
+      if (st != QGEMM_OK) return st;
+      continue;
+    }
     // y[:, n0 .. n0+ncols) = x * slab^T over one segment (hi) or two (hi, then lo)
     TcArgs a;
     a.kind = KIND_BF16;
     a.A = x; a.B = slab;
     a.M = M; a.N = ncols; a.K = 2 * K;
-    a.nseg = terms;
-    a.b_seg = terms == 2 ? 0x2u : 0u;
+    a.nseg = slab_terms;
+    a.b_seg = slab_terms == 2 ? 0x2u : 0u;
     a.b_pitch = row_bytes;
     a.out = static_cast<__nv_bfloat16*>(y) + n0; a.out_dtype = QGEMM_BF16; a.ldc = N;
     const qgemm_status st = launch_tc_gemm(s, a);

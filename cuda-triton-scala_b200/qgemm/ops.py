@@ -112,9 +112,10 @@ class QuantizedGemmOps:
                                 workspace_bytes: int, *, zero_point: int = 8,
                                 group_size: int = 128, one_term: bool = False):
         """Group-wise W4A16 for prefill-sized M on prepackW4Tiled weights: bf16 slabs
-        expanded in `workspace`, then the tensor-core bf16 GEMM.  Each weight is
-        expanded exactly (hi + lo), or with one_term to bf16((q - zp) * s) alone (half
-        the tensor work; relative weight error <= 2^-9)."""
+        expanded in `workspace`, then the tensor-core bf16 GEMM.  Exact by default: q - zp
+        in the slab and the group scales applied in fp32 to each group's partial sums
+        (group_size a multiple of 64, 16-byte aligned scales), else hi + lo per weight;
+        with one_term, bf16((q - zp) * s) alone (relative weight error <= 2^-9)."""
         if one_term:
             L.call("qgemm_w4a16_grouped_gemm_prefill_ex", self._h, L.addr(x), L.addr(wt),
                    L.addr(scales), zero_point, group_size, L.addr(y), M, N, K,

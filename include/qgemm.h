@@ -292,9 +292,12 @@ QGEMM_API qgemm_status qgemm_prepack_w4_frag(qgemm_stream_t s, uint64_t wq, uint
 
 /* Group-wise W4A16 GEMM for prefill-sized M (the same arithmetic as
  * qgemm_w4a16_grouped_gemm on the same prepacked weights `wt`): the weights are
- * expanded slab by slab into the caller's workspace, each (q - zero_point) * scale
- * as two bf16 values hi + lo that sum to it exactly, and multiplied on the tensor
- * cores with fp32 sums (twice the algorithmic tensor work; the products are exact).
+ * expanded slab by slab into the caller's workspace and multiplied on the tensor
+ * cores with exact products and fp32 sums.  When group_size is a multiple of 64 and
+ * `scales` is 16-byte aligned, the slab holds q - zero_point (exact in bf16) and the
+ * scales are applied in fp32 to each group's partial sums (the algorithmic tensor
+ * work); otherwise each (q - zero_point) * scale is stored as two bf16 values hi + lo
+ * that sum to it exactly (twice the tensor work).  The two forms round differently.
  * Any M; meant for M in the hundreds and above, where the expansion is a few percent
  * of the call.  workspace: 16-byte aligned, at least 1024 * Kp bytes (one 256-column
  * slab; Kp = K rounded up to a multiple of 64); qgemm_w4a16_prefill_workspace_bytes

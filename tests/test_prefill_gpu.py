@@ -3,9 +3,11 @@
 * bf16 GEMM: against a float64 numpy product of the same bf16 operands (exact
   products; only the fp32 summation order and the final bf16 rounding differ), max
   elementwise relative error <= 1e-2 (helpers.rel_err);
-* prefill W4A16 (QuantizedGemmOps.scala:229-245 generalised to groups), exact two-term
-  expansion: against the CPU oracle, <= 1e-2; results do not depend on the slab width
-  the workspace allows;
+* prefill W4A16 (QuantizedGemmOps.scala:229-245 generalised to groups), exact
+  expansion: q - zp in the slab and the group scales applied in fp32 to each group's
+  tensor-core partial sums (group sizes that are multiples of 64, 16-byte aligned
+  scales), else the two-term hi + lo slab; against the CPU oracle, <= 1e-2; results do
+  not depend on the slab width the workspace allows;
 * the one-term expansion (bf16((q - zp) * s), relative weight error <= 2^-9) is gated on
   the forward error of a floating-point GEMM instead, max |y - exact| / sum_k |x w| <=
   2^-8 + K 2^-24 (helpers.gemm_bound_ratio): its weight roundings are relative to each
@@ -78,6 +80,8 @@ def prefill(gpu, x, wq, sc, M, N, K, G, zp=8, ws_bytes=None, one_term=False):
     (64, 4096, 4096, 128, 8),    # small M: 1-CTA tiles
     (1, 264, 512, 16, 0),
     (260, 4096, 11008, 128, 8),  # Llama-2-7B down projection (K not a multiple of 256)
+    (300, 520, 1024, 128, 5),    # group-scaled: the last tile's columns past N
+    (520, 2304, 1536, 192, 8),   # group-scaled: three k-blocks a group
 ])
 def test_prefill_vs_oracle(gpu, oracle, M, N, K, G, zp):
     x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=M + N + K + G)
@@ -95,6 +99,31 @@ def test_prefill_large_sampled_rows(gpu, oracle):
                                      [0, 255, 256, M - 1]]))
     ref, _ = oracle.w4a16_grouped(wq, sc, 8, G, x[rows])
     assert rel_err(syn.bf16_to_float(y[rows]), ref) <= TOL_BF16
+
+
+def test_prefill_unaligned_scales_take_the_two_term_form(gpu, oracle):
+    """Scales that are not 16-byte aligned go through the hi + lo slab instead of the
+    group-scaled multiply: both within the tolerance of the oracle, different bits."""
+    M, N, K, G = 300, 512, 1024, 128
+    x, wq, sc = syn.w4a16_inputs(M, N, K, group=G, seed=77)
+    dev, st, ops = gpu
+    y_gs = prefill(gpu, x, wq, sc, M, N, K, G)
+    wt = Out(dev, st, ops.w4TiledBytes(K, N))
+    ops.prepackW4Tiled(dev_array(gpu, wq), wt, K, N)
+    # the same scales one element into a buffer: 2-byte aligned only
+    sc_pad = np.concatenate([np.zeros(1, sc.dtype), sc.reshape(-1)])
+    sc_dev = dev_array(gpu, sc_pad)
+    y = Out(dev, st, M * N * 2)
+    kp = (K + 63) // 64 * 64
+    ws = Out(dev, st, N * kp * 4)
+    ops.w4a16GemmGroupedPrefill(dev_array(gpu, x), wt, sc_dev.address + 2, y, M, N, K, ws,
+                                N * kp * 4, group_size=G)
+    st.sync()
+    y_two = y.read(np.uint16, (M, N))
+    ref, _ = oracle.w4a16_grouped(wq, sc, 8, G, x)
+    assert rel_err(syn.bf16_to_float(y_gs), ref) <= TOL_BF16
+    assert rel_err(syn.bf16_to_float(y_two), ref) <= TOL_BF16
+    assert not np.array_equal(y_gs, y_two)
 
 
 def test_prefill_slab_width_does_not_change_results(gpu):
