@@ -73,14 +73,17 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-llama", action="store_true", help="skip the Llama-shaped W4A16 stack")
-    p.add_argument("--only", choices=["all", "w8a8", "large", "w4a16", "llama", "f32", "side"],
+    p.add_argument("--only", choices=["all", "w8a8", "large", "w4a16", "llama", "f32", "side",
+                                      "prefill"],
                    default="all",
                    help="run one workload alone (for profiling); prints its own JSON line")
     p.add_argument("--as-world", type=int, default=1,
                    help="with --only large: run rank 0's shard of a W-GPU job on this GPU")
     p.add_argument("--profile", action="store_true",
-                   help="with --only w8a8|w4a16: warmup + steps plain launches and nothing "
-                        "else (no clock warm-up, no graphs), for ncu captures")
+                   help="with --only w8a8|w4a16|prefill: warmup + steps plain launches and "
+                        "nothing else (no clock warm-up, no graphs), for ncu captures")
+    p.add_argument("--rows", type=int, default=4096,
+                   help="with --only prefill: activation rows of the prefill GEMM")
     return p.parse_args()
 
 
@@ -871,6 +874,48 @@ def llama_stack(ops, peaks, layers=32, prefill_steps=3, decode_steps=50):
     return res
 
 
+def prefill_one(ops, M, steps, warmup, profile, peaks):
+    """One exact W4A16 prefill call of the Llama-2-7B gate+up projection (K=4096,
+    N=22016, group 128, fragment-ordered weights) at M rows: the slab expansion and the
+    group-scaled multiply.  With `profile`, warmup + steps plain calls and nothing else
+    (the form an ncu capture uses)."""
+    import torch
+    K, N, G = 4096, 22016, 128
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+    q = torch.randint(-2**31, 2**31 - 1, (K, N // 8), dtype=torch.int32, device="cuda",
+                      generator=gen)
+    wt = torch.empty(ops.w4FragBytes(K, N), dtype=torch.uint8, device="cuda")
+    ops.prepackW4Frag(q, wt, K, N)
+    sc = (torch.rand((K // G, N), device="cuda", generator=gen) * 0.015 + 0.005).to(torch.bfloat16)
+    x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    ws_bytes = ops.w4PrefillWorkspaceBytes(K, N)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+
+    def call():
+        ops.w4a16GemmGroupedPrefillFrag(x, wt, sc, y, M, N, K, ws, ws_bytes, zero_point=8,
+                                        group_size=G)
+    if profile:
+        for _ in range(warmup + steps):
+            call()
+        torch.cuda.synchronize()
+        return {"launches": warmup + steps, "shape": [M, N, K]}
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / steps
+    flops = 2.0 * M * N * K
+    return {"shape": [M, N, K], "ms_per_call": t * 1e3, "TFLOPs": flops / t / 1e12,
+            "frac_of_bf16_burst_peak": flops / t / 1e12 / peaks["bf16_tflops"]}
+
+
 def gather_output(st, lo, rank, world, reps=5):
     """The whole headline output on every rank, timed apart from the headline: the NCCL
     all-gather of the bf16 output blocks and the [world][M][NL] -> [M][N] unshard kernel
@@ -1204,6 +1249,13 @@ def main():
         r = llama_stack(ops, peaks)
         if rank == 0:
             print(json.dumps({"only": "llama", "llama2_7b_w4a16_stack": r}), flush=True)
+        finish()
+        return 0
+    if args.only == "prefill":
+        log("w4a16 exact prefill, gate+up projection (only)")
+        r = prefill_one(ops, args.rows, K, W, args.profile, peaks)
+        if rank == 0:
+            print(json.dumps({"only": "prefill", **r}), flush=True)
         finish()
         return 0
     if args.only == "large":
