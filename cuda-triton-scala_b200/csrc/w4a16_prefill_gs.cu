@@ -48,8 +48,7 @@ namespace w4gs {
 constexpr int BK = 128;                        // bytes of K per stage: 64 bf16
 constexpr int KB_ELEMS = 64;
 constexpr int UMMA_K = 32;                     // bytes of K per MMA: 16 bf16
-constexpr int STAGES = 4;                     // 4 measured faster than 5 (4.1 vs 4.3-4.7 ms at
-                                               // 16384 x 22016 x 4096)
+constexpr int STAGES = 4;                      // 4 measured faster than 5 at 16384 x 22016 x 4096
 constexpr int A_BYTES = 128 * BK;              // 16 KB: this CTA's 128 rows
 constexpr int B_BYTES = 128 * BK;              // 16 KB: this CTA's 128 columns
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -334,7 +333,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
           if (c == 1) {  // the accumulator is free for the group after next
             ptx::tc_fence_before();
-            if (ok) ptx::mbar_arrive_cluster(a ? te1 : te0);
+            if (ok) ptx::mbar_arrive_remote(a ? te1 : te0);
           }
 #pragma unroll
           for (int j = 0; j < 64; j += 4) {
