@@ -373,7 +373,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-    if (elected) ptx::bulk_wait_group_all();
+    if (elected) ptx::bulk_wait_group_read<0>();  // the writes complete with the grid
   }
 
   ptx::tc_fence_before();

@@ -640,7 +640,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::tc_fence_before();
       ptx::mbar_arrive(tempty_bar(a));
     }
-    if (elected) ptx::bulk_wait_group_all();
+    // The CTA may exit once its last stores have read their staging buffers; the writes
+    // themselves complete with the grid.  The peer windows of the fused all-gather are
+    // waited for in full.
+    if (elected) {
+      if (p.npeer) ptx::bulk_wait_group_all();
+      else ptx::bulk_wait_group_read<0>();
+    }
   }
 
   ptx::tc_fence_before();
@@ -938,7 +944,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (elected) p.cnt[tt] = 0;
       ptx::named_bar_sync(1, 128);  // the flag is rewritten only after everyone read it
     }
-    if (elected) ptx::bulk_wait_group_all();
+    // The CTA may exit once its last stores have read their staging buffers; the writes
+    // themselves complete with the grid.  The peer windows of the fused all-gather are
+    // waited for in full.
+    if (elected) {
+      if (p.npeer) ptx::bulk_wait_group_all();
+      else ptx::bulk_wait_group_read<0>();
+    }
   }
 
   ptx::tc_fence_before();
