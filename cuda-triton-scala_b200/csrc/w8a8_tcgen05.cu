@@ -362,10 +362,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
                                               bool elected, int& chunk_seq, bool ok,
                                               const int32_t* parts = nullptr, int nparts = 0,
                                               size_t part_stride = 0, bool add_tmem = false,
-                                              int ncols = 256) {
+                                              int ncols = 256, const float* sb_smem = nullptr,
+                                              const float* sa_pre = nullptr) {
   const int row = row0 + q * 32 + lane;
   const int rl = q * 32 + lane;  // row within the staging block
-  const float sa = (!p.fp_acc && !p.no_out && row < p.M) ? __ldg(p.sA + row) : 0.f;
+  // sb_smem / sa_pre: the item's column scales (from column n0 on) and this row's scale,
+  // loaded by the caller before the accumulator was ready, off the epilogue's path
+  const float sa = sa_pre ? *sa_pre
+                          : (!p.fp_acc && !p.no_out && row < p.M) ? __ldg(p.sA + row) : 0.f;
   const bool skip = p.skip_flag != nullptr && *reinterpret_cast<const volatile int*>(p.skip_flag) != 0;
   if (!p.tma_store) {
 #pragma unroll 1
@@ -410,6 +414,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       if (p.fp_acc) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) sb[j] = 1.f;
+      } else if (sb_smem) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(sb_smem + ch * cwe + sub * 32 + j);
+          sb[j] = v.x; sb[j + 1] = v.y; sb[j + 2] = v.z; sb[j + 3] = v.w;
+        }
       } else if (nc + 32 <= p.N && ((reinterpret_cast<uintptr_t>(p.sB + nc) & 15) == 0)) {
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
@@ -677,8 +687,9 @@ constexpr int STAGES = 6;
 constexpr int A_BYTES = 128 * BK;              // 16 KB
 constexpr int B_BYTES = 128 * BK;              // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES; // 32 KB per CTA
+constexpr int SB_BYTES = 256 * 4;              // the current item's column scales (fp32)
 constexpr int SMEM_BYTES = 232448;
-static_assert(STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024 <= SMEM_BYTES,
+static_assert(STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + SB_BYTES + 1024 <= SMEM_BYTES,
               "shared memory budget");
 }  // namespace pair
 
@@ -869,6 +880,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const uint32_t te_leader1 = ptx::map_to_rank(tempty_bar(1), 0);
     volatile int* last_flag = abort_flag + 1;
     const int rl = q * 32 + lane;  // row of this CTA's half-tile
+    float* sb_smem = reinterpret_cast<float*>(gbar + BAR_BYTES);  // pair::SB_BYTES
+    const bool scaled = !p.fp_acc && !p.no_out;
     int it = 0;
     int tile, kb0, kb1, part, half;
     for (; pair_item(p, pair_id, npairs, it, tile, kb0, kb1, part, half); ++it) {
@@ -876,6 +889,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tile_coords(tile, p, mb, nb);
       const int a = it & 1;
       const uint32_t aphase = (uint32_t)((it >> 1) & 1);
+      // This item's column scales into shared memory and this row's scale into a
+      // register while the MMAs run: in the last item nothing else hides their latency.
+      const int n0i = nb * BN + (half > 0 ? BN / 2 : 0);
+      const int nci = half >= 0 ? BN / 2 : BN;
+      ptx::named_bar_sync(1, 128);  // the previous item's epilogue is done with sb_smem
+      if (scaled)
+        for (int c = rl; c < nci; c += 128) sb_smem[c] = n0i + c < p.N ? __ldg(p.sB + n0i + c) : 0.f;
+      const int row_i = mb * BM + (int)rank * 128 + rl;
+      const float sa_i = (scaled && row_i < p.M) ? __ldg(p.sA + row_i) : 0.f;
+      ptx::named_bar_sync(1, 128);
+      const float* sbp = scaled ? sb_smem : nullptr;
       bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag, p.wait_ns);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is .sync.aligned
       if (!ok && lane == 0 && !*abort_flag)
@@ -883,8 +907,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       ptx::tc_fence_after();
       if (part < 0) {
         epilogue_tile(p, &tmO, &pm, tmem_base, (uint32_t)(a * BN), q, lane,
-                      mb * BM + (int)rank * 128, nb * BN + (half > 0 ? BN / 2 : 0), stg_base,
-                      elected, chunk_seq, ok, nullptr, 0, 0, false, half >= 0 ? BN / 2 : BN);
+                      mb * BM + (int)rank * 128, n0i, stg_base, elected, chunk_seq, ok, nullptr,
+                      0, 0, false, nci, sbp, &sa_i);
         ptx::tc_fence_before();
         ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
         continue;
@@ -938,7 +962,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const bool ready = ok && *last_flag != 0;
       epilogue_tile(p, &tmO, &pm, tmem_base, (uint32_t)(a * BN), q, lane,
                     mb * BM + (int)rank * 128, nb * BN, stg_base, elected, chunk_seq, ready,
-                    p.part + (size_t)tt * p.split_s * slot_ints, p.split_s - 1, slot_ints, true);
+                    p.part + (size_t)tt * p.split_s * slot_ints, p.split_s - 1, slot_ints, true,
+                    BN, sbp, &sa_i);
       ptx::tc_fence_before();
       ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
       if (elected) p.cnt[tt] = 0;
