@@ -45,7 +45,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch from one `ncu --set full` capture of the same
 # kernel on the same workload: the W8A8 pair kernel at 4096^3, the M = 1 decode on the
 # fragment order, and the fp32 matmul's tf32 GEMM at 4096^3.
-NCU_TRAFFIC_W8A8_4096 = 33682688 + 2535936
+NCU_TRAFFIC_W8A8_4096 = 33675008 + 2621952
 NCU_TRAFFIC_W4A16_M1 = 30306304 + 0
 NCU_TRAFFIC_F32_GEMM_4096 = 985069568 + 61620736
 

@@ -900,7 +900,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const float sa_i = (scaled && row_i < p.M) ? __ldg(p.sA + row_i) : 0.f;
       ptx::named_bar_sync(1, 128);
       const float* sbp = scaled ? sb_smem : nullptr;
-      bool ok = ptx::mbar_wait_sleep(tfull_bar(a), aphase, abort_flag, p.wait_ns);
+      // a spinning wait: the last item's epilogue starts as soon as its accumulator is done
+      bool ok = ptx::mbar_wait(tfull_bar(a), aphase, abort_flag, p.wait_ns);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is .sync.aligned
       if (!ok && lane == 0 && !*abort_flag)
         report_pair(p.err, DEVERR_TIMEOUT_EPILOGUE, abort_flag, rank);
@@ -910,7 +911,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                       mb * BM + (int)rank * 128, n0i, stg_base, elected, chunk_seq, ok, nullptr,
                       0, 0, false, nci, sbp, &sa_i);
         ptx::tc_fence_before();
-        ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
+        ptx::mbar_arrive_remote(a ? te_leader1 : te_leader0);
         continue;
       }
       // A K part of a tail tile.  Parts 0 .. split_s-2 park their partial sums (this
@@ -938,7 +939,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
         }
         ptx::tc_fence_before();
-        ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);  // TMEM is free again
+        ptx::mbar_arrive_remote(a ? te_leader1 : te_leader0);  // TMEM is free again
         __threadfence();
         ptx::named_bar_sync(1, 128);
         if (elected) atomicAdd(p.cnt + tt, 1);
@@ -965,7 +966,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                     p.part + (size_t)tt * p.split_s * slot_ints, p.split_s - 1, slot_ints, true,
                     BN, sbp, &sa_i);
       ptx::tc_fence_before();
-      ptx::mbar_arrive_cluster(a ? te_leader1 : te_leader0);
+      ptx::mbar_arrive_remote(a ? te_leader1 : te_leader0);
       if (elected) p.cnt[tt] = 0;
       ptx::named_bar_sync(1, 128);  // the flag is rewritten only after everyone read it
     }
