@@ -231,17 +231,13 @@ __device__ __forceinline__ void cluster_sync_all() {
 // Arrive on an mbarrier that may live in another CTA of the cluster, with release
 // semantics at CTA scope only: enough when the barrier orders tensor-memory accesses
 // (tcgen05.wait + tcgen05.fence::before_thread_sync before it), not generic memory.  A
-// cluster-scope release waits on the thread's outstanding memory operations; once per
-// 128-k group in the group-scaled prefill it cost a third of the kernel's time.
+// cluster-scope release (mbarrier.arrive.release.cluster) waits on the thread's
+// outstanding memory operations; once per 128-k group in the group-scaled prefill it
+// cost a third of the kernel's time.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-// Arrive on an mbarrier that may live in another CTA of the cluster.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
 
 // 2-D TMA tile load into this CTA's shared memory for a CTA-pair MMA: completion is
 // counted on `bar_cluster`, an mbarrier that may be in the peer CTA.
